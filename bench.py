@@ -1,0 +1,589 @@
+#!/usr/bin/env python
+"""Benchmark of the B200 paged-KV decode hot path.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload decode_c2|decode_c4]
+                    [--impl ours|reference]
+
+A "step" is one decode step of the configured batch through every layer:
+per layer, the KV append of this step's token (nvk_kv_append) and paged GQA
+decode attention over the whole context (nvk_paged_decode), replayed as ONE
+CUDA graph captured by DecodeGraphRunner at the batch size.
+
+Workloads (seeded synthetic inputs with the configs' shapes; no model weights):
+  decode_c2 (default, N=1 headline): 28 layers, 32 sequences, context ~
+      U[256, 2304], 16 query / 8 KV heads, head_dim 128, block 128, pool =
+      80% of free HBM, block tables drawn without replacement from a seeded
+      permutation of the pool. At N > 1 every rank runs its own such batch on
+      its own pool (sequence-sharded replicas, no collective): weak scaling.
+  decode_c4: 256 sequences, context ~ U[2048, 6144], split evenly across
+      ranks by sequence (strong scaling).
+
+Printed (rank 0, one JSON line): value = KV bytes read by decode attention
+per step, summed over ranks, / max-over-ranks step time (GB/s); tok/s; the
+dominant kernel's roofline (decode attention timed alone with CUDA events on
+its stream); the prefill-sized append GB/s; an end-to-end figure through the
+public API with pinned host inputs and a device->host read of the outputs;
+SM clocks sampled by nvidia-smi during the measurement; the CPU baseline
+(eager torch-CPU expression of the reference path on a bounded sample).
+
+--impl reference times that CPU path alone on the host cores (rank 0 only).
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from dataclasses import dataclass
+from pathlib import Path
+
+import torch
+
+ROOT = Path(__file__).resolve().parent
+KVH, HEAD_DIM, BLOCK = 8, 128, 128
+
+
+@dataclass
+class Workload:
+    name: str
+    layers: int
+    batch: int
+    heads: int
+    kv_heads: int
+    ctx_lo: int
+    ctx_hi: int
+    scaling: str  # "weak": batch per rank; "strong": batch split across ranks
+    util: float = 0.8
+    describe: str = ""
+
+
+WORKLOADS = {
+    "decode_c2": Workload("decode_c2", 28, 32, 16, 8, 256, 2304, "weak",
+                          describe="config[1]: Qwen3-0.6B decode step, 32 seqs, ctx~U[256,2304], CUDA graph bs 32"),
+    "decode_c4": Workload("decode_c4", 28, 256, 16, 8, 2048, 6144, "strong",
+                          describe="config[3]: Qwen3-0.6B decode step, 256 seqs, ctx~U[2048,6144], sequence-sharded"),
+}
+
+
+# --------------------------------------------------------------- helpers ----
+def peaks() -> tuple[float, str]:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            return float(json.loads(p.read_text())["hbm_gbs"]), "measured"
+        except Exception:
+            pass
+    return 6650.0, "fallback"
+
+
+def profiled_traffic(workload: str) -> float | None:
+    """Per-launch DRAM bytes of the decode kernel from a committed ncu summary
+    (a line 'traffic_bytes_per_launch: N' in profiles/paged_decode_<workload>.txt)."""
+    p = ROOT / "profiles" / f"paged_decode_{workload}.txt"
+    if not p.exists():
+        return None
+    for line in p.read_text().splitlines():
+        if line.startswith("traffic_bytes_per_launch:"):
+            try:
+                return float(line.split(":", 1)[1].strip())
+            except ValueError:
+                return None
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi clock/throttle sampling in the background (every 200 ms)."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = None
+
+    def __enter__(self):
+        try:
+            fd, self.path = tempfile.mkstemp(prefix="clocks", suffix=".csv")
+            os.close(fd)
+            self.fh = open(self.path, "w")
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=self.fh, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+            self.fh.close()
+
+    def summary(self) -> dict:
+        rows = []
+        if self.path and os.path.exists(self.path):
+            for line in open(self.path):
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) >= 9:
+                    rows.append(parts)
+            os.unlink(self.path)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
+        def num(x):
+            try:
+                return float(x)
+            except ValueError:
+                return None
+        sm = [num(r[1]) for r in rows if num(r[1]) is not None]
+        smax = [num(r[2]) for r in rows if num(r[2]) is not None]
+        power = [num(r[3]) for r in rows if num(r[3]) is not None]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for r in rows for n, v in zip(names, r[5:9]) if v.lower() == "active"})
+        loaded = [s for s, p in zip(sm, power) if p is not None and p > 200] or sm
+        return {"sm_mhz": statistics.median(loaded) if loaded else None, "sm_max_mhz": max(smax) if smax else None,
+                "reasons": reasons, "samples": len(rows), "power_w_max": max(power) if power else None}
+
+
+def dist_setup(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1 and args.impl == "ours":
+        import datetime
+
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    elif args.impl == "ours":
+        torch.cuda.set_device(local)
+    return world, rank, local
+
+
+def barrier_sync(world):
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+    torch.cuda.synchronize()
+
+
+def max_over_ranks(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    import torch.distributed as dist
+
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def sum_over_ranks(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    import torch.distributed as dist
+
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.SUM)
+    return float(t.item())
+
+
+# ----------------------------------------------------------------- setup ----
+def rank_contexts(wl: Workload, world: int, rank: int) -> list[int]:
+    """Context lengths (before this step's token) of this rank's sequences."""
+    from nano_vllm_ascend_b200.sharding import sequence_shard
+
+    if wl.scaling == "strong":
+        g = torch.Generator().manual_seed(0)
+        ctx = torch.randint(wl.ctx_lo, wl.ctx_hi + 1, (wl.batch,), generator=g).tolist()
+        return [ctx[i] for i in sequence_shard(wl.batch, world, rank)]
+    g = torch.Generator().manual_seed(1000 + rank)
+    return torch.randint(wl.ctx_lo, wl.ctx_hi + 1, (wl.batch,), generator=g).tolist()
+
+
+class AttentionOnlyDecoder:
+    """Stands in for Qwen3ForCausalLM inside the decode graph: per layer, the
+    reference's Qwen3Attention hot-path order (qwen3.py:91-117) -- append this
+    step's K/V, then paged attention -- on static per-layer q/k/v buffers."""
+
+    def __init__(self, layers: int, batch: int, heads: int, kv_heads: int, device, seed: int = 7):
+        from nano_vllm_ascend_b200 import PagedAttention
+
+        g = torch.Generator(device=device).manual_seed(seed)
+        self.q = torch.randn(layers, batch, heads, HEAD_DIM, generator=g, device=device).to(torch.bfloat16)
+        self.k = torch.randn(layers, batch, kv_heads, HEAD_DIM, generator=g, device=device).to(torch.bfloat16)
+        self.v = torch.randn(layers, batch, kv_heads, HEAD_DIM, generator=g, device=device).to(torch.bfloat16)
+        self.attn = PagedAttention(heads, kv_heads, HEAD_DIM)
+        self.layers = layers
+
+    def __call__(self, input_ids_flat, position_ids_flat, kv_cache, attn_metadata, is_prefill=False):
+        outs = []
+        for layer in range(self.layers):
+            kv_cache.write(layer, self.k[layer], self.v[layer], attn_metadata.slot_mapping)
+            kc, vc = kv_cache.get_physical_cache(layer)
+            outs.append(self.attn(self.q[layer], kc, vc, attn_metadata.block_tables, attn_metadata.context_lens))
+
+        class Out:
+            logits = torch.stack(outs)
+
+        return Out()
+
+
+def build(wl: Workload, world: int, rank: int, device, pool_blocks: int = 0):
+    from nano_vllm_ascend_b200 import BlockManager, PagedKVCache
+    from nano_vllm_ascend_b200.pool import num_blocks_from_memory
+
+    ctx = rank_contexts(wl, world, rank)
+    b = len(ctx)
+    num_blocks = num_blocks_from_memory(wl.util, wl.layers, BLOCK, wl.kv_heads, HEAD_DIM, torch.bfloat16, device)
+    if pool_blocks > 0:
+        num_blocks = min(num_blocks, pool_blocks)
+    bm = BlockManager(num_blocks, BLOCK, device)
+    g = torch.Generator().manual_seed(42 + rank)
+    bm.free_block_ids = torch.randperm(num_blocks, generator=g).tolist()
+    slots = list(range(b))
+    bm.prepare_prefill_metadata(slots, ctx, [0] * b, [[] for _ in slots])
+    md = bm.prepare_decode_metadata(slots, ctx, q_len=1)
+    kv = PagedKVCache(wl.layers, num_blocks, BLOCK, wl.kv_heads, HEAD_DIM, torch.bfloat16, device)
+    used = torch.unique(torch.cat([torch.tensor(bm.block_tables[s], dtype=torch.int64) for s in slots])).to(device)
+    gen = torch.Generator(device=device).manual_seed(5 + rank)
+    for layer in range(wl.layers):
+        shape = (used.numel(), BLOCK, wl.kv_heads, HEAD_DIM)
+        kv.key_cache[layer].index_copy_(0, used, torch.randn(shape, generator=gen, device=device, dtype=torch.bfloat16))
+        kv.value_cache[layer].index_copy_(0, used,
+                                          torch.randn(shape, generator=gen, device=device, dtype=torch.bfloat16))
+    model = AttentionOnlyDecoder(wl.layers, b, wl.heads, wl.kv_heads, device, seed=11 + rank)
+    return ctx, bm, md, kv, model, num_blocks
+
+
+def kv_bytes_per_layer(ctx_after: list[int], kv_heads: int) -> int:
+    return sum(ctx_after) * kv_heads * HEAD_DIM * 2 * 2
+
+
+# --------------------------------------------------------------- measure ----
+def time_decode_kernel(wl, md, kv, model, device, launches: int, seconds: float = 0.8) -> tuple[float, int]:
+    """Average duration (s) of one nvk_paged_decode launch, cycling layers so
+    that every launch reads a different 100+ MB slice of HBM."""
+    from nano_vllm_ascend_b200 import ops
+
+    b = model.q.shape[1]
+    tables = md.block_tables.to(device)
+    ctx = md.context_lens.to(device=device, dtype=torch.int32)
+    total = int(((md.context_lens.long() + BLOCK - 1) // BLOCK).sum())
+    bps = ops.choose_blocks_per_split(wl.kv_heads, tables.shape[1], total, b,
+                                      torch.cuda.get_device_properties(device).multi_processor_count)
+    splits = math.ceil(tables.shape[1] / bps)
+    ws = torch.zeros(ops.decode_workspace_bytes(b, wl.heads, wl.kv_heads, HEAD_DIM, splits), dtype=torch.uint8,
+                     device=device)
+    out = torch.empty_like(model.q[0])
+    scale = HEAD_DIM ** -0.5
+    stream = torch.cuda.current_stream(device)
+
+    def launch(i):
+        layer = i % wl.layers
+        kc, vc = kv.get_physical_cache(layer)
+        ops.paged_decode(out, model.q[layer], kc, vc, tables, ctx, scale, ws, bps, splits)
+
+    for i in range(5):
+        launch(i)
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    # first pass sizes the loop so that it lasts about `seconds` (clock sampling)
+    for rep in range(2):
+        start.record(stream)
+        for i in range(launches):
+            launch(i)
+        end.record(stream)
+        end.synchronize()
+        per = start.elapsed_time(end) / 1e3 / launches
+        if rep == 0:
+            launches = max(launches, int(seconds / max(per, 1e-7)))
+    return per, bps
+
+
+def time_append(kv, bm, device, rows: int, launches: int) -> float:
+    """Average duration (s) of one prefill-sized append (rows tokens, K+V) into free blocks."""
+    from nano_vllm_ascend_b200 import ops
+
+    free = bm.free_block_ids[: (rows + BLOCK - 1) // BLOCK]
+    slots = torch.cat([torch.arange(f * BLOCK, (f + 1) * BLOCK) for f in free])[:rows].to(device)
+    g = torch.Generator(device=device).manual_seed(3)
+    k = torch.randn(rows, kv.num_kv_heads, HEAD_DIM, generator=g, device=device).to(torch.bfloat16)
+    v = torch.randn(rows, kv.num_kv_heads, HEAD_DIM, generator=g, device=device).to(torch.bfloat16)
+    stream = torch.cuda.current_stream(device)
+    for i in range(3):
+        ops.kv_append(kv.key_cache[i % kv.num_layers], kv.value_cache[i % kv.num_layers], k, v, slots)
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    for i in range(launches):
+        layer = i % kv.num_layers
+        ops.kv_append(kv.key_cache[layer], kv.value_cache[layer], k, v, slots)
+    end.record(stream)
+    end.synchronize()
+    return start.elapsed_time(end) / 1e3 / launches
+
+
+class CpuBaseline:
+    """Eager torch-CPU reference path (oracle/cpu_baseline.py) on one layer's
+    worth of this workload: the sequences' blocks in a host pool, this step's
+    append (index_copy_) and decode attention (gather + fp32 softmax). Every
+    layer of a step is identical work, so a step costs layers x one layer."""
+
+    def __init__(self, wl: Workload, ctx: list[int], threads: int):
+        torch.set_num_threads(threads)
+        self.wl, self.ctx, self.threads = wl, ctx, threads
+        b = len(ctx)
+        g = torch.Generator().manual_seed(0)
+        nblk = [(n + 1 + BLOCK - 1) // BLOCK for n in ctx]
+        nb = sum(nblk)
+        self.kc = torch.randn(nb, BLOCK, wl.kv_heads, HEAD_DIM, generator=g).to(torch.bfloat16)
+        self.vc = torch.randn(nb, BLOCK, wl.kv_heads, HEAD_DIM, generator=g).to(torch.bfloat16)
+        perm = torch.randperm(nb, generator=g).to(torch.int32)
+        self.tables = torch.zeros(b, max(nblk), dtype=torch.int32)
+        self.slots = torch.zeros(b, dtype=torch.int64)
+        used = 0
+        for i, m in enumerate(nblk):
+            self.tables[i, :m] = perm[used : used + m]
+            used += m
+            self.slots[i] = int(self.tables[i, ctx[i] // BLOCK]) * BLOCK + ctx[i] % BLOCK
+        self.q = torch.randn(b, wl.heads, HEAD_DIM, generator=g).to(torch.bfloat16)
+        self.k = torch.randn(b, wl.kv_heads, HEAD_DIM, generator=g).to(torch.bfloat16)
+        self.v = torch.randn(b, wl.kv_heads, HEAD_DIM, generator=g).to(torch.bfloat16)
+        self.ctx_after = torch.tensor([n + 1 for n in ctx], dtype=torch.int32)
+        self.bytes_layer = kv_bytes_per_layer([n + 1 for n in ctx], wl.kv_heads)
+
+    def layer(self) -> None:
+        from oracle import cpu_baseline
+
+        cpu_baseline.append(self.kc, self.vc, self.k, self.v, self.slots)
+        cpu_baseline.decode(self.q, self.kc, self.vc, self.tables, self.ctx_after, HEAD_DIM ** -0.5)
+
+    def time_layers(self, seconds: float, min_layers: int = 1) -> tuple[float, int]:
+        """Runs layer() until ``seconds`` elapsed (at least min_layers); returns (s per layer, layers)."""
+        n = 0
+        t0 = time.perf_counter()
+        while True:
+            self.layer()
+            n += 1
+            el = time.perf_counter() - t0
+            if n >= min_layers and el >= seconds:
+                return el / n, n
+
+
+def cpu_baseline_decode(wl: Workload, ctx: list[int], seconds: float, threads: int) -> dict:
+    base = CpuBaseline(wl, ctx, threads)
+    base.layer()  # warm-up
+    per_layer, n = base.time_layers(seconds)
+    gbs = base.bytes_layer / per_layer / 1e9
+    return {"value": gbs, "unit": "GB/s", "cores": threads, "kind": "port",
+            "sample": f"{n} layer-steps (append + decode attention) of {len(ctx)} seqs on one layer's pool, "
+                      f"{n * per_layer:.1f}s", "ms_per_layer": per_layer * 1e3,
+            "tok_per_s": len(ctx) / (per_layer * wl.layers)}
+
+
+# ------------------------------------------------------------------ arms ----
+def run_reference(args, world, rank):
+    if rank != 0:
+        return 0
+    wl = WORKLOADS[args.workload]
+    threads = os.cpu_count() or 1
+    ctx = rank_contexts(wl, 1, 0)
+    base = CpuBaseline(wl, ctx, threads)
+    # a step = one layer of the workload (append + decode attention); the
+    # full step costs layers x that, reported in ms_per_step
+    for _ in range(args.warmup):
+        base.layer()
+    per_layer, n = base.time_layers(0.0, min_layers=args.steps)
+    gbs = base.bytes_layer / per_layer / 1e9
+    line = {
+        "impl": "reference", "metric": "paged decode-attn KV GB/s", "value": gbs, "unit": "GB/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": per_layer * wl.layers * 1e3, "higher_is_better": True, "scaling": wl.scaling,
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": wl.describe, "layers": wl.layers, "batch": len(ctx), "seq_len": [wl.ctx_lo, wl.ctx_hi],
+                   "parallelism": "host CPU"},
+        "tok_per_s": len(ctx) / (per_layer * wl.layers),
+        "cpu_baseline": {"value": gbs, "unit": "GB/s", "cores": threads, "kind": "port",
+                         "sample": f"{n} layer-steps (append + decode attention, one layer of the workload each)"},
+        "e2e": {"value": gbs, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def run_ours(args, world, rank, local):
+    from nano_vllm_ascend_b200 import DecodeGraphRunner
+
+    wl = WORKLOADS[args.workload]
+    device = torch.device("cuda", local)
+    ctx, bm, md, kv, model, num_blocks = build(wl, world, rank, device, args.pool_blocks)
+    b = len(ctx)
+    ctx_after = [n + 1 for n in ctx]
+    bytes_layer = kv_bytes_per_layer(ctx_after, wl.kv_heads)
+    bytes_step = bytes_layer * wl.layers
+
+    runner = DecodeGraphRunner(model, kv, batch_sizes=[b], max_model_len=wl.ctx_hi + 64, block_size=BLOCK,
+                               device=device)
+    input_ids = torch.zeros(b, dtype=torch.long, device=device)
+    positions = torch.tensor(ctx, dtype=torch.long, device=device)
+    if runner.forward(input_ids, positions, md) is None:
+        raise RuntimeError("decode graph capture failed")
+    entry = runner.entries[b]
+    torch.cuda.synchronize()
+
+    with ClockSampler(local) as clocks:
+        # dominant kernel alone (roofline)
+        t_dec, bps = time_decode_kernel(wl, md, kv, model, device, launches=max(56, 4 * wl.layers),
+                                        seconds=0.0 if args.quick else 0.8)
+        t_app = time_append(kv, bm, device, rows=8192, launches=8 if args.quick else 56)
+        # the step: W warm-up replays, then exactly K timed replays
+        for _ in range(args.warmup):
+            entry.graph.replay()
+        barrier_sync(world)
+        stream = torch.cuda.current_stream(device)
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record(stream)
+        for _ in range(args.steps):
+            entry.graph.replay()
+        end.record(stream)
+        barrier_sync(world)
+        t_step = start.elapsed_time(end) / 1e3 / args.steps
+
+        # end to end through the public API: pinned host inputs -> device,
+        # runner.forward (metadata refresh + replay), outputs -> host
+        h_q = model.q.cpu().pin_memory()
+        h_k = model.k.cpu().pin_memory()
+        h_v = model.v.cpu().pin_memory()
+        h_out = torch.empty(entry.logits.shape, dtype=entry.logits.dtype).pin_memory()
+        h_tables = md.block_tables.cpu().pin_memory()
+        h_slots = md.slot_mapping.cpu().pin_memory()
+        h_ctx = md.context_lens.pin_memory()
+        h_pos = positions.cpu().pin_memory()
+        h_ids = input_ids.cpu().pin_memory()
+
+        def e2e_step():
+            model.q.copy_(h_q, non_blocking=True)
+            model.k.copy_(h_k, non_blocking=True)
+            model.v.copy_(h_v, non_blocking=True)
+            step_md = type(md)(block_tables=h_tables.to(device, non_blocking=True), context_lens=h_ctx,
+                               slot_mapping=h_slots.to(device, non_blocking=True))
+            logits = runner.forward(h_ids.to(device, non_blocking=True), h_pos.to(device, non_blocking=True),
+                                    step_md)
+            h_out.copy_(logits, non_blocking=True)
+
+        for _ in range(args.warmup):
+            e2e_step()
+        barrier_sync(world)
+        e_start, e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e_start.record(stream)
+        for _ in range(args.steps):
+            e2e_step()
+        e_end.record(stream)
+        barrier_sync(world)
+        t_e2e = e_start.elapsed_time(e_end) / 1e3 / args.steps
+    clk = clocks.summary()
+
+    h2d = sum(t.numel() * t.element_size() for t in (h_q, h_k, h_v, h_tables, h_slots, h_ctx, h_pos, h_ids))
+    d2h = h_out.numel() * h_out.element_size()
+
+    t_step_max = max_over_ranks(t_step, world)
+    t_e2e_max = max_over_ranks(t_e2e, world)
+    bytes_all = sum_over_ranks(float(bytes_step), world)
+    seqs_all = sum_over_ranks(float(b), world)
+    peak, peak_kind = peaks()
+    dec_bytes_launch = bytes_layer + b * wl.heads * HEAD_DIM * 2 * 2 + md.block_tables.numel() * 4 + b * 4
+    achieved = dec_bytes_launch / t_dec / 1e9
+    app_bytes = 8192 * wl.kv_heads * HEAD_DIM * 2 * 2 * 2 + 8192 * 8
+    traffic = profiled_traffic(wl.name)
+
+    if rank == 0:
+        cpu = None
+        if world == 1 and not args.no_cpu_baseline:
+            cpu = cpu_baseline_decode(wl, ctx, seconds=args.cpu_seconds, threads=os.cpu_count() or 1)
+        line = {
+            "metric": "paged decode-attn KV GB/s",
+            "value": bytes_all / t_step_max / 1e9,
+            "unit": "GB/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": t_step_max * 1e3,
+            "higher_is_better": True,
+            "scaling": wl.scaling,
+            "vs_baseline": None,
+            "dtype": "bf16",
+            "data": "synthetic: seeded N(0,1) q/K/V, seeded context lengths and block tables (no weights)",
+            "config": {
+                "workload": wl.describe,
+                "layers": wl.layers,
+                "batch_per_gpu": b,
+                "global_batch": int(seqs_all),
+                "seq_len": [wl.ctx_lo, wl.ctx_hi],
+                "heads": [wl.heads, wl.kv_heads, HEAD_DIM],
+                "block_size": BLOCK,
+                "pool_blocks": num_blocks,
+                "parallelism": f"sequence-sharded x{world}, independent pools, no collective",
+                "cache": "inputs larger than L2: every step reads %.2f GB of KV" % (bytes_step / 1e9),
+                "blocks_per_split": bps,
+            },
+            "tok_per_s": seqs_all / t_step_max,
+            "hbm_frac_of_step": (bytes_all / t_step_max / 1e9) / (peak * world),
+            "append": {"gbs": app_bytes / t_app / 1e9, "rows": 8192, "us": t_app * 1e6,
+                       "frac": app_bytes / t_app / 1e9 / peak},
+            "roofline": {"kernel": "paged_decode_kernel", "bound": "hbm", "achieved": achieved, "peak": peak,
+                         "peak_kind": peak_kind, "unit": "GB/s", "frac": achieved / peak,
+                         "frac_of_nominal_8tbs": achieved / 8000.0, "traffic": traffic,
+                         "algorithmic_bytes_per_launch": dec_bytes_launch, "us_per_launch": t_dec * 1e6},
+            "e2e": {"value": bytes_all / t_e2e_max / 1e9, "unit": "GB/s", "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h, "ms_per_step": t_e2e_max * 1e3},
+            "clocks": clk,
+            "gpu_launches": args.steps * wl.layers * 2,
+            "cpu_baseline": cpu,
+        }
+        print(json.dumps(line), flush=True)
+    runner.release()
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="decode_c2")
+    ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--pool-blocks", type=int, default=0,
+                    help="cap the KV pool at this many blocks (small-footprint profiling runs)")
+    ap.add_argument("--quick", action="store_true", help="short roofline loops (profiling runs)")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        ap.error("--warmup must be >= 3")
+    sys.path.insert(0, str(ROOT))
+    world, rank, local = dist_setup(args)
+    if args.impl == "reference":
+        return run_reference(args, world, rank)
+    return run_ours(args, world, rank, local)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,149 @@
+/*
+ * nvk_paged_kv.h -- C ABI of the B200 paged-KV-cache hot path.
+ *
+ * Plain pointers, sizes and a CUDA stream; no framework types. Every entry
+ * point validates its arguments on the host, returns NVK_OK (0) or a negative
+ * NVK_ERR_* code, and only enqueues work on `stream` (no host synchronisation,
+ * no allocation), so each call can be captured into a CUDA graph.
+ *
+ * Memory layout shared by all kernels (the reference pool layout):
+ *   key_cache / value_cache of ONE layer: bf16 [num_blocks, block_size,
+ *   num_kv_heads, head_dim], contiguous. Token slot s = block_id * block_size
+ *   + offset addresses row s of the flattened [num_blocks * block_size,
+ *   num_kv_heads, head_dim] view.
+ *
+ * Reference interfaces replaced (paths inside Pla-Yer/nano_vllm_ascend):
+ *   nvk_kv_append      <- PagedKVCache.write, src/nanovllm_ascend/npu/paged_kv_cache.py:44-69
+ *                         (two Tensor.index_copy_ calls at :68-69)
+ *   nvk_paged_decode   <- torch_npu._npu_paged_attention, called from
+ *                         src/nanovllm_ascend/layers/npu_paged_attention.py:58,89 and
+ *                         src/nanovllm_ascend/npu/acl_graph.py:232
+ *   nvk_paged_decode_workspace_size
+ *                      <- torch_npu._npu_paged_attention_get_workspace,
+ *                         src/nanovllm_ascend/layers/npu_paged_attention.py:42-52
+ *   nvk_paged_prefill  <- torch_npu.npu_fused_infer_attention_score, paged mode
+ *                         (block_table + absolute actual_seq_lengths_kv, sparse_mode=3),
+ *                         src/nanovllm_ascend/layers/npu_prefill_attention.py:82-96
+ *   nvk_dense_prefill  <- the same op, dense mode (contiguous k/v, cumulative
+ *                         actual_seq_lengths_kv), npu_prefill_attention.py:97-112
+ */
+#ifndef NVK_PAGED_KV_H_
+#define NVK_PAGED_KV_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define NVK_API __attribute__((visibility("default")))
+#else
+#define NVK_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Same object as cudaStream_t / CUstream; NULL is the legacy default stream. */
+typedef struct CUstream_st* nvk_stream_t;
+
+enum {
+  NVK_OK = 0,
+  NVK_ERR_INVALID_ARGUMENT = -1, /* shape, stride, alignment or null-pointer error */
+  NVK_ERR_UNSUPPORTED = -2,      /* valid, but outside what the kernels implement   */
+  NVK_ERR_WORKSPACE = -3,        /* workspace missing or too small                  */
+  NVK_ERR_CUDA = -4              /* a CUDA runtime/driver call failed               */
+};
+
+/* Message for the most recent non-zero return on the calling thread. */
+NVK_API const char* nvk_last_error(void);
+
+/* ABI version, bumped on any signature change. */
+NVK_API int nvk_abi_version(void);
+
+/*
+ * KV append: key_cache[slot_mapping[t]] = key[t]; value_cache[slot_mapping[t]]
+ * = value[t] for t < num_tokens, each row num_kv_heads * head_dim bf16 values.
+ *
+ * key/value: bf16 rows [num_tokens, num_kv_heads, head_dim]; heads and dims are
+ *   contiguous, consecutive tokens are key_token_stride / value_token_stride
+ *   ELEMENTS apart (lets the caller pass a slice of a fused QKV projection).
+ * slot_mapping: int64 [num_tokens], device memory.
+ * num_slots: num_blocks * block_size (rows in the flattened pool).
+ * error_word: optional device int; a slot outside [0, num_slots) is skipped and
+ *   sets bit 4 there (index_copy_ would raise; a device kernel must not write
+ *   out of bounds). May be NULL.
+ * Bit-exact: rows are moved as raw 16-byte words.
+ */
+NVK_API int nvk_kv_append(const void* key, const void* value, int64_t key_token_stride, int64_t value_token_stride,
+                  void* key_cache, void* value_cache, const int64_t* slot_mapping, int64_t num_tokens,
+                  int64_t num_slots, int num_kv_heads, int head_dim, int* error_word, nvk_stream_t stream);
+
+/*
+ * Bytes of split-K workspace nvk_paged_decode needs for `batch` sequences,
+ * `num_kv_heads` KV heads, `num_heads` query heads and at most `max_splits`
+ * context splits per sequence. The workspace must be zero-filled once before
+ * its first use; the kernel returns its counters to zero after every call.
+ * Calls that share one workspace must be ordered on one stream.
+ */
+NVK_API int nvk_paged_decode_workspace_size(int batch, int num_heads, int num_kv_heads, int head_dim, int max_splits,
+                                    size_t* bytes);
+
+/*
+ * Paged GQA decode attention, one query token per sequence:
+ *   out[b, h, :] = softmax(scale * q[b, h, :] . K_b[:, g(h), :]^T) V_b[:, g(h), :]
+ * over the first context_lens[b] tokens of sequence b, whose token i lives in
+ * block block_tables[b * block_table_stride + i / block_size] at offset
+ * i % block_size; g(h) = h / (num_heads / num_kv_heads).
+ *
+ * out, query: bf16 [batch, num_heads, head_dim], contiguous.
+ * block_tables: int32, row b at block_tables + b * block_table_stride, the
+ *   first max_blocks_per_seq entries meaningful (zero padding is fine: only
+ *   entries below ceil(context_lens[b] / block_size) are read).
+ * context_lens: int32 [batch] in DEVICE memory (includes the token appended
+ *   this step, as in the reference).
+ * blocks_per_split: KV blocks one CTA walks; splits = ceil(blocks / this).
+ * workspace: see nvk_paged_decode_workspace_size; max_splits must be at least
+ *   ceil(max_blocks_per_seq / blocks_per_split).
+ * Supported: head_dim 128; num_heads / num_kv_heads in {1, 2, 4, 8};
+ *   block_size a power of two in [16, 256].
+ */
+NVK_API int nvk_paged_decode(void* out, const void* query, const void* key_cache, const void* value_cache, int num_blocks,
+                     int block_size, const int32_t* block_tables, int block_table_stride, int max_blocks_per_seq,
+                     const int32_t* context_lens, int batch, int num_heads, int num_kv_heads, int head_dim,
+                     float scale, int blocks_per_split, int max_splits, void* workspace, size_t workspace_bytes,
+                     nvk_stream_t stream);
+
+/*
+ * Paged causal prefill attention (prefix-cache aware). Sequence b owns query
+ * rows [cu_seqlens_q[b], cu_seqlens_q[b+1]) of `query` and attends over the
+ * first kv_lens[b] tokens of its paged KV (cached prefix + the rows appended
+ * this step), bottom-right aligned: query i of a sequence with q_len Lq and
+ * kv_len Lk sees key j iff j <= Lk - Lq + i.
+ *
+ * out, query: bf16 [total_q, num_heads, head_dim], contiguous.
+ * cu_seqlens_q: int32 [batch + 1], kv_lens: int32 [batch], device memory.
+ * max_q_len: upper bound of any q_len (sizes the grid).
+ * Supported: head_dim 128, block_size 128, num_heads % num_kv_heads == 0.
+ */
+NVK_API int nvk_paged_prefill(void* out, const void* query, const void* key_cache, const void* value_cache, int num_blocks,
+                      int block_size, const int32_t* block_tables, int block_table_stride,
+                      const int32_t* cu_seqlens_q, const int32_t* kv_lens, int batch, int total_q, int max_q_len,
+                      int num_heads, int num_kv_heads, int head_dim, float scale, int* error_word,
+                      nvk_stream_t stream);
+
+/*
+ * Dense causal prefill attention over contiguous key/value rows
+ * [total_kv, num_kv_heads, head_dim]; sequence b owns key rows
+ * [cu_seqlens_kv[b], cu_seqlens_kv[b+1]). Same masking and support as
+ * nvk_paged_prefill.
+ */
+NVK_API int nvk_dense_prefill(void* out, const void* query, const void* key, const void* value,
+                      const int32_t* cu_seqlens_q, const int32_t* cu_seqlens_kv, int batch, int total_q,
+                      int total_kv, int max_q_len, int num_heads, int num_kv_heads, int head_dim, float scale,
+                      int* error_word, nvk_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* NVK_PAGED_KV_H_ */

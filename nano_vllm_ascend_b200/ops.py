@@ -1,0 +1,233 @@
+"""Tensor-level wrappers over the C-ABI kernels.
+
+Each function validates devices, dtypes, shapes and strides, then calls the
+matching ``nvk_*`` entry point on the tensors' current CUDA stream. Nothing
+here computes on the host: there is no non-CUDA path.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import math
+
+import torch
+
+from . import _lib
+
+_BF16 = torch.bfloat16
+_KV_DTYPES = (torch.bfloat16, torch.float16)
+
+
+def _ptr(t: torch.Tensor | None) -> ctypes.c_void_p:
+    return ctypes.c_void_p(0 if t is None else t.data_ptr())
+
+
+def _stream(device: torch.device) -> ctypes.c_void_p:
+    return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+
+
+def _require_cuda(name: str, t: torch.Tensor, device: torch.device | None = None) -> None:
+    if not t.is_cuda:
+        raise ValueError(f"{name} must be a CUDA tensor (got device {t.device})")
+    if device is not None and t.device != device:
+        raise ValueError(f"{name} is on {t.device}, expected {device}")
+
+
+def _require_rows(name: str, t: torch.Tensor) -> None:
+    """[T, heads, dim] with heads and dims packed; the token stride may be larger."""
+    if t.dim() != 3 or t.stride(2) != 1 or t.stride(1) != t.shape[2]:
+        raise ValueError(f"{name} must be [tokens, heads, dim] with contiguous heads/dims, got "
+                         f"shape {tuple(t.shape)} stride {t.stride()}")
+
+
+# ----------------------------------------------------------------- append ---
+def kv_append(
+    key_cache: torch.Tensor,
+    value_cache: torch.Tensor,
+    key: torch.Tensor,
+    value: torch.Tensor,
+    slot_mapping: torch.Tensor,
+    error_word: torch.Tensor | None = None,
+) -> None:
+    """key_cache.view(-1, KVH, D)[slot_mapping] = key (same for value), in place.
+
+    ``key_cache``/``value_cache`` are ONE layer of the pool, [NB, BS, KVH, D]
+    contiguous. ``slot_mapping`` must be int64 on the same device.
+    """
+    dev = key_cache.device
+    for name, t in (("key_cache", key_cache), ("value_cache", value_cache), ("key", key), ("value", value),
+                    ("slot_mapping", slot_mapping)):
+        _require_cuda(name, t, dev)
+    if key_cache.dtype not in _KV_DTYPES or key.dtype != key_cache.dtype or value.dtype != key_cache.dtype \
+            or value_cache.dtype != key_cache.dtype:
+        raise ValueError(f"kv_append: dtype mismatch (cache {key_cache.dtype}, key {key.dtype}, value {value.dtype})")
+    if not (key_cache.is_contiguous() and value_cache.is_contiguous()) or key_cache.shape != value_cache.shape:
+        raise ValueError("kv_append: key/value cache must be contiguous and of equal shape")
+    num_blocks, block_size, kvh, d = key_cache.shape
+    _require_rows("key", key)
+    _require_rows("value", value)
+    if key.shape != value.shape or key.shape[1] != kvh or key.shape[2] != d:
+        raise ValueError(f"kv shape mismatch: got {tuple(key.shape)} / {tuple(value.shape)}")
+    if slot_mapping.dtype != torch.int64 or slot_mapping.numel() != key.shape[0]:
+        raise ValueError("kv_append: slot_mapping must be int64 with one entry per token")
+    slot_mapping = slot_mapping.contiguous()
+    if error_word is not None:
+        _require_cuda("error_word", error_word, dev)
+    _lib.call(
+        "nvk_kv_append", _ptr(key), _ptr(value), key.stride(0), value.stride(0), _ptr(key_cache), _ptr(value_cache),
+        _ptr(slot_mapping), key.shape[0], num_blocks * block_size, kvh, d, _ptr(error_word), _stream(dev),
+    )
+
+
+# ----------------------------------------------------------------- decode ---
+def decode_workspace_bytes(batch: int, num_heads: int, num_kv_heads: int, head_dim: int, max_splits: int) -> int:
+    out = ctypes.c_size_t(0)
+    _lib.call("nvk_paged_decode_workspace_size", batch, num_heads, num_kv_heads, head_dim, max_splits,
+              ctypes.byref(out))
+    return int(out.value)
+
+
+def choose_blocks_per_split(
+    num_kv_heads: int,
+    max_blocks_per_seq: int,
+    total_blocks: int | None,
+    batch: int,
+    num_sms: int = 148,
+    ctas_per_sm: int = 2,
+    waves: int = 4,
+    max_blocks_per_cta: int = 16,
+) -> int:
+    """Picks how many pool blocks one decode CTA walks.
+
+    Aims for at least ``waves`` full waves of CTAs (so the tail wave is short)
+    while capping one CTA's work, which bounds the load imbalance at the end
+    of the grid. ``total_blocks`` is the sum of ceil(ctx/bs) over the batch
+    when known (CPU context lengths), else half the table width per sequence.
+    """
+    if total_blocks is None:
+        total_blocks = max(1, batch * max(1, max_blocks_per_seq // 2))
+    target = num_sms * ctas_per_sm * waves
+    bps = math.ceil(num_kv_heads * total_blocks / target)
+    return int(max(1, min(bps, max_blocks_per_cta, max(1, max_blocks_per_seq))))
+
+
+def paged_decode(
+    out: torch.Tensor,
+    query: torch.Tensor,
+    key_cache: torch.Tensor,
+    value_cache: torch.Tensor,
+    block_tables: torch.Tensor,
+    context_lens: torch.Tensor,
+    scale: float,
+    workspace: torch.Tensor,
+    blocks_per_split: int,
+    max_splits: int | None = None,
+) -> torch.Tensor:
+    """Paged GQA decode attention into ``out`` ([B, H, D] bf16)."""
+    dev = query.device
+    for name, t in (("out", out), ("query", query), ("key_cache", key_cache), ("value_cache", value_cache),
+                    ("block_tables", block_tables), ("context_lens", context_lens), ("workspace", workspace)):
+        _require_cuda(name, t, dev)
+    if query.dtype != _BF16 or out.dtype != _BF16 or key_cache.dtype != _BF16 or value_cache.dtype != _BF16:
+        raise ValueError("paged_decode: query, out and caches must be bfloat16")
+    if not (query.is_contiguous() and out.is_contiguous() and key_cache.is_contiguous()
+            and value_cache.is_contiguous()):
+        raise ValueError("paged_decode: query, out and caches must be contiguous")
+    batch, num_heads, head_dim = query.shape
+    num_blocks, block_size, kvh, d = key_cache.shape
+    if d != head_dim or value_cache.shape != key_cache.shape or out.shape != query.shape:
+        raise ValueError(f"paged_decode: shape mismatch q={tuple(query.shape)} cache={tuple(key_cache.shape)}")
+    if block_tables.dtype != torch.int32 or block_tables.dim() != 2 or block_tables.stride(1) != 1 \
+            or block_tables.shape[0] != batch:
+        raise ValueError("paged_decode: block_tables must be int32 [batch, max_blocks] with unit column stride")
+    if context_lens.dtype != torch.int32 or context_lens.numel() != batch or not context_lens.is_contiguous():
+        raise ValueError("paged_decode: context_lens must be a contiguous int32 [batch] device tensor")
+    width = block_tables.shape[1]
+    if max_splits is None:
+        max_splits = math.ceil(width / blocks_per_split)
+    _lib.call(
+        "nvk_paged_decode", _ptr(out), _ptr(query), _ptr(key_cache), _ptr(value_cache), num_blocks, block_size,
+        _ptr(block_tables), block_tables.stride(0), width, _ptr(context_lens), batch, num_heads, kvh, head_dim,
+        float(scale), blocks_per_split, max_splits, _ptr(workspace), workspace.numel() * workspace.element_size(),
+        _stream(dev),
+    )
+    return out
+
+
+def decode_error_word(workspace: torch.Tensor) -> int:
+    """Reads (synchronously) the device error word at the head of a decode workspace."""
+    return int(workspace[:4].view(torch.int32).item())
+
+
+# ---------------------------------------------------------------- prefill ---
+def paged_prefill(
+    out: torch.Tensor,
+    query: torch.Tensor,
+    key_cache: torch.Tensor,
+    value_cache: torch.Tensor,
+    block_tables: torch.Tensor,
+    cu_seqlens_q: torch.Tensor,
+    kv_lens: torch.Tensor,
+    max_q_len: int,
+    scale: float,
+    error_word: torch.Tensor | None = None,
+) -> torch.Tensor:
+    """Causal (bottom-right) prefill attention over the paged pool into ``out``."""
+    dev = query.device
+    for name, t in (("out", out), ("query", query), ("key_cache", key_cache), ("value_cache", value_cache),
+                    ("block_tables", block_tables), ("cu_seqlens_q", cu_seqlens_q), ("kv_lens", kv_lens)):
+        _require_cuda(name, t, dev)
+    if query.dtype != _BF16 or out.dtype != _BF16 or key_cache.dtype != _BF16 or value_cache.dtype != _BF16:
+        raise ValueError("paged_prefill: query, out and caches must be bfloat16")
+    if not (query.is_contiguous() and out.is_contiguous() and key_cache.is_contiguous()
+            and value_cache.is_contiguous()):
+        raise ValueError("paged_prefill: query, out and caches must be contiguous")
+    total_q, num_heads, head_dim = query.shape
+    num_blocks, block_size, kvh, d = key_cache.shape
+    batch = kv_lens.numel()
+    if d != head_dim or out.shape != query.shape or value_cache.shape != key_cache.shape:
+        raise ValueError("paged_prefill: shape mismatch")
+    if block_tables.dtype != torch.int32 or block_tables.dim() != 2 or block_tables.stride(1) != 1 \
+            or block_tables.shape[0] != batch:
+        raise ValueError("paged_prefill: block_tables must be int32 [batch, max_blocks]")
+    if cu_seqlens_q.dtype != torch.int32 or cu_seqlens_q.numel() != batch + 1 or kv_lens.dtype != torch.int32:
+        raise ValueError("paged_prefill: cu_seqlens_q must be int32 [batch+1] and kv_lens int32 [batch]")
+    _lib.call(
+        "nvk_paged_prefill", _ptr(out), _ptr(query), _ptr(key_cache), _ptr(value_cache), num_blocks, block_size,
+        _ptr(block_tables), block_tables.stride(0), _ptr(cu_seqlens_q.contiguous()), _ptr(kv_lens.contiguous()),
+        batch, total_q, int(max_q_len), num_heads, kvh, head_dim, float(scale), _ptr(error_word), _stream(dev),
+    )
+    return out
+
+
+def dense_prefill(
+    out: torch.Tensor,
+    query: torch.Tensor,
+    key: torch.Tensor,
+    value: torch.Tensor,
+    cu_seqlens_q: torch.Tensor,
+    cu_seqlens_kv: torch.Tensor,
+    max_q_len: int,
+    scale: float,
+    error_word: torch.Tensor | None = None,
+) -> torch.Tensor:
+    """Causal (bottom-right) prefill attention over contiguous K/V rows."""
+    dev = query.device
+    for name, t in (("out", out), ("query", query), ("key", key), ("value", value), ("cu_seqlens_q", cu_seqlens_q),
+                    ("cu_seqlens_kv", cu_seqlens_kv)):
+        _require_cuda(name, t, dev)
+    if any(t.dtype != _BF16 for t in (out, query, key, value)):
+        raise ValueError("dense_prefill: tensors must be bfloat16")
+    if not all(t.is_contiguous() for t in (out, query, key, value)):
+        raise ValueError("dense_prefill: tensors must be contiguous")
+    total_q, num_heads, head_dim = query.shape
+    total_kv, kvh, d = key.shape
+    batch = cu_seqlens_q.numel() - 1
+    if d != head_dim or value.shape != key.shape or out.shape != query.shape or cu_seqlens_kv.numel() != batch + 1:
+        raise ValueError("dense_prefill: shape mismatch")
+    _lib.call(
+        "nvk_dense_prefill", _ptr(out), _ptr(query), _ptr(key), _ptr(value), _ptr(cu_seqlens_q.contiguous()),
+        _ptr(cu_seqlens_kv.contiguous()), batch, total_q, total_kv, int(max_q_len), num_heads, kvh, head_dim,
+        float(scale), _ptr(error_word), _stream(dev),
+    )
+    return out

@@ -1,0 +1,97 @@
+"""C-ABI library checks that need no GPU.
+
+The library loads on a host without a driver, exports exactly the entry points
+declared in include/*.h, and rejects bad arguments on the host (before any CUDA
+call) with the documented status codes.
+"""
+
+import ctypes
+import re
+import subprocess
+from pathlib import Path
+
+import pytest
+
+from nano_vllm_ascend_b200 import _lib
+
+ROOT = Path(__file__).resolve().parent.parent
+HEADERS = sorted((ROOT / "include").glob("*.h"))
+
+
+def declared_functions() -> set[str]:
+    names = set()
+    for h in HEADERS:
+        text = h.read_text()
+        text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+        for m in re.finditer(r"^\s*(?:const\s+)?[A-Za-z_][A-Za-z0-9_\s\*]*?\b(nvk_[a-z0-9_]+)\s*\(", text, re.M):
+            names.add(m.group(1))
+    return names
+
+
+def test_headers_declare_the_boundary():
+    names = declared_functions()
+    assert {"nvk_kv_append", "nvk_paged_decode", "nvk_paged_decode_workspace_size", "nvk_paged_prefill",
+            "nvk_dense_prefill", "nvk_last_error", "nvk_abi_version"} <= names
+
+
+def test_library_exports_every_declared_symbol():
+    lib = _lib.load()
+    for name in declared_functions():
+        assert hasattr(lib, name), f"{name} declared in include/ but not exported"
+    assert set(_lib.SIGNATURES) == declared_functions()
+    out = subprocess.run(["nm", "-D", "--defined-only", str(_lib.LIB_PATH)], capture_output=True, text=True).stdout
+    exported = {line.split()[-1] for line in out.splitlines() if " T " in line and "nvk_" in line}
+    assert exported == declared_functions(), "only the declared C entry points may be exported"
+
+
+def test_version_and_error_string():
+    lib = _lib.load()
+    assert lib.nvk_abi_version() == 1
+    assert isinstance(lib.nvk_last_error(), bytes)
+
+
+def test_host_side_validation_codes():
+    lib = _lib.load()
+    n = ctypes.c_void_p(0)
+    # unsupported head_dim -> NVK_ERR_UNSUPPORTED with a message
+    rc = lib.nvk_paged_decode(n, n, n, n, 8, 128, n, 4, 4, n, 2, 16, 8, 64, 0.1, 1, 4, n, 0, n)
+    assert rc == _lib.NVK_ERR_UNSUPPORTED and b"head_dim" in lib.nvk_last_error()
+    # GQA ratio 3 unsupported
+    rc = lib.nvk_paged_decode(n, n, n, n, 8, 128, n, 4, 4, n, 2, 24, 8, 128, 0.1, 1, 4, n, 0, n)
+    assert rc == _lib.NVK_ERR_UNSUPPORTED
+    # block size not a power of two
+    rc = lib.nvk_paged_decode(n, n, n, n, 8, 96, n, 4, 4, n, 2, 16, 8, 128, 0.1, 1, 4, n, 0, n)
+    assert rc == _lib.NVK_ERR_UNSUPPORTED and b"block_size" in lib.nvk_last_error()
+    # too few splits for the table width
+    rc = lib.nvk_paged_decode(n, n, n, n, 8, 128, n, 8, 8, n, 2, 16, 8, 128, 0.1, 2, 3, n, 0, n)
+    assert rc == _lib.NVK_ERR_INVALID_ARGUMENT and b"max_splits" in lib.nvk_last_error()
+    # null pointers are rejected before any launch
+    rc = lib.nvk_paged_decode(n, n, n, n, 8, 128, n, 4, 4, n, 2, 16, 8, 128, 0.1, 1, 4, n, 0, n)
+    assert rc == _lib.NVK_ERR_INVALID_ARGUMENT
+    # batch 0 is a no-op
+    rc = lib.nvk_paged_decode(n, n, n, n, 8, 128, n, 4, 4, n, 0, 16, 8, 128, 0.1, 1, 4, n, 0, n)
+    assert rc == _lib.NVK_OK
+    # append: row not a multiple of 16 bytes, zero tokens is a no-op
+    rc = lib.nvk_kv_append(n, n, 3, 3, n, n, n, 1, 8, 1, 3, n, n)
+    assert rc == _lib.NVK_ERR_UNSUPPORTED
+    assert lib.nvk_kv_append(n, n, 1024, 1024, n, n, n, 0, 8, 8, 128, n, n) == _lib.NVK_OK
+    rc = lib.nvk_kv_append(n, n, 1024, 1024, n, n, n, 4, 8, 8, 128, n, n)
+    assert rc == _lib.NVK_ERR_INVALID_ARGUMENT
+
+
+def test_workspace_size_is_monotone():
+    sz = ctypes.c_size_t()
+    lib = _lib.load()
+    sizes = []
+    for splits in (1, 2, 8):
+        assert lib.nvk_paged_decode_workspace_size(32, 16, 8, 128, splits, ctypes.byref(sz)) == 0
+        sizes.append(sz.value)
+    assert sizes[0] < sizes[1] < sizes[2]
+    # 32 seqs x 8 kv heads x 8 splits x 2 q heads x 128 floats is the bulk
+    assert sizes[2] >= 32 * 8 * 8 * 2 * 128 * 4
+    assert lib.nvk_paged_decode_workspace_size(32, 16, 8, 64, 1, ctypes.byref(sz)) == _lib.NVK_ERR_UNSUPPORTED
+
+
+def test_call_wrapper_raises_value_error_on_bad_arguments():
+    with pytest.raises(ValueError, match="head_dim"):
+        _lib.call("nvk_paged_decode_workspace_size", 1, 16, 8, 64, 1, ctypes.byref(ctypes.c_size_t()))
