@@ -114,6 +114,30 @@ NVK_API int nvk_paged_decode(void* out, const void* query, const void* key_cache
                      nvk_stream_t stream);
 
 /*
+ * nvk_paged_decode without a caller workspace. No counterpart in the
+ * reference: it exists for callers that cannot allocate device memory where
+ * they run attention (a plugin's enqueue callback inside a framework that owns
+ * all device buffers, a cgo/JNI/N-API binding with no device allocator, a
+ * serving thread that must not take cudaMalloc's implicit synchronisation).
+ *
+ * Same arguments and results as nvk_paged_decode. The split-K scratch is a
+ * fixed 16 MiB array in the library's device memory, present on every GPU
+ * that loads the library until the process exits; a call whose scratch need
+ * (nvk_paged_decode_workspace_size) exceeds 16 MiB returns
+ * NVK_ERR_UNSUPPORTED. It calls no allocator. The first call on each device
+ * resolves the array's device address (cudaGetSymbolAddress) and caches it;
+ * make that first call before any stream capture begins on the device. Every
+ * call clears the scratch's error word and counters on `stream` and then uses
+ * the same array, so calls whose execution overlaps on the GPU (different
+ * streams, or different host threads) race: order them on one stream.
+ */
+NVK_API int nvk_paged_decode_noalloc(void* out, const void* query, const void* key_cache, const void* value_cache,
+                                     int num_blocks, int block_size, const int32_t* block_tables,
+                                     int block_table_stride, int max_blocks_per_seq, const int32_t* context_lens,
+                                     int batch, int num_heads, int num_kv_heads, int head_dim, float scale,
+                                     int blocks_per_split, int max_splits, nvk_stream_t stream);
+
+/*
  * Paged causal prefill attention (prefix-cache aware). Sequence b owns query
  * rows [cu_seqlens_q[b], cu_seqlens_q[b+1]) of `query` and attends over the
  * first kv_lens[b] tokens of its paged KV (cached prefix + the rows appended

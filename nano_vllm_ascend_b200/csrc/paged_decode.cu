@@ -27,6 +27,7 @@
 //    the last CTA of a (seq, kv_head) to arrive (atomic ticket) merges them and
 //    resets the ticket, so the workspace is reusable and graph-capturable.
 #include <cfloat>
+#include <mutex>
 
 #include "host_common.h"
 #include "nvk_common.cuh"
@@ -520,4 +521,87 @@ extern "C" int nvk_paged_decode(void* out, const void* query, const void* key_ca
     case 4: return launch<4>(km, vm, a, batch, st);
     default: return launch<8>(km, vm, a, batch, st);
   }
+}
+
+// ---------------------------------------------------------------------------
+// Allocation-free decode entry point.
+//
+// Some callers cannot allocate device memory where they run attention: a
+// plugin's enqueue callback inside a host framework that owns every device
+// buffer and forbids allocating there, a binding from a language with no
+// device allocator of its own (cgo, JNI, N-API), or a latency-critical serving
+// thread that must not take cudaMalloc's implicit device synchronisation. For
+// them the split-K scratch lives in a fixed array in this library's device
+// memory instead of a caller-provided workspace. The array costs
+// kNoAllocScratchBytes on every GPU that loads the library, until the process
+// exits.
+namespace {
+
+constexpr size_t kNoAllocScratchBytes = size_t(16) << 20;  // 16 MiB per device
+constexpr int kNoAllocMaxDevices = 64;
+
+}  // namespace
+
+static __device__ __align__(256) uint8_t g_noalloc_decode_scratch[kNoAllocScratchBytes];
+
+namespace {
+
+// Device address of the scratch array on the current device. The symbol's
+// host-side name is only a handle: the address is fetched with
+// cudaGetSymbolAddress once per device (with that device current) and cached.
+int noalloc_scratch(void** out) {
+  static std::mutex mu;
+  static void* addr[kNoAllocMaxDevices] = {};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return nvk::check_cuda(e, "paged_decode_noalloc: cudaGetDevice");
+  if (dev < 0 || dev >= kNoAllocMaxDevices)
+    return nvk::fail(NVK_ERR_UNSUPPORTED, "paged_decode_noalloc: device %d above %d", dev, kNoAllocMaxDevices);
+  std::lock_guard<std::mutex> lock(mu);
+  if (addr[dev] == nullptr) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_noalloc_decode_scratch);
+    if (e != cudaSuccess) return nvk::check_cuda(e, "paged_decode_noalloc: cudaGetSymbolAddress");
+    addr[dev] = p;
+  }
+  *out = addr[dev];
+  return NVK_OK;
+}
+
+}  // namespace
+
+extern "C" int nvk_paged_decode_noalloc(void* out, const void* query, const void* key_cache,
+                                        const void* value_cache, int num_blocks, int block_size,
+                                        const int32_t* block_tables, int block_table_stride, int max_blocks_per_seq,
+                                        const int32_t* context_lens, int batch, int num_heads, int num_kv_heads,
+                                        int head_dim, float scale, int blocks_per_split, int max_splits,
+                                        nvk_stream_t stream) {
+  using namespace nvk;
+  size_t need = 0;
+  size_t header = 0;
+  const bool sane = batch > 0 && num_heads > 0 && num_kv_heads > 0 && num_heads % num_kv_heads == 0 &&
+                    max_splits > 0 && head_dim == kD;
+  if (sane) {
+    const WsLayout wl = ws_layout(batch, num_heads, num_kv_heads, max_splits);
+    need = wl.total;
+    header = wl.ml_off;  // error word + arrival counters
+    if (need > kNoAllocScratchBytes)
+      return fail(NVK_ERR_UNSUPPORTED,
+                  "paged_decode_noalloc: %zu bytes of split-K scratch needed, the static scratch holds %zu "
+                  "(fewer splits, a smaller batch, or nvk_paged_decode with a caller workspace)",
+                  need, kNoAllocScratchBytes);
+  }
+  void* scratch = nullptr;
+  int rc = noalloc_scratch(&scratch);
+  if (rc != NVK_OK) return rc;
+  if (sane) {
+    // The array keeps the previous call's contents: clear the error word and
+    // the arrival counters, which must start at zero.
+    rc = check_cuda(cudaMemsetAsync(scratch, 0, header, reinterpret_cast<cudaStream_t>(stream)),
+                    "paged_decode_noalloc: clear scratch header");
+    if (rc != NVK_OK) return rc;
+  }
+  return nvk_paged_decode(out, query, key_cache, value_cache, num_blocks, block_size, block_tables,
+                          block_table_stride, max_blocks_per_seq, context_lens, batch, num_heads, num_kv_heads,
+                          head_dim, scale, blocks_per_split, max_splits, scratch, kNoAllocScratchBytes, stream);
 }
