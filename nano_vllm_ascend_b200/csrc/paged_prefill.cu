@@ -1,14 +1,423 @@
-// Causal prefill attention (paged and dense). The tcgen05 kernel lands here;
-// until then both entry points report NVK_ERR_UNSUPPORTED.
+// Causal prefill attention on the sm_100a tensor cores (tcgen05 + TMEM).
+//
+// Replaces torch_npu.npu_fused_infer_attention_score as called from
+// src/nanovllm_ascend/layers/npu_prefill_attention.py:82-112 (TND layout,
+// sparse_mode=3): paged mode reads the whole KV of a sequence (cached prefix
+// + rows appended this step) through its block table with absolute kv
+// lengths; dense mode reads contiguous K/V rows delimited by cumulative
+// lengths. Masking is bottom-right aligned: query i of a sequence with Lq
+// queries and Lk keys sees key j iff j <= Lk - Lq + i.
+//
+// One CTA = 128 query rows of one sequence x one query head.
+//   warp 4 (producer): TMA loads of the Q tile once, then 128-key K and V
+//     tiles (one pool block each, 128-byte swizzle = the canonical UMMA
+//     operand layout) into a 2-stage ring.
+//   warp 5 (MMA): allocates 256 TMEM columns (S: 0-127, O: 128-255) and one
+//     lane issues S = Q K^T (8 x M128 N128 K16, both K-major) and
+//     O += P V (8 x M128 N128 K16, P K-major from smem, V MN-major), with
+//     tcgen05.commit signalling the mbarriers.
+//   warps 0-3 (softmax): thread r owns query row r = TMEM lane r: loads its
+//     S row (tcgen05.ld), masks, base-2 online softmax with lazy rescaling
+//     of O in TMEM (only when the running max grows by more than 2^8), writes
+//     P as bf16 into smem in the K-major SW128 layout, and at the end
+//     normalises its O row and stores it.
+// Every mbarrier wait is bounded; on a timeout the CTA records the error,
+// drains its in-flight copies and MMAs, frees TMEM and exits.
 #include "host_common.h"
+#include "nvk_common.cuh"
+#include "tcgen05.cuh"
 
-extern "C" int nvk_paged_prefill(void*, const void*, const void*, const void*, int, int, const int32_t*, int,
-                                 const int32_t*, const int32_t*, int, int, int, int, int, int, float, int*,
-                                 nvk_stream_t) {
-  return nvk::fail(NVK_ERR_UNSUPPORTED, "paged_prefill: not built yet");
+namespace nvk {
+namespace {
+
+constexpr int kD = 128;
+constexpr int kRows = 128;              // query rows per CTA, keys per KV tile
+constexpr int kHalfBytes = kRows * 128; // one 64-dim half of a 128-row tile
+constexpr int kTileBytes = 2 * kHalfBytes;
+constexpr int kStages = 2;
+constexpr int kSoftmaxThreads = 128;
+constexpr int kProducerWarp = 4;
+constexpr int kMmaWarp = 5;
+constexpr int kThreads = 6 * 32;
+constexpr uint32_t kTmemCols = 256;
+constexpr float kRescaleThreshold = 8.0f;
+
+struct PrefillArgs {
+  __nv_bfloat16* out;
+  const int32_t* block_tables;
+  const int32_t* cu_q;
+  const int32_t* kv_lens;  // paged: absolute kv length per sequence
+  const int32_t* cu_kv;    // dense: cumulative kv rows
+  int* err;
+  int bt_stride;
+  int num_blocks;
+  int num_heads;
+  int qpk;
+  int paged;
+  float scale_log2;
+};
+
+struct PrefillSmem {
+  alignas(1024) uint8_t q[kTileBytes];
+  alignas(1024) uint8_t k[kStages][kTileBytes];
+  alignas(1024) uint8_t v[kStages][kTileBytes];
+  alignas(1024) uint8_t p[kTileBytes];
+  uint64_t bar_q;
+  uint64_t full_k[kStages];
+  uint64_t full_v[kStages];
+  uint64_t kv_empty[kStages];
+  uint64_t s_full;
+  uint64_t p_full;
+  uint64_t o_done;
+  uint64_t fin;
+  uint32_t tmem_base;
+  volatile int abort;
+};
+
+__device__ __forceinline__ void flag_error(const PrefillArgs& a, PrefillSmem& sm, int code) {
+  if (a.err) atomicOr(a.err, code);
+  sm.abort = 1;
 }
 
-extern "C" int nvk_dense_prefill(void*, const void*, const void*, const void*, const int32_t*, const int32_t*, int,
-                                 int, int, int, int, int, int, float, int*, nvk_stream_t) {
-  return nvk::fail(NVK_ERR_UNSUPPORTED, "dense_prefill: not built yet");
+__global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_constant__ CUtensorMap qmap,
+                                                              const __grid_constant__ CUtensorMap kmap,
+                                                              const __grid_constant__ CUtensorMap vmap,
+                                                              const PrefillArgs a) {
+  const int qt = gridDim.x - 1 - blockIdx.x;  // heaviest (last) query tiles first
+  const int h = blockIdx.y, b = blockIdx.z;
+  const int q0 = a.cu_q[b];
+  const int lq = a.cu_q[b + 1] - q0;
+  if (qt * kRows >= lq) return;
+  const int lk = a.paged ? a.kv_lens[b] : (a.cu_kv[b + 1] - a.cu_kv[b]);
+  const int kv_row0 = a.paged ? 0 : a.cu_kv[b];
+  const int g = h / a.qpk;
+  const int i_last = min(qt * kRows + kRows - 1, lq - 1);
+  const int lim_last = min(lk - lq + i_last, lk - 1);
+  const int n_kv = lim_last < 0 ? 0 : lim_last / kRows + 1;
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  __nv_bfloat16* out_row = nullptr;
+  const int i = qt * kRows + tid;  // query row within the sequence (softmax threads)
+  if (tid < kSoftmaxThreads && i < lq) out_row = a.out + (static_cast<int64_t>(q0 + i) * a.num_heads + h) * kD;
+
+  if (n_kv == 0) {  // no visible key for any row of this tile: zeros
+    if (out_row) {
+      for (int c = 0; c < kD; c += 8) *reinterpret_cast<uint4*>(out_row + c) = make_uint4(0, 0, 0, 0);
+    }
+    return;
+  }
+
+  extern __shared__ uint8_t smem_raw[];
+  PrefillSmem& sm =
+      *reinterpret_cast<PrefillSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+
+  if (tid == 0) {
+    mbar_init(&sm.bar_q, 1);
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&sm.full_k[s], 1);
+      mbar_init(&sm.full_v[s], 1);
+      mbar_init(&sm.kv_empty[s], 1);
+    }
+    mbar_init(&sm.s_full, 1);
+    mbar_init(&sm.p_full, kSoftmaxThreads);
+    mbar_init(&sm.o_done, 1);
+    mbar_init(&sm.fin, 1);
+    sm.abort = 0;
+    fence_mbar_init();
+  }
+  if (warp == kMmaWarp) {
+    tmem_alloc(&sm.tmem_base, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = sm.tmem_base;
+  const uint32_t tmem_s = tmem;
+  const uint32_t tmem_o = tmem + kRows;
+
+  if (warp == kProducerWarp) {
+    // -------------------------------------------------------- producer ----
+    if (lane == 0) {
+      tma_prefetch_desc(&qmap);
+      tma_prefetch_desc(&kmap);
+      tma_prefetch_desc(&vmap);
+      mbar_arrive_expect_tx(&sm.bar_q, kTileBytes);
+      tma_load_3d(sm.q, &qmap, &sm.bar_q, 0, h, q0 + qt * kRows);
+      tma_load_3d(sm.q + kHalfBytes, &qmap, &sm.bar_q, 64, h, q0 + qt * kRows);
+      const int32_t* bt = a.block_tables + static_cast<int64_t>(b) * a.bt_stride;
+      int issued = 0;
+      for (int j = 0; j < n_kv && !sm.abort; ++j) {
+        const int s = j & 1;
+        if (j >= kStages && !mbar_wait(&sm.kv_empty[s], ((j >> 1) - 1) & 1)) {
+          flag_error(a, sm, kErrWaitTimeout);
+          break;
+        }
+        int row;
+        if (a.paged) {
+          int blk = bt[j];
+          if (blk < 0 || blk >= a.num_blocks) {
+            if (a.err) atomicOr(a.err, kErrBadBlockId);
+            blk = a.num_blocks;  // fully outside the tensor map: zero fill
+          }
+          row = blk * kRows;
+        } else {
+          row = kv_row0 + j * kRows;
+        }
+        mbar_arrive_expect_tx(&sm.full_k[s], kTileBytes);
+        tma_load_3d(sm.k[s], &kmap, &sm.full_k[s], 0, g, row);
+        tma_load_3d(sm.k[s] + kHalfBytes, &kmap, &sm.full_k[s], 64, g, row);
+        mbar_arrive_expect_tx(&sm.full_v[s], kTileBytes);
+        tma_load_3d(sm.v[s], &vmap, &sm.full_v[s], 0, g, row);
+        tma_load_3d(sm.v[s] + kHalfBytes, &vmap, &sm.full_v[s], 64, g, row);
+        ++issued;
+      }
+      // Drain every copy this CTA issued before it may exit.
+      (void)mbar_wait(&sm.bar_q, 0);
+      for (int j = max(0, issued - kStages); j < issued; ++j) {
+        (void)mbar_wait(&sm.full_k[j & 1], (j >> 1) & 1);
+        (void)mbar_wait(&sm.full_v[j & 1], (j >> 1) & 1);
+      }
+    }
+  } else if (warp == kMmaWarp) {
+    // ------------------------------------------------------------- MMA ----
+    if (lane == 0) {
+      constexpr uint32_t idesc_qk = umma_idesc_bf16(kRows, kRows, false);
+      constexpr uint32_t idesc_pv = umma_idesc_bf16(kRows, kD, true);
+      const uint32_t q_addr = smem_u32(sm.q), p_addr = smem_u32(sm.p);
+      bool ok = mbar_wait(&sm.bar_q, 0);
+      if (!ok) flag_error(a, sm, kErrWaitTimeout);
+      for (int j = 0; ok && j < n_kv; ++j) {
+        const int s = j & 1;
+        const uint32_t ph = (j >> 1) & 1;
+        if (!mbar_wait(&sm.full_k[s], ph)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t k_addr = smem_u32(sm.k[s]);
+#pragma unroll
+        for (int kk = 0; kk < kD / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * kHalfBytes + (kk & 3) * 32;
+          umma_f16_ss(tmem_s, smem_desc_sw128(q_addr + off, 16, 1024), smem_desc_sw128(k_addr + off, 16, 1024),
+                      idesc_qk, kk > 0);
+        }
+        umma_commit(&sm.s_full);
+        if (!mbar_wait(&sm.p_full, j & 1)) { ok = false; break; }
+        tc_fence_after();
+        if (!mbar_wait(&sm.full_v[s], ph)) { ok = false; break; }
+        const uint32_t v_addr = smem_u32(sm.v[s]);
+#pragma unroll
+        for (int kk = 0; kk < kRows / 16; ++kk) {
+          const uint64_t pa = smem_desc_sw128(p_addr + (kk >> 2) * kHalfBytes + (kk & 3) * 32, 16, 1024);
+          const uint64_t vb = smem_desc_sw128(v_addr + kk * 16 * 128, kHalfBytes, 1024);
+          umma_f16_ss(tmem_o, pa, vb, idesc_pv, (j > 0 || kk > 0) ? 1u : 0u);
+        }
+        umma_commit(&sm.kv_empty[s]);
+        umma_commit(&sm.o_done);
+      }
+      if (!ok) flag_error(a, sm, kErrWaitTimeout);
+      // All MMAs of this CTA complete before TMEM is released.
+      umma_commit(&sm.fin);
+      (void)mbar_wait(&sm.fin, 0);
+    }
+  } else {
+    // --------------------------------------------------------- softmax ----
+    const int r = tid;
+    const int lim = (i < lq) ? (lk - lq + i) : (lk - 1);
+    const uint32_t t_lane = static_cast<uint32_t>(warp * 32) << 16;
+    const uint32_t p_row = smem_u32(sm.p) + r * 128;
+    const int sw = r & 7;
+    float m = -INFINITY, l = 0.f;
+    bool ok = true;
+    for (int j = 0; j < n_kv; ++j) {
+      // warp-uniform outcome: the tcgen05.ld/st below need a converged warp
+      if (!__all_sync(0xffffffffu, mbar_wait(&sm.s_full, j & 1))) { ok = false; break; }
+      tc_fence_after();
+      uint32_t sr[4][32];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) tmem_ld32(tmem_s + t_lane + c * 32, sr[c]);
+      tmem_ld_wait();
+      const int kbase = j * kRows;
+      const bool need_mask = kbase + kRows - 1 > lim;
+      float mt = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+#pragma unroll
+        for (int e = 0; e < 32; ++e) {
+          float x = __uint_as_float(sr[c][e]) * a.scale_log2;
+          if (need_mask && kbase + c * 32 + e > lim) x = -INFINITY;
+          sr[c][e] = __float_as_uint(x);
+          mt = fmaxf(mt, x);
+        }
+      }
+      const float m_new = fmaxf(m, mt);
+      const bool resc = m_new > m + kRescaleThreshold;
+      const float alpha = resc ? fast_exp2(m - m_new) : 1.f;
+      if (j > 0) {
+        if (!__all_sync(0xffffffffu, mbar_wait(&sm.o_done, (j - 1) & 1))) { ok = false; break; }
+        tc_fence_after();
+        if (__any_sync(0xffffffffu, resc)) {
+#pragma unroll 1
+          for (int c = 0; c < 4; ++c) {
+            uint32_t o[32];
+            tmem_ld32(tmem_o + t_lane + c * 32, o);
+            tmem_ld_wait();
+#pragma unroll
+            for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
+            tmem_st32(tmem_o + t_lane + c * 32, o);
+          }
+          tmem_st_wait();
+        }
+      }
+      if (resc) {
+        l *= alpha;
+        m = m_new;
+      }
+      const float mu = (m == -INFINITY) ? 0.f : m;
+      float sum = 0.f;
+#pragma unroll
+      for (int c8 = 0; c8 < 16; ++c8) {  // 16 chunks of 8 keys
+        const int c = c8 >> 2, e0 = (c8 & 3) * 8;
+        uint32_t w[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float p0 = fast_exp2(__uint_as_float(sr[c][e0 + 2 * e]) - mu);
+          const float p1 = fast_exp2(__uint_as_float(sr[c][e0 + 2 * e + 1]) - mu);
+          sum += p0 + p1;
+          w[e] = pack_bf16x2(p0, p1);
+        }
+        const int half = c8 >> 3, chunk = c8 & 7;
+        st_shared_v4(p_row + half * kHalfBytes + ((chunk ^ sw) << 4), w[0], w[1], w[2], w[3]);
+      }
+      l += sum;
+      fence_proxy_async_smem();
+      tc_fence_before();
+      mbar_arrive(&sm.p_full);
+    }
+    if (ok && !__all_sync(0xffffffffu, mbar_wait(&sm.o_done, (n_kv - 1) & 1))) ok = false;
+    if (!ok) {
+      flag_error(a, sm, kErrWaitTimeout);
+    } else {
+      tc_fence_after();
+      const float inv = l > 0.f ? 1.f / l : 0.f;
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        uint32_t o[32];
+        tmem_ld32(tmem_o + t_lane + c * 32, o);
+        tmem_ld_wait();
+        if (out_row) {
+#pragma unroll
+          for (int q4 = 0; q4 < 4; ++q4) {
+            uint4 wv;
+            wv.x = pack_bf16x2(__uint_as_float(o[q4 * 8 + 0]) * inv, __uint_as_float(o[q4 * 8 + 1]) * inv);
+            wv.y = pack_bf16x2(__uint_as_float(o[q4 * 8 + 2]) * inv, __uint_as_float(o[q4 * 8 + 3]) * inv);
+            wv.z = pack_bf16x2(__uint_as_float(o[q4 * 8 + 4]) * inv, __uint_as_float(o[q4 * 8 + 5]) * inv);
+            wv.w = pack_bf16x2(__uint_as_float(o[q4 * 8 + 6]) * inv, __uint_as_float(o[q4 * 8 + 7]) * inv);
+            *reinterpret_cast<uint4*>(out_row + c * 32 + q4 * 8) = wv;
+          }
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == kMmaWarp) {
+    __syncwarp();
+    tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+int launch_prefill(const CUtensorMap& qm, const CUtensorMap& km, const CUtensorMap& vm, const PrefillArgs& a,
+                   int batch, int max_q_len, cudaStream_t stream) {
+  const size_t smem = sizeof(PrefillSmem) + 1024;
+  int rc = ensure_dynamic_smem(reinterpret_cast<const void*>(&prefill_kernel), smem);
+  if (rc != NVK_OK) return rc;
+  const dim3 grid((max_q_len + kRows - 1) / kRows, a.num_heads, batch);
+  prefill_kernel<<<grid, kThreads, smem, stream>>>(qm, km, vm, a);
+  return check_cuda(cudaGetLastError(), "prefill launch");
+}
+
+int check_common(const void* out, const void* query, int batch, int total_q, int max_q_len, int num_heads,
+                 int num_kv_heads, int head_dim, const char* who) {
+  if (batch < 0 || total_q < 0 || max_q_len < 0 || num_heads <= 0 || num_kv_heads <= 0)
+    return fail(NVK_ERR_INVALID_ARGUMENT, "%s: bad sizes (batch=%d total_q=%d max_q_len=%d heads=%d kv_heads=%d)",
+                who, batch, total_q, max_q_len, num_heads, num_kv_heads);
+  if (head_dim != kD) return fail(NVK_ERR_UNSUPPORTED, "%s: head_dim %d unsupported (128 only)", who, head_dim);
+  if (num_heads % num_kv_heads != 0)
+    return fail(NVK_ERR_INVALID_ARGUMENT, "%s: num_heads %d not a multiple of num_kv_heads %d", who, num_heads,
+                num_kv_heads);
+  if (batch > 65535 || num_heads > 65535)
+    return fail(NVK_ERR_UNSUPPORTED, "%s: batch %d or heads %d above grid limit", who, batch, num_heads);
+  if (!out || !query) return fail(NVK_ERR_INVALID_ARGUMENT, "%s: null pointer", who);
+  if (!aligned16(out) || !aligned16(query))
+    return fail(NVK_ERR_INVALID_ARGUMENT, "%s: q/out must be 16-byte aligned", who);
+  return NVK_OK;
+}
+
+}  // namespace
+}  // namespace nvk
+
+extern "C" int nvk_paged_prefill(void* out, const void* query, const void* key_cache, const void* value_cache,
+                                 int num_blocks, int block_size, const int32_t* block_tables, int block_table_stride,
+                                 const int32_t* cu_seqlens_q, const int32_t* kv_lens, int batch, int total_q,
+                                 int max_q_len, int num_heads, int num_kv_heads, int head_dim, float scale,
+                                 int* error_word, nvk_stream_t stream) {
+  using namespace nvk;
+  int rc = check_common(out, query, batch, total_q, max_q_len, num_heads, num_kv_heads, head_dim, "paged_prefill");
+  if (rc != NVK_OK) return rc;
+  if (batch == 0 || total_q == 0 || max_q_len == 0) return NVK_OK;
+  if (block_size != kRows)
+    return fail(NVK_ERR_UNSUPPORTED, "paged_prefill: block_size %d unsupported (128 only)", block_size);
+  if (num_blocks <= 0 || !key_cache || !value_cache || !block_tables || !cu_seqlens_q || !kv_lens)
+    return fail(NVK_ERR_INVALID_ARGUMENT, "paged_prefill: null pointer or empty pool");
+  if (block_table_stride <= 0) return fail(NVK_ERR_INVALID_ARGUMENT, "paged_prefill: bad block table stride");
+  CUtensorMap qm, km, vm;
+  if ((rc = kv_tensor_map(&qm, query, total_q, num_heads, kRows)) != NVK_OK) return rc;
+  const int64_t rows = static_cast<int64_t>(num_blocks) * block_size;
+  if ((rc = kv_tensor_map(&km, key_cache, rows, num_kv_heads, kRows)) != NVK_OK) return rc;
+  if ((rc = kv_tensor_map(&vm, value_cache, rows, num_kv_heads, kRows)) != NVK_OK) return rc;
+  PrefillArgs a{};
+  a.out = static_cast<__nv_bfloat16*>(out);
+  a.block_tables = block_tables;
+  a.cu_q = cu_seqlens_q;
+  a.kv_lens = kv_lens;
+  a.cu_kv = nullptr;
+  a.err = error_word;
+  a.bt_stride = block_table_stride;
+  a.num_blocks = num_blocks;
+  a.num_heads = num_heads;
+  a.qpk = num_heads / num_kv_heads;
+  a.paged = 1;
+  a.scale_log2 = scale * 1.4426950408889634f;
+  return launch_prefill(qm, km, vm, a, batch, max_q_len, reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" int nvk_dense_prefill(void* out, const void* query, const void* key, const void* value,
+                                 const int32_t* cu_seqlens_q, const int32_t* cu_seqlens_kv, int batch, int total_q,
+                                 int total_kv, int max_q_len, int num_heads, int num_kv_heads, int head_dim,
+                                 float scale, int* error_word, nvk_stream_t stream) {
+  using namespace nvk;
+  int rc = check_common(out, query, batch, total_q, max_q_len, num_heads, num_kv_heads, head_dim, "dense_prefill");
+  if (rc != NVK_OK) return rc;
+  if (batch == 0 || total_q == 0 || max_q_len == 0) return NVK_OK;
+  if (total_kv <= 0 || !key || !value || !cu_seqlens_q || !cu_seqlens_kv)
+    return fail(NVK_ERR_INVALID_ARGUMENT, "dense_prefill: null pointer or no keys");
+  CUtensorMap qm, km, vm;
+  if ((rc = kv_tensor_map(&qm, query, total_q, num_heads, kRows)) != NVK_OK) return rc;
+  if ((rc = kv_tensor_map(&km, key, total_kv, num_kv_heads, kRows)) != NVK_OK) return rc;
+  if ((rc = kv_tensor_map(&vm, value, total_kv, num_kv_heads, kRows)) != NVK_OK) return rc;
+  PrefillArgs a{};
+  a.out = static_cast<__nv_bfloat16*>(out);
+  a.block_tables = nullptr;
+  a.cu_q = cu_seqlens_q;
+  a.kv_lens = nullptr;
+  a.cu_kv = cu_seqlens_kv;
+  a.err = error_word;
+  a.bt_stride = 0;
+  a.num_blocks = 0;
+  a.num_heads = num_heads;
+  a.qpk = num_heads / num_kv_heads;
+  a.paged = 0;
+  a.scale_log2 = scale * 1.4426950408889634f;
+  return launch_prefill(qm, km, vm, a, batch, max_q_len, reinterpret_cast<cudaStream_t>(stream));
 }
