@@ -68,18 +68,24 @@ WORKLOADS = {
                           describe="config[1]: Qwen3-0.6B decode step, 32 seqs, ctx~U[256,2304], CUDA graph bs 32"),
     "decode_c4": Workload("decode_c4", 28, 256, 16, 8, 2048, 6144, "strong",
                           describe="config[3]: Qwen3-0.6B decode step, 256 seqs, ctx~U[2048,6144], sequence-sharded"),
+    # prefill: ctx_lo = cached prefix tokens, ctx_hi = new tokens per request
+    "prefill_c3": Workload("prefill_c3", 28, 32, 16, 8, 768, 256, "weak",
+                           describe="config[2]: Qwen3-0.6B prefix-cache prefill, 32 requests x (768 cached + 256 new)"),
 }
 
 
 # --------------------------------------------------------------- helpers ----
-def peaks() -> tuple[float, str]:
+def peaks(key: str = "hbm_gbs") -> tuple[float, str]:
+    """Roofline denominators: measured copy bandwidth (GB/s) or bf16 GEMM
+    TFLOP/s from MEASURED_PEAKS.json, else this pool's earlier measurement."""
+    fallback = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
     p = ROOT / "MEASURED_PEAKS.json"
     if p.exists():
         try:
-            return float(json.loads(p.read_text())["hbm_gbs"]), "measured"
+            return float(json.loads(p.read_text())[key]), "measured"
         except Exception:
             pass
-    return 6650.0, "fallback"
+    return fallback[key], "fallback"
 
 
 def profiled_traffic(workload: str) -> float | None:
@@ -273,7 +279,7 @@ def kv_bytes_per_layer(ctx_after: list[int], kv_heads: int) -> int:
 
 
 # --------------------------------------------------------------- measure ----
-def time_decode_kernel(wl, md, kv, model, device, launches: int, seconds: float = 0.8) -> tuple[float, int]:
+def time_decode_kernel(wl, md, kv, model, device, launches: int, seconds: float = 0.8) -> float:
     """Average duration (s) of one nvk_paged_decode launch, cycling layers so
     that every launch reads a different 100+ MB slice of HBM."""
     from nano_vllm_ascend_b200 import ops
@@ -281,11 +287,7 @@ def time_decode_kernel(wl, md, kv, model, device, launches: int, seconds: float 
     b = model.q.shape[1]
     tables = md.block_tables.to(device)
     ctx = md.context_lens.to(device=device, dtype=torch.int32)
-    total = int(((md.context_lens.long() + BLOCK - 1) // BLOCK).sum())
-    bps = ops.choose_blocks_per_split(wl.kv_heads, tables.shape[1], total, b,
-                                      torch.cuda.get_device_properties(device).multi_processor_count)
-    splits = math.ceil(tables.shape[1] / bps)
-    ws = torch.zeros(ops.decode_workspace_bytes(b, wl.heads, wl.kv_heads, HEAD_DIM, splits), dtype=torch.uint8,
+    ws = torch.zeros(ops.decode_workspace_bytes(b, wl.heads, wl.kv_heads, HEAD_DIM), dtype=torch.uint8,
                      device=device)
     out = torch.empty_like(model.q[0])
     scale = HEAD_DIM ** -0.5
@@ -294,7 +296,7 @@ def time_decode_kernel(wl, md, kv, model, device, launches: int, seconds: float 
     def launch(i):
         layer = i % wl.layers
         kc, vc = kv.get_physical_cache(layer)
-        ops.paged_decode(out, model.q[layer], kc, vc, tables, ctx, scale, ws, bps, splits)
+        ops.paged_decode(out, model.q[layer], kc, vc, tables, ctx, scale, ws)
 
     for i in range(5):
         launch(i)
@@ -310,7 +312,9 @@ def time_decode_kernel(wl, md, kv, model, device, launches: int, seconds: float 
         per = start.elapsed_time(end) / 1e3 / launches
         if rep == 0:
             launches = max(launches, int(seconds / max(per, 1e-7)))
-    return per, bps
+    if ops.decode_error_word(ws) != 0:
+        raise RuntimeError(f"decode kernel error word {ops.decode_error_word(ws)}")
+    return per
 
 
 def time_append(kv, bm, device, rows: int, launches: int) -> float:
@@ -446,8 +450,8 @@ def run_ours(args, world, rank, local):
 
     with ClockSampler(local) as clocks:
         # dominant kernel alone (roofline)
-        t_dec, bps = time_decode_kernel(wl, md, kv, model, device, launches=max(56, 4 * wl.layers),
-                                        seconds=0.0 if args.quick else 0.8)
+        t_dec = time_decode_kernel(wl, md, kv, model, device, launches=max(56, 4 * wl.layers),
+                                   seconds=0.0 if args.quick else 0.8)
         t_app = time_append(kv, bm, device, rows=8192, launches=8 if args.quick else 56)
         # the step: W warm-up replays, then exactly K timed replays
         for _ in range(args.warmup):
@@ -537,7 +541,7 @@ def run_ours(args, world, rank, local):
                 "pool_blocks": num_blocks,
                 "parallelism": f"sequence-sharded x{world}, independent pools, no collective",
                 "cache": "inputs larger than L2: every step reads %.2f GB of KV" % (bytes_step / 1e9),
-                "blocks_per_split": bps,
+                "decode_grid": "persistent, one CTA per SM",
             },
             "tok_per_s": seqs_all / t_step_max,
             "hbm_frac_of_step": (bytes_all / t_step_max / 1e9) / (peak * world),
@@ -563,6 +567,211 @@ def run_ours(args, world, rank, local):
     return 0
 
 
+# ---------------------------------------------------------------- prefill ----
+def prefill_flops(q_lens: list[int], kv_lens: list[int], heads: int) -> float:
+    """4 * D * (visible (query, key) pairs), bottom-right causal."""
+    pairs = 0
+    for lq, lk in zip(q_lens, kv_lens):
+        pairs += lq * (lk - lq) + lq * (lq + 1) // 2
+    return 4.0 * HEAD_DIM * heads * pairs
+
+
+def build_prefill(wl: Workload, device, pool_blocks: int = 0):
+    """The config-3 state: a 768-token prefix cached by an earlier request
+    (6 full blocks, hashed by cache_full_blocks), then 32 requests that hit it
+    and prefill only their 256 new tokens."""
+    from nano_vllm_ascend_b200 import BatchPrefillAttention, BlockManager, PagedKVCache
+    from nano_vllm_ascend_b200.pool import num_blocks_from_memory
+
+    prefix_len, new_len, b = wl.ctx_lo, wl.ctx_hi, wl.batch
+    num_blocks = num_blocks_from_memory(wl.util, wl.layers, BLOCK, wl.kv_heads, HEAD_DIM, torch.bfloat16, device)
+    if pool_blocks > 0:
+        num_blocks = min(num_blocks, pool_blocks)
+    bm = BlockManager(num_blocks, BLOCK, device)
+    g = torch.Generator().manual_seed(42)
+    bm.free_block_ids = torch.randperm(num_blocks, generator=g).tolist()
+    prefix = torch.randint(0, 10000, (prefix_len,), generator=g)
+    seed_prompt = torch.cat([prefix, torch.randint(0, 10000, (1,), generator=g)])
+    bm.prepare_prefill_metadata([0], [prefix_len + 1], [0], [[]])
+    bm.cache_full_blocks(slot=0, token_ids=seed_prompt, num_cached_blocks=0, num_full_blocks=prefix_len // BLOCK)
+    kv = PagedKVCache(wl.layers, num_blocks, BLOCK, wl.kv_heads, HEAD_DIM, torch.bfloat16, device)
+    gen = torch.Generator(device=device).manual_seed(5)
+    used = torch.tensor(bm.block_tables[0], dtype=torch.int64, device=device)
+    for layer in range(wl.layers):
+        shape = (used.numel(), BLOCK, wl.kv_heads, HEAD_DIM)
+        kv.key_cache[layer].index_copy_(0, used, torch.randn(shape, generator=gen, device=device, dtype=torch.bfloat16))
+        kv.value_cache[layer].index_copy_(0, used,
+                                          torch.randn(shape, generator=gen, device=device, dtype=torch.bfloat16))
+    slots, hits, prompts = [], [], []
+    for r in range(b):
+        prompt = torch.cat([prefix, torch.randint(0, 10000, (new_len,), generator=g)])
+        hit = bm.find_longest_prefix_blocks(prompt, max_cache_blocks=(prefix_len + new_len) // BLOCK - 1)
+        assert len(hit) * BLOCK == prefix_len, "prefix must be hash-hit"
+        slots.append(r + 1)
+        hits.append(hit)
+        prompts.append(prompt)
+    md = bm.prepare_prefill_metadata(slots, [new_len] * b, [prefix_len] * b, hits)
+    assert md.use_paged_prefill
+    t = new_len * b
+    q = torch.randn(wl.layers, t, wl.heads, HEAD_DIM, generator=gen, device=device).to(torch.bfloat16)
+    k = torch.randn(wl.layers, t, wl.kv_heads, HEAD_DIM, generator=gen, device=device).to(torch.bfloat16)
+    v = torch.randn(wl.layers, t, wl.kv_heads, HEAD_DIM, generator=gen, device=device).to(torch.bfloat16)
+    attn = BatchPrefillAttention(wl.heads, wl.kv_heads, HEAD_DIM, BLOCK, max_mask_len=4096)
+    return bm, md, kv, attn, q, k, v, num_blocks
+
+
+def run_prefill_ours(args, world, rank, local):
+    from nano_vllm_ascend_b200 import ops
+
+    wl = WORKLOADS[args.workload]
+    device = torch.device("cuda", local)
+    bm, md, kv, attn, q, k, v, num_blocks = build_prefill(wl, device, args.pool_blocks)
+    b = wl.batch
+    q_lens, kv_lens = [wl.ctx_hi] * b, [wl.ctx_lo + wl.ctx_hi] * b
+    flops_layer = prefill_flops(q_lens, kv_lens, wl.heads)
+    stream = torch.cuda.current_stream(device)
+
+    def step():
+        for layer in range(wl.layers):
+            kv.write(layer, k[layer], v[layer], md.slot_mapping)
+            kc, vc = kv.get_physical_cache(layer)
+            attn(q[layer], k[layer], v[layer], md, kc, vc)
+
+    step()
+    torch.cuda.synchronize()
+    # dominant kernel alone: prefill attention, cycling layers
+    cu = torch.tensor([0] + list(range(wl.ctx_hi, wl.ctx_hi * b + 1, wl.ctx_hi)), dtype=torch.int32, device=device)
+    kvl = torch.tensor(kv_lens, dtype=torch.int32, device=device)
+    tables = md.block_tables.to(device)
+    out = torch.empty_like(q[0])
+
+    def pf(i):
+        layer = i % wl.layers
+        kc, vc = kv.get_physical_cache(layer)
+        ops.paged_prefill(out, q[layer], kc, vc, tables, cu, kvl, wl.ctx_hi, HEAD_DIM ** -0.5)
+
+    with ClockSampler(local) as clocks:
+        for i in range(3):
+            pf(i)
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        launches = 56
+        for rep in range(2):
+            start.record(stream)
+            for i in range(launches):
+                pf(i)
+            end.record(stream)
+            end.synchronize()
+            t_pf = start.elapsed_time(end) / 1e3 / launches
+            if rep == 0 and not args.quick:
+                launches = max(launches, int(0.8 / t_pf))
+        t_app = time_append(kv, bm, device, rows=8192, launches=8 if args.quick else 56)
+        for _ in range(args.warmup):
+            step()
+        barrier_sync(world)
+        start.record(stream)
+        for _ in range(args.steps):
+            step()
+        end.record(stream)
+        barrier_sync(world)
+        t_step = start.elapsed_time(end) / 1e3 / args.steps
+        # e2e: pinned host q/k/v in, attention outputs back
+        h_q, h_k, h_v = q.cpu().pin_memory(), k.cpu().pin_memory(), v.cpu().pin_memory()
+        h_out = torch.empty(q.shape, dtype=q.dtype).pin_memory()
+
+        def e2e_step():
+            q.copy_(h_q, non_blocking=True)
+            k.copy_(h_k, non_blocking=True)
+            v.copy_(h_v, non_blocking=True)
+            for layer in range(wl.layers):
+                kv.write(layer, k[layer], v[layer], md.slot_mapping)
+                kc, vc = kv.get_physical_cache(layer)
+                h_out[layer].copy_(attn(q[layer], k[layer], v[layer], md, kc, vc), non_blocking=True)
+
+        for _ in range(args.warmup):
+            e2e_step()
+        barrier_sync(world)
+        start.record(stream)
+        for _ in range(args.steps):
+            e2e_step()
+        end.record(stream)
+        barrier_sync(world)
+        t_e2e = start.elapsed_time(end) / 1e3 / args.steps
+    clk = clocks.summary()
+    t_step_max = max_over_ranks(t_step, world)
+    t_e2e_max = max_over_ranks(t_e2e, world)
+    flops_all = sum_over_ranks(flops_layer * wl.layers, world)
+    peak, kind = peaks("bf16_tflops")
+    achieved = flops_layer / t_pf / 1e12
+    h2d = sum(t.numel() * t.element_size() for t in (h_q, h_k, h_v))
+    if rank == 0:
+        cpu = None
+        if world == 1 and not args.no_cpu_baseline:
+            cpu = cpu_baseline_prefill(wl, args.cpu_seconds, os.cpu_count() or 1)
+        line = {
+            "metric": "prefix prefill attention TFLOP/s", "value": flops_all / t_step_max / 1e12, "unit": "TFLOP/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": t_step_max * 1e3,
+            "higher_is_better": True, "scaling": wl.scaling, "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic: seeded prompts sharing a 768-token prefix (hash-hit), seeded N(0,1) q/K/V",
+            "config": {"workload": wl.describe, "layers": wl.layers, "global_batch": b * world,
+                       "seq_len": wl.ctx_lo + wl.ctx_hi, "new_tokens": wl.ctx_hi, "cached_prefix": wl.ctx_lo,
+                       "heads": [wl.heads, wl.kv_heads, HEAD_DIM], "block_size": BLOCK, "pool_blocks": num_blocks,
+                       "parallelism": f"request-sharded x{world}, no collective",
+                       "cache": "per step 28 x (8192-row append + 60.16 GFLOP attention)"},
+            "tok_per_s": b * wl.ctx_hi * world / t_step_max,
+            "append": {"gbs": (8192 * wl.kv_heads * HEAD_DIM * 8 + 8192 * 8) / t_app / 1e9, "rows": 8192,
+                       "us": t_app * 1e6},
+            "roofline": {"kernel": "prefill_kernel", "bound": "tensor", "achieved": achieved, "peak": peak,
+                         "peak_kind": kind + " (burst, kernel timed alone)", "unit": "TFLOP/s",
+                         "frac": achieved / peak, "traffic": None, "algorithmic_flops_per_launch": flops_layer,
+                         "us_per_launch": t_pf * 1e6},
+            "e2e": {"value": flops_all / t_e2e_max / 1e12, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": h_out.numel() * h_out.element_size(), "ms_per_step": t_e2e_max * 1e3},
+            "clocks": clk, "gpu_launches": args.steps * wl.layers * 2, "cpu_baseline": cpu,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+def cpu_baseline_prefill(wl: Workload, seconds: float, threads: int, min_layers: int = 1) -> dict:
+    """Eager torch-CPU path for one config-3 layer (append + prefill over the
+    paged pool), repeated until ``seconds``; TFLOP/s of the attention."""
+    from oracle import cpu_baseline
+
+    torch.set_num_threads(threads)
+    g = torch.Generator().manual_seed(0)
+    b, lq, lk = wl.batch, wl.ctx_hi, wl.ctx_lo + wl.ctx_hi
+    nblk = lk // BLOCK
+    nb = 6 + b * (nblk - 6)
+    kc = torch.randn(nb, BLOCK, wl.kv_heads, HEAD_DIM, generator=g).to(torch.bfloat16)
+    vc = torch.randn(nb, BLOCK, wl.kv_heads, HEAD_DIM, generator=g).to(torch.bfloat16)
+    tables = torch.zeros(b, nblk, dtype=torch.int32)
+    tables[:, :6] = torch.arange(6, dtype=torch.int32)
+    tables[:, 6:] = (6 + torch.arange(b * (nblk - 6), dtype=torch.int32)).view(b, nblk - 6)
+    slots = torch.cat([torch.arange(int(t) * BLOCK, int(t) * BLOCK + BLOCK) for t in tables[:, 6:].flatten()])
+    q = torch.randn(b * lq, wl.heads, HEAD_DIM, generator=g).to(torch.bfloat16)
+    k = torch.randn(b * lq, wl.kv_heads, HEAD_DIM, generator=g).to(torch.bfloat16)
+    v = torch.randn(b * lq, wl.kv_heads, HEAD_DIM, generator=g).to(torch.bfloat16)
+    cu = list(range(0, b * lq + 1, lq))
+    flops = prefill_flops([lq] * b, [lk] * b, wl.heads)
+    n = 0
+    t0 = time.perf_counter()
+    while True:
+        cpu_baseline.append(kc, vc, k, v, slots)
+        cpu_baseline.prefill(q, kc, vc, tables, cu, [lk] * b, HEAD_DIM ** -0.5)
+        n += 1
+        el = time.perf_counter() - t0
+        if n >= min_layers and el >= seconds:
+            break
+    return {"value": flops * n / el / 1e12, "unit": "TFLOP/s", "cores": threads, "kind": "port",
+            "sample": f"{n} layer-steps (8192-row append + prefill attention of 32 x 256 queries over 1024 keys), "
+                      f"{el:.1f}s", "ms_per_layer": el / n * 1e3}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -580,8 +789,26 @@ def main():
         ap.error("--warmup must be >= 3")
     sys.path.insert(0, str(ROOT))
     world, rank, local = dist_setup(args)
+    prefill = args.workload.startswith("prefill")
     if args.impl == "reference":
+        if prefill:
+            if rank != 0:
+                return 0
+            wl = WORKLOADS[args.workload]
+            threads = os.cpu_count() or 1
+            cpu_baseline_prefill(wl, 0.0, threads, min_layers=max(1, args.warmup // 3))
+            r = cpu_baseline_prefill(wl, 0.0, threads, min_layers=args.steps)
+            print(json.dumps({"impl": "reference", "metric": "prefix prefill attention TFLOP/s", "value": r["value"],
+                              "unit": "TFLOP/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+                              "ms_per_step": r["ms_per_layer"] * wl.layers, "higher_is_better": True,
+                              "scaling": wl.scaling, "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+                              "config": {"workload": wl.describe, "parallelism": "host CPU"}, "cpu_baseline": r,
+                              "e2e": {"value": r["value"], "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
+                                      "d2h_bytes_per_step": 0}}), flush=True)
+            return 0
         return run_reference(args, world, rank)
+    if prefill:
+        return run_prefill_ours(args, world, rank, local)
     return run_ours(args, world, rank, local)
 
 

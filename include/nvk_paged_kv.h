@@ -57,7 +57,7 @@ enum {
 /* Message for the most recent non-zero return on the calling thread. */
 NVK_API const char* nvk_last_error(void);
 
-/* ABI version, bumped on any signature change. */
+/* ABI version, bumped on any signature change (2: persistent decode, num_ctas). */
 NVK_API int nvk_abi_version(void);
 
 /*
@@ -79,14 +79,15 @@ NVK_API int nvk_kv_append(const void* key, const void* value, int64_t key_token_
                   int64_t num_slots, int num_kv_heads, int head_dim, int* error_word, nvk_stream_t stream);
 
 /*
- * Bytes of split-K workspace nvk_paged_decode needs for `batch` sequences,
- * `num_kv_heads` KV heads, `num_heads` query heads and at most `max_splits`
- * context splits per sequence. The workspace must be zero-filled once before
- * its first use; the kernel returns its counters to zero after every call.
- * Calls that share one workspace must be ordered on one stream.
+ * Bytes of workspace nvk_paged_decode needs for `batch` sequences with
+ * `num_kv_heads` KV heads and `num_heads` query heads on `num_ctas` CTAs
+ * (0 = one per SM of the current device): an error word, one arrival ticket
+ * per (sequence, KV head) and two partial-result slots per CTA. Zero it once
+ * before first use; every call leaves the tickets at zero again. Calls that
+ * share one workspace must be ordered on one stream.
  */
-NVK_API int nvk_paged_decode_workspace_size(int batch, int num_heads, int num_kv_heads, int head_dim, int max_splits,
-                                    size_t* bytes);
+NVK_API int nvk_paged_decode_workspace_size(int batch, int num_heads, int num_kv_heads, int head_dim, int num_ctas,
+                                            size_t* bytes);
 
 /*
  * Paged GQA decode attention, one query token per sequence:
@@ -100,18 +101,16 @@ NVK_API int nvk_paged_decode_workspace_size(int batch, int num_heads, int num_kv
  *   first max_blocks_per_seq entries meaningful (zero padding is fine: only
  *   entries below ceil(context_lens[b] / block_size) are read).
  * context_lens: int32 [batch] in DEVICE memory (includes the token appended
- *   this step, as in the reference).
- * blocks_per_split: KV blocks one CTA walks; splits = ceil(blocks / this).
- * workspace: see nvk_paged_decode_workspace_size; max_splits must be at least
- *   ceil(max_blocks_per_seq / blocks_per_split).
+ *   this step, as in the reference); a length of 0 yields zeros.
+ * num_ctas: persistent grid size, 0 = one CTA per SM (the tuned default).
+ * workspace: see nvk_paged_decode_workspace_size (same batch/heads/num_ctas).
  * Supported: head_dim 128; num_heads / num_kv_heads in {1, 2, 4, 8};
  *   block_size a power of two in [16, 256].
  */
 NVK_API int nvk_paged_decode(void* out, const void* query, const void* key_cache, const void* value_cache, int num_blocks,
                      int block_size, const int32_t* block_tables, int block_table_stride, int max_blocks_per_seq,
                      const int32_t* context_lens, int batch, int num_heads, int num_kv_heads, int head_dim,
-                     float scale, int blocks_per_split, int max_splits, void* workspace, size_t workspace_bytes,
-                     nvk_stream_t stream);
+                     float scale, int num_ctas, void* workspace, size_t workspace_bytes, nvk_stream_t stream);
 
 /*
  * nvk_paged_decode without a caller workspace. No counterpart in the
@@ -120,7 +119,7 @@ NVK_API int nvk_paged_decode(void* out, const void* query, const void* key_cache
  * all device buffers, a cgo/JNI/N-API binding with no device allocator, a
  * serving thread that must not take cudaMalloc's implicit synchronisation).
  *
- * Same arguments and results as nvk_paged_decode. The split-K scratch is a
+ * Same arguments and results as nvk_paged_decode. The scratch is a
  * fixed 16 MiB array in the library's device memory, present on every GPU
  * that loads the library until the process exits; a call whose scratch need
  * (nvk_paged_decode_workspace_size) exceeds 16 MiB returns
@@ -135,7 +134,7 @@ NVK_API int nvk_paged_decode_noalloc(void* out, const void* query, const void* k
                                      int num_blocks, int block_size, const int32_t* block_tables,
                                      int block_table_stride, int max_blocks_per_seq, const int32_t* context_lens,
                                      int batch, int num_heads, int num_kv_heads, int head_dim, float scale,
-                                     int blocks_per_split, int max_splits, nvk_stream_t stream);
+                                     int num_ctas, nvk_stream_t stream);
 
 /*
  * Paged causal prefill attention (prefix-cache aware). Sequence b owns query

@@ -38,12 +38,12 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "nvk_paged_decode": (
         _i32,
         [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _i32, _i32, _c_void_p, _i32, _i32, _c_void_p, _i32, _i32, _i32,
-         _i32, _f32, _i32, _i32, _c_void_p, _size_t, _c_void_p],
+         _i32, _f32, _i32, _c_void_p, _size_t, _c_void_p],
     ),
     "nvk_paged_decode_noalloc": (
         _i32,
         [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _i32, _i32, _c_void_p, _i32, _i32, _c_void_p, _i32, _i32, _i32,
-         _i32, _f32, _i32, _i32, _c_void_p],
+         _i32, _f32, _i32, _c_void_p],
     ),
     "nvk_paged_prefill": (
         _i32,

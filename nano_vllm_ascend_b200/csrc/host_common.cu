@@ -36,9 +36,10 @@ struct MapKey {
   int mid;
   int box_rows;
   int64_t row_stride;
+  int box_mid;
   bool operator==(const MapKey& o) const {
     return base == o.base && rows == o.rows && mid == o.mid && box_rows == o.box_rows &&
-           row_stride == o.row_stride;
+           row_stride == o.row_stride && box_mid == o.box_mid;
   }
 };
 
@@ -56,7 +57,7 @@ std::mutex g_cache_mu;
 size_t hash_key(const MapKey& k) {
   uint64_t h = reinterpret_cast<uintptr_t>(k.base) * 0x9E3779B97F4A7C15ull;
   h ^= static_cast<uint64_t>(k.rows) + 0x632BE59BD9B4E019ull + (h << 6) + (h >> 2);
-  h ^= static_cast<uint64_t>(k.mid * 131 + k.box_rows) + (h << 6) + (h >> 2);
+  h ^= static_cast<uint64_t>(k.mid * 131 + k.box_rows * 7 + k.box_mid) + (h << 6) + (h >> 2);
   h ^= static_cast<uint64_t>(k.row_stride) + (h << 6) + (h >> 2);
   return static_cast<size_t>(h % kCacheSlots);
 }
@@ -77,9 +78,9 @@ int check_cuda(cudaError_t err, const char* what) {
 }
 
 int kv_tensor_map(CUtensorMap* out, const void* base, int64_t rows, int mid, int box_rows,
-                  int64_t row_stride_elems) {
+                  int64_t row_stride_elems, int box_mid) {
   if (row_stride_elems <= 0) row_stride_elems = static_cast<int64_t>(mid) * 128;
-  const MapKey key{base, rows, mid, box_rows, row_stride_elems};
+  const MapKey key{base, rows, mid, box_rows, row_stride_elems, box_mid};
   const size_t slot = hash_key(key);
   {
     std::lock_guard<std::mutex> lock(g_cache_mu);
@@ -98,7 +99,10 @@ int kv_tensor_map(CUtensorMap* out, const void* base, int64_t rows, int mid, int
                 (long long)row_stride_elems);
   const cuuint64_t dims[3] = {128, static_cast<cuuint64_t>(mid), static_cast<cuuint64_t>(rows)};
   const cuuint64_t strides[2] = {128 * 2, static_cast<cuuint64_t>(row_stride_elems) * 2};
-  const cuuint32_t box[3] = {64, 1, static_cast<cuuint32_t>(box_rows)};
+  if (box_mid < 1 || box_mid > mid || box_rows < 1 || box_rows > 256)
+    return fail(NVK_ERR_INVALID_ARGUMENT, "tensor map box {64, %d, %d} outside {%d, %lld}", box_mid, box_rows, mid,
+                (long long)rows);
+  const cuuint32_t box[3] = {64, static_cast<cuuint32_t>(box_mid), static_cast<cuuint32_t>(box_rows)};
   const cuuint32_t estride[3] = {1, 1, 1};
   CUtensorMap map;
   CUresult r = fn(&map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, estride,
@@ -140,4 +144,4 @@ int ensure_dynamic_smem(const void* kernel, size_t bytes) {
 
 extern "C" const char* nvk_last_error(void) { return nvk::g_last_error; }
 
-extern "C" int nvk_abi_version(void) { return 1; }
+extern "C" int nvk_abi_version(void) { return 2; }

@@ -34,6 +34,8 @@ __global__ void __launch_bounds__(kAppendThreads) kv_append_kernel(
     const uint4* __restrict__ key, const uint4* __restrict__ value, int64_t key_stride_w, int64_t value_stride_w,
     uint4* __restrict__ key_cache, uint4* __restrict__ value_cache, const int64_t* __restrict__ slots,
     int64_t num_tokens, int64_t num_slots, int words_per_row, int* __restrict__ error_word) {
+  pdl_launch_dependents();
+  pdl_wait();
   const int64_t total = num_tokens * words_per_row;
   const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
   for (int64_t base = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; base < total;
@@ -97,9 +99,11 @@ extern "C" int nvk_kv_append(const void* key, const void* value, int64_t key_tok
   if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   const int64_t want = (total + int64_t(kAppendThreads) * kAppendUnroll - 1) / (int64_t(kAppendThreads) * kAppendUnroll);
   const int blocks = static_cast<int>(want < int64_t(sms) * 8 ? (want > 0 ? want : 1) : int64_t(sms) * 8);
-  kv_append_kernel<<<blocks, kAppendThreads, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
-      static_cast<const uint4*>(key), static_cast<const uint4*>(value), key_token_stride * 2 / 16,
-      value_token_stride * 2 / 16, static_cast<uint4*>(key_cache), static_cast<uint4*>(value_cache), slot_mapping,
-      num_tokens, num_slots, words_per_row, error_word);
-  return check_cuda(cudaGetLastError(), "kv_append launch");
+  const cudaError_t e = launch_pdl(kv_append_kernel, dim3(blocks), dim3(kAppendThreads), 0,
+                                   reinterpret_cast<cudaStream_t>(stream), static_cast<const uint4*>(key),
+                                   static_cast<const uint4*>(value), key_token_stride * 2 / 16,
+                                   value_token_stride * 2 / 16, static_cast<uint4*>(key_cache),
+                                   static_cast<uint4*>(value_cache), slot_mapping, num_tokens, num_slots,
+                                   words_per_row, error_word);
+  return check_cuda(e, "kv_append launch");
 }

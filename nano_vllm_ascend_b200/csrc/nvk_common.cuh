@@ -126,4 +126,13 @@ __device__ __forceinline__ void named_barrier_sync(int id, int nthreads) {
 
 __host__ __device__ constexpr int ceil_div(int a, int b) { return (a + b - 1) / b; }
 
+// Programmatic dependent launch. A kernel launched with programmatic stream
+// serialisation may start while its predecessor in the stream is still
+// running: it must call pdl_wait() before touching global memory the
+// predecessor writes (the wait returns once the predecessor has completed and
+// its writes are visible; without such a launch it returns at once).
+// pdl_launch_dependents() lets the successor be scheduled early.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 }  // namespace nvk

@@ -1,4 +1,5 @@
-// Paged GQA decode attention (one query token per sequence).
+// Paged GQA decode attention (one query token per sequence) on the sm_100a
+// tensor cores, as a persistent, continuously streaming kernel.
 //
 // Replaces torch_npu._npu_paged_attention as called from
 // src/nanovllm_ascend/layers/npu_paged_attention.py:58,89 (and the graph
@@ -6,55 +7,72 @@
 //   out[b,h] = softmax(scale * q[b,h] . K[b,:,g(h)]^T) . V[b,:,g(h)]
 // over the first context_lens[b] tokens reached through block_tables[b].
 //
-// B200 design (HBM-bound: every KV byte is read exactly once):
-//  * grid = (split, kv_head, seq). A CTA owns one KV head of one sequence over
-//    `blocks_per_split` pool blocks and serves ALL query heads of that GQA
-//    group from the same KV read.
-//  * warp 4 = producer: stages the split's block ids in shared memory, then
-//    one lane streams 64-token stages of K and V (two 64-dim halves each) with
-//    3-D TMA tile loads (box {64 dims, 1 head, <=32 tokens}, 128-byte swizzle)
-//    into a STAGES-deep ring guarded by full/empty mbarriers.
-//  * warps 0-3 = consumers: each owns 16 tokens of a stage. LPT = 2*QPK lanes
-//    share a token, each holding 64/QPK dims of every query head of the group
-//    in registers (q pre-scaled by scale*log2 e), so q and the f32
-//    accumulators take 64 registers each whatever the GQA ratio. The lane ->
-//    (token, 16-byte chunk) map is chosen against the 128-byte swizzle so that
-//    every quarter-warp of a 128-bit shared load hits 8 distinct bank groups.
-//  * online softmax in base 2 with lazy rescaling (the running max only moves
-//    when a tile max exceeds it by more than 2^8), per warp; warps merge once
-//    at the end through shared memory.
-//  * split-K without a second launch: every split writes (m, l, o) partials;
-//    the last CTA of a (seq, kv_head) to arrive (atomic ticket) merges them and
-//    resets the ticket, so the workspace is reusable and graph-capturable.
+// HBM-bound: every KV byte is read once. Design:
+//  * work = 128-token tiles of every (sequence, KV head) pair, linearised
+//    sequence-major. The grid is persistent (one CTA per SM); CTA c takes the
+//    contiguous range [c*T/C, (c+1)*T/C) of the T tiles, so loads stream
+//    without per-CTA fill/drain and the load balance is within one tile.
+//    A range holds whole pairs ("segments") plus at most a partial pair at
+//    each end; a pair split across CTAs is merged by the CTA that finishes
+//    its piece last (atomic ticket), from two partial slots per CTA.
+//  * warp 4 (producer): per segment a TMA load of the group's QPK query rows
+//    into a zero-padded 16-row operand; per tile, TMA loads of the K and V
+//    tile (box {64 dims, 1 head, <=32 tokens}, 128-byte swizzle, only the
+//    sub-boxes that hold context tokens) into a 3-stage ring.
+//  * warp 5 (MMA): S^T[128 tok x 16] = K[128 x 128] . Qpad^T (A and B
+//    K-major) and O^T[128 dims x 16] += V^T . P^T (A = the V tile read
+//    MN-major, B = P^T K-major): M=128 N=16 K=16 UMMAs with f32 accumulators
+//    in TMEM (S double buffered, O and the query operand four deep, so short
+//    segments do not wait on each other), completion via tcgen05.commit.
+//  * warps 0-3 (softmax): thread t owns token t of S^T (and dim t of O^T).
+//    Base-2 online softmax per query head with lazy rescaling (the reference
+//    max moves only when a tile max exceeds it by more than 2^8); the tile
+//    max is exchanged across the 4 warps once per tile; P^T goes to shared
+//    memory as bf16; l is summed once per segment.
+// Every mbarrier wait is bounded (%globaltimer); a timeout sets the error
+// word, the CTA drains its copies and MMAs, frees TMEM and exits.
 #include <cfloat>
 #include <mutex>
 
 #include "host_common.h"
 #include "nvk_common.cuh"
+#include "tcgen05.cuh"
 
 namespace nvk {
 namespace {
 
 constexpr int kD = 128;
-constexpr int kTile = 64;  // tokens per pipeline stage
-constexpr int kConsumerWarps = 4;
-constexpr int kThreads = (kConsumerWarps + 1) * 32;
-constexpr int kHalfBytes = kTile * 128;        // 64 tokens x 64 dims x bf16
-constexpr int kStageBytes = 4 * kHalfBytes;    // K lo, K hi, V lo, V hi
-constexpr int kTokPerWarp = kTile / kConsumerWarps;
-constexpr int kMaxSplitBlocks = 256;
+constexpr int kTile = 128;          // tokens per tile
+constexpr int kHalf = kTile * 128;  // one 64-dim half of a K or V tile
+constexpr int kKV = 2 * kHalf;      // one K (or V) tile
 constexpr int kStages = 3;
+constexpr int kN = 16;              // UMMA N: the GQA group, zero padded
+constexpr int kQHalf = kN * 128;    // 16 rows x 64 dims
+constexpr int kQBytes = 2 * kQHalf;
+constexpr int kMaxSeqs = 1024;      // sequences per launch (tile prefix in smem)
+constexpr int kSoftmaxThreads = 128;
+constexpr int kProducerWarp = 4;
+constexpr int kMmaWarp = 5;
+constexpr int kEpilogueWarp0 = 6;           // warps 6-9: one per TMEM lane quarter
+constexpr int kEpilogueThreads = 128;
+constexpr int kThreads = 10 * 32;
+constexpr int kQBufs = 4;           // query operands in flight (one per segment)
+constexpr int kOBufs = 4;           // O accumulators in flight (one per segment)
+constexpr uint32_t kTmemCols = 128; // S: 0-31 (2 x 16), O: 32-95 (4 x 16)
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
+constexpr int kChunkTiles = 32;            // tiles whose block ids the producer stages at once
+constexpr int kMaxMergePieces = 32;        // pieces staged per merge pass
+constexpr int kTicketStride = 32;          // ints: one 128-byte line per ticket (no shared lines)
 
 struct DecodeArgs {
   __nv_bfloat16* out;
-  const __nv_bfloat16* q;
   const int32_t* block_tables;
   const int32_t* context_lens;
-  float* ws_o;
-  float2* ws_ml;
-  int* ws_cnt;
+  float* ws_o;    // [C][2][QPK][kD] partial numerators
+  float2* ws_ml;  // [C][2][QPK] partial (reference max, denominator)
+  int* ws_cnt;    // [batch * KVH] arrival tickets, back at zero after every call
   int* err;
+  int batch;
   int bt_stride;
   int max_blocks;
   int num_blocks;
@@ -63,396 +81,870 @@ struct DecodeArgs {
   int sub_rows;
   int num_heads;
   int num_kv_heads;
-  int blocks_per_split;
-  int max_splits;
+  int qpk;
   float scale_log2;
 };
 
-template <int QPK>
-struct Layout {
-  static constexpr int kLPT = 2 * QPK;         // lanes per token
-  static constexpr int kDPL = kD / kLPT;       // dims per lane
-  static constexpr int kNCH = kDPL / 8;        // 16-byte chunks per lane
-  static constexpr int kTPP = 32 / kLPT;       // tokens per warp pass
-  static constexpr int kNP = kTokPerWarp / kTPP;  // passes per stage
-  static_assert(kNCH >= 1 && kNP >= 1, "bad GQA ratio");
-};
-
-template <int QPK>
 struct Smem {
-  alignas(1024) uint8_t stage[kStages][kStageBytes];
-  uint64_t full[kStages];
-  uint64_t empty[kStages];
-  int blocks[kMaxSplitBlocks];
-  float red_m[kConsumerWarps][QPK];
-  float red_l[kConsumerWarps][QPK];
-  float red_o[kConsumerWarps][QPK][kD];
-  int last;
+  alignas(1024) uint8_t k[kStages][kKV];
+  alignas(1024) uint8_t v[kStages][kKV];
+  alignas(1024) uint8_t q[kQBufs][kQBytes];
+  alignas(1024) uint8_t p[2][kQBytes];
+  int tiles_before[kMaxSeqs + 1];
+  uint8_t last_rows[kMaxSeqs];           // context tokens in each sequence's last tile (1..128)
+  int blocks[kChunkTiles * kTile / 16];  // block ids of up to kChunkTiles tiles
+  float red[2][4][8];
+  int warp_ok[2][4];
+  int resc_ok[4];  // rescale-path exchange (its own slot: warp_ok[] belongs to the tile)
+  uint64_t full_k[kStages], full_v[kStages], kv_empty[kStages];
+  uint64_t q_full[kQBufs], q_empty[kQBufs];
+  uint64_t s_full[2], s_free[2], p_full[2], pv_done[2];
+  uint64_t o_full[kOBufs], o_empty[kOBufs];
+  uint64_t fin;
+  uint32_t tmem_base;
+  int total_tiles;
+  // softmax -> epilogue hand-off, one per O buffer
+  struct SegInfo {
+    int b, g, n, ntiles, pair_t0, slot;
+    float m[8];
+    float l_part[4][8];
+  } seg_info[kOBufs];
+  uint64_t seg_ready[kOBufs];
+  int last[2];
+  int pend_pair[2], pend_t0[2], pend_n[2], pend_b[2], pend_g[2];  // partial pieces, published at the end
+  int pieces[kMaxMergePieces];
+  int npieces;
+  float2 mml[kMaxMergePieces * 8];          // (m, l) of the pieces being merged
+  int epi_ok[4];
+  volatile int abort;
 };
 
-// Two CTAs per SM while q + accumulators fit (QPK <= 2); one above that.
-template <int QPK>
-__global__ void __launch_bounds__(kThreads, (QPK <= 2) ? 2 : 1) paged_decode_kernel(const __grid_constant__ CUtensorMap kmap,
-                                                                   const __grid_constant__ CUtensorMap vmap,
-                                                                   const DecodeArgs a) {
-  using Lay = Layout<QPK>;
-  constexpr int LPT = Lay::kLPT, DPL = Lay::kDPL, NCH = Lay::kNCH, TPP = Lay::kTPP, NP = Lay::kNP;
+__device__ __forceinline__ int seq_tiles(int len) { return (len + kTile - 1) / kTile; }
 
-  const int split = blockIdx.x, g = blockIdx.y, b = blockIdx.z;
-  int L = a.context_lens[b];
-  if (L < 0) L = 0;
-  if (L > a.max_blocks * a.block_size) {
-    if (threadIdx.x == 0 && split == 0) atomicOr(a.err, kErrContextTooLong);
-    L = a.max_blocks * a.block_size;
+// Sequence whose pairs hold linear tile t: the largest b with
+// kvh * tiles_before[b] <= t (this skips sequences without tiles).
+__device__ __forceinline__ int find_seq(const Smem& sm, int batch, int kvh, int t) {
+  int lo = 0, hi = batch - 1;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (kvh * sm.tiles_before[mid] <= t) lo = mid;
+    else hi = mid - 1;
   }
-  const int nblk = (L + a.block_size - 1) >> a.log2_bs;
-  int nsplit = (nblk + a.blocks_per_split - 1) / a.blocks_per_split;
-  if (nsplit < 1) nsplit = 1;
-  if (split >= nsplit) return;  // uniform over the CTA
+  return lo;
+}
 
-  extern __shared__ uint8_t smem_raw[];
-  Smem<QPK>& sm = *reinterpret_cast<Smem<QPK>*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+// The T tiles of a launch split into C contiguous ranges: CTA c gets
+// q = T / C tiles, plus one more if c < r = T % C. Range starts and owners are
+// then multiplications and one 32-bit divide by a per-launch constant (no
+// 64-bit divisions on the critical path), and empty ranges (T < C) all sit at
+// the end, so the CTAs holding pieces of one pair are contiguous.
+struct Sched {
+  int total, ctas, q, r, big;  // big = r * (q + 1): tiles held by the longer ranges
+};
 
-  const int split_blk0 = split * a.blocks_per_split;
-  const int split_nblk = min(a.blocks_per_split, nblk - split_blk0);
-  const int tok_begin = split_blk0 * a.block_size;
-  const int tok_end = min(L, tok_begin + a.blocks_per_split * a.block_size);
-  const int ntiles = tok_end > tok_begin ? (tok_end - tok_begin + kTile - 1) / kTile : 0;
+__device__ __forceinline__ Sched make_sched(int total, int ctas) {
+  Sched sc;
+  sc.total = total;
+  sc.ctas = ctas;
+  sc.q = total / ctas;
+  sc.r = total - sc.q * ctas;
+  sc.big = sc.r * (sc.q + 1);
+  return sc;
+}
 
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  if (threadIdx.x == 0) {
-    for (int s = 0; s < kStages; ++s) {
-      mbar_init(&sm.full[s], 1);
-      mbar_init(&sm.empty[s], kConsumerWarps);
+__device__ __forceinline__ int range_lo(int c, const Sched& sc) { return c * sc.q + min(c, sc.r); }
+
+// CTA whose range holds linear tile t.
+__device__ __forceinline__ int cta_of(int t, const Sched& sc) {
+  return t < sc.big ? t / (sc.q + 1) : sc.r + (t - sc.big) / max(sc.q, 1);  // q >= 1 whenever t >= big
+}
+
+// Partial slot of CTA cc for a pair starting at pair_t0: 0 when the pair is
+// the first segment of cc's range (the range starts inside the pair), else 1.
+__device__ __forceinline__ int64_t part_index(int cc, int pair_t0, const Sched& sc, int qpk) {
+  const int slot = (range_lo(cc, sc) >= pair_t0) ? 0 : 1;
+  return (static_cast<int64_t>(cc) * 2 + slot) * qpk;
+}
+
+// One contiguous run of tiles of one (sequence, KV head) pair inside this CTA.
+struct Segment {
+  int b, g, len, i0, n, ntiles, pair_t0, start;
+};
+
+__device__ __forceinline__ Segment next_segment(const Smem& sm, const DecodeArgs& a, int t, int hi) {
+  Segment s;
+  s.b = find_seq(sm, a.batch, a.num_kv_heads, t);
+  s.n = sm.tiles_before[s.b + 1] - sm.tiles_before[s.b];
+  const int off = t - a.num_kv_heads * sm.tiles_before[s.b];
+  s.g = off / s.n;
+  s.i0 = off - s.g * s.n;
+  s.ntiles = min(hi - t, s.n - s.i0);
+  s.pair_t0 = t - s.i0;
+  s.start = t;
+  s.len = (s.n - 1) * kTile + sm.last_rows[s.b];  // a segment exists only when s.n >= 1
+  return s;
+}
+
+// Order in which a CTA walks its range [lo, hi): first the (at most two)
+// partial segments -- pieces of pairs shared with the neighbouring CTAs --
+// then the whole pairs. Both pieces of every split pair are thus finished
+// early in every CTA, and their merge overlaps the streaming of whole pairs
+// instead of trailing the kernel. Every role follows the same order.
+struct SegIter {
+  // Up to three sub-ranges, kept in named registers (no dynamically indexed
+  // local array: after an acquire at GPU scope local memory may miss L1).
+  int lo0, hi0, lo1, hi1, lo2, hi2, nr, ri, t, npartial;
+
+  __device__ __forceinline__ void init(const Smem& sm, const DecodeArgs& a, int lo, int hi) {
+    nr = 0;
+    ri = 0;
+    npartial = 0;
+    lo0 = hi0 = lo1 = hi1 = lo2 = hi2 = 0;
+    t = lo;
+    if (lo >= hi) return;
+    const Segment f = next_segment(sm, a, lo, hi);
+    const int e0 = lo + f.ntiles;
+    if (e0 >= hi) {  // a single segment
+      lo0 = lo;
+      hi0 = hi;
+      nr = 1;
+      npartial = (f.ntiles != f.n) ? 1 : 0;
+      return;
     }
+    const Segment l = next_segment(sm, a, hi - 1, hi);
+    const int s1 = max(e0, l.pair_t0);  // start of the last segment
+    const bool f_part = f.ntiles != f.n;
+    const bool l_part = (hi - s1) != l.n;
+    const int m0 = f_part ? e0 : lo, m1 = l_part ? s1 : hi;
+    if (f_part) push(lo, e0), ++npartial;
+    if (l_part) push(s1, hi), ++npartial;
+    if (m0 < m1) push(m0, m1);
+    t = lo0;
+  }
+
+  __device__ __forceinline__ void push(int x, int y) {
+    if (nr == 0) lo0 = x, hi0 = y;
+    else if (nr == 1) lo1 = x, hi1 = y;
+    else lo2 = x, hi2 = y;
+    ++nr;
+  }
+  __device__ __forceinline__ int cur_hi() const { return ri == 0 ? hi0 : (ri == 1 ? hi1 : hi2); }
+  __device__ __forceinline__ int cur_lo() const { return ri == 0 ? lo0 : (ri == 1 ? lo1 : lo2); }
+
+  __device__ __forceinline__ bool next(const Smem& sm, const DecodeArgs& a, Segment& s) {
+    while (ri < nr && t >= cur_hi()) {
+      ++ri;
+      if (ri < nr) t = cur_lo();
+    }
+    if (ri >= nr) return false;
+    s = next_segment(sm, a, t, cur_hi());
+    t += s.ntiles;
+    return true;
+  }
+};
+
+__device__ __forceinline__ void flag_error(const DecodeArgs& a, Smem& sm, int code) {
+  atomicOr(a.err, code);
+  sm.abort = 1;
+}
+
+// QPK consecutive 32-bit TMEM columns of this thread's lane (warp-collective).
+__device__ __forceinline__ void tmem_ld_cols(uint32_t taddr, int qpk, float (&v)[8]) {
+  uint32_t r[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+  if (qpk == 1) {
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x1.b32 {%0}, [%1];" : "=r"(r[0]) : "r"(taddr));
+  } else if (qpk == 2) {
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x2.b32 {%0, %1}, [%2];" : "=r"(r[0]), "=r"(r[1]) : "r"(taddr));
+  } else if (qpk == 4) {
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x4.b32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(taddr));
+  } else {
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+                   "=r"(r[7])
+                 : "r"(taddr));
+  }
+  tmem_ld_wait();
+#pragma unroll
+  for (int h = 0; h < 8; ++h) v[h] = __uint_as_float(r[h]);
+}
+
+__device__ __forceinline__ void tmem_st_cols(uint32_t taddr, int qpk, const float (&v)[8]) {
+  uint32_t r[8];
+#pragma unroll
+  for (int h = 0; h < 8; ++h) r[h] = __float_as_uint(v[h]);
+  if (qpk == 1) {
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x1.b32 [%0], {%1};" ::"r"(taddr), "r"(r[0]) : "memory");
+  } else if (qpk == 2) {
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x2.b32 [%0], {%1, %2};" ::"r"(taddr), "r"(r[0]), "r"(r[1])
+                 : "memory");
+  } else if (qpk == 4) {
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x4.b32 [%0], {%1, %2, %3, %4};" ::"r"(taddr), "r"(r[0]),
+                 "r"(r[1]), "r"(r[2]), "r"(r[3])
+                 : "memory");
+  } else {
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"r"(taddr),
+                 "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7])
+                 : "memory");
+  }
+  tmem_st_wait();
+}
+
+constexpr int kFastPieces = 4;  // pieces per pair merged with one round of loads
+
+// Publishes this CTA's partial pieces (one acq_rel ticket each, both in
+// flight together) and merges every pair whose last piece this CTA holds.
+// A merge with up to kFastPieces pieces issues every (m, l) and value load
+// of both pairs at once: two global round trips in all. Called by the 128
+// epilogue threads right after the partial segments.
+template <int QPK>
+__device__ __forceinline__ void publish_and_merge(Smem& sm, const DecodeArgs& a, int c, const Sched& sc, int e,
+                                                  int d, bool all_ok) {
+  if (!all_ok) {
+    if (e == 0) flag_error(a, sm, kErrWaitTimeout);
+    return;
+  }
+  if (e < 2) {
+    int last = 0;
+    if (sm.pend_n[e] > 0) {
+      const int c_first = cta_of(sm.pend_t0[e], sc);
+      const int c_last = cta_of(sm.pend_t0[e] + sm.pend_n[e] - 1, sc);
+      const int pieces = c_last - c_first + 1;  // ranges holding tiles are contiguous
+      int old;
+      // release this CTA's stores, acquire the other pieces'
+      asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], 1;" : "=r"(old) : "l"(a.ws_cnt + static_cast<int64_t>(sm.pend_pair[e]) * kTicketStride) : "memory");
+      last = (old == pieces - 1);
+    }
+    sm.last[e] = last;
+  }
+  named_barrier_sync(2, kEpilogueThreads);
+
+  // Fast path: pieces are the contiguous CTAs c_first .. c_last of the pair.
+  int cf[2], np[2];
+  bool slow[2];
+#pragma unroll
+  for (int k = 0; k < 2; ++k) {
+    cf[k] = 0;
+    np[k] = 0;
+    if (sm.last[k]) {
+      const int pair_t0 = sm.pend_t0[k];
+      cf[k] = cta_of(pair_t0, sc);
+      np[k] = cta_of(pair_t0 + sm.pend_n[k] - 1, sc) - cf[k] + 1;
+    }
+    slow[k] = np[k] > kFastPieces;
+  }
+  float2 mlv[2][kFastPieces][QPK];
+  float ov[2][kFastPieces][QPK];
+#pragma unroll
+  for (int k = 0; k < 2; ++k) {
+#pragma unroll
+    for (int u = 0; u < kFastPieces; ++u) {
+#pragma unroll
+      for (int h = 0; h < QPK; ++h) {
+        const bool use = !slow[k] && u < np[k];
+        const int64_t pp = use ? part_index(cf[k] + u, sm.pend_t0[k], sc, QPK) + h : 0;
+        mlv[k][u][h] = use ? __ldcg(&a.ws_ml[pp]) : make_float2(-INFINITY, 0.f);
+        ov[k][u][h] = use ? __ldcg(&a.ws_o[pp * kD + d]) : 0.f;
+      }
+    }
+  }
+#pragma unroll
+  for (int k = 0; k < 2; ++k) {
+    if (!sm.last[k] || slow[k]) continue;
+    __nv_bfloat16* out = a.out + (static_cast<int64_t>(sm.pend_b[k]) * a.num_heads + sm.pend_g[k] * QPK) * kD;
+#pragma unroll
+    for (int h = 0; h < QPK; ++h) {
+      float M = -INFINITY;
+#pragma unroll
+      for (int u = 0; u < kFastPieces; ++u) M = fmaxf(M, mlv[k][u][h].x);
+      float num = 0.f, den = 0.f;
+      if (M != -INFINITY) {
+#pragma unroll
+        for (int u = 0; u < kFastPieces; ++u) {
+          if (mlv[k][u][h].x == -INFINITY) continue;
+          const float w = fast_exp2(mlv[k][u][h].x - M);
+          num = fmaf(w, ov[k][u][h], num);
+          den = fmaf(w, mlv[k][u][h].y, den);
+        }
+      }
+      out[h * kD + d] = __float2bfloat16_rn(den > 0.f ? num / den : 0.f);
+    }
+    if (e == 0) a.ws_cnt[static_cast<int64_t>(sm.pend_pair[k]) * kTicketStride] = 0;
+  }
+
+  // Slow path (a pair split over more than kFastPieces CTAs): staged passes.
+  for (int k = 0; k < 2; ++k) {
+    if (!sm.last[k] || !slow[k]) continue;
+    const int pair_t0 = sm.pend_t0[k], pn = sm.pend_n[k];
+    const int c_first = cta_of(pair_t0, sc);
+    const int c_last = cta_of(pair_t0 + pn - 1, sc);
+    float num[QPK], den[QPK], M[QPK];
+#pragma unroll
+    for (int h = 0; h < QPK; ++h) {
+      num[h] = 0.f;
+      den[h] = 0.f;
+      M[h] = -INFINITY;
+    }
+    for (int c0 = c_first; c0 <= c_last; c0 += kMaxMergePieces) {
+      if (e == 0) {
+        int n = 0;
+        for (int cc = c0; cc <= min(c_last, c0 + kMaxMergePieces - 1); ++cc) sm.pieces[n++] = cc;
+        sm.npieces = n;
+      }
+      named_barrier_sync(2, kEpilogueThreads);
+      const int n = sm.npieces;
+      for (int r = e; r < n * QPK; r += kEpilogueThreads)
+        sm.mml[r] = __ldcg(&a.ws_ml[part_index(sm.pieces[r / QPK], pair_t0, sc, QPK) + (r % QPK)]);
+      named_barrier_sync(2, kEpilogueThreads);
+#pragma unroll
+      for (int h = 0; h < QPK; ++h) {
+        float mg = M[h];
+        for (int p = 0; p < n; ++p) mg = fmaxf(mg, sm.mml[p * QPK + h].x);
+        const float s_old = (M[h] == -INFINITY) ? 0.f : fast_exp2(M[h] - mg);
+        num[h] *= s_old;
+        den[h] *= s_old;
+        M[h] = mg;
+        for (int p = 0; p < n; ++p) {
+          const float2 ml = sm.mml[p * QPK + h];
+          if (ml.x == -INFINITY) continue;
+          const float w = fast_exp2(ml.x - mg);
+          num[h] = fmaf(w, __ldcg(&a.ws_o[(part_index(sm.pieces[p], pair_t0, sc, QPK) + h) * kD + d]), num[h]);
+          den[h] = fmaf(w, ml.y, den[h]);
+        }
+      }
+      named_barrier_sync(2, kEpilogueThreads);  // staging is rewritten by the next group
+    }
+    __nv_bfloat16* out = a.out + (static_cast<int64_t>(sm.pend_b[k]) * a.num_heads + sm.pend_g[k] * QPK) * kD;
+#pragma unroll
+    for (int h = 0; h < QPK; ++h) out[h * kD + d] = __float2bfloat16_rn(den[h] > 0.f ? num[h] / den[h] : 0.f);
+    if (e == 0) a.ws_cnt[static_cast<int64_t>(sm.pend_pair[k]) * kTicketStride] = 0;
+  }
+}
+
+template <int QPK>
+__global__ void __launch_bounds__(kThreads, 1) paged_decode_kernel(const __grid_constant__ CUtensorMap kmap,
+                                                                   const __grid_constant__ CUtensorMap vmap,
+                                                                   const __grid_constant__ CUtensorMap qmap,
+                                                                   const DecodeArgs a) {
+  extern __shared__ uint8_t smem_raw[];
+  Smem& sm = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int c = blockIdx.x, ctas = gridDim.x;
+  const int kvh = a.num_kv_heads;
+
+  if (tid == 32) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&sm.full_k[s], 1);
+      mbar_init(&sm.full_v[s], 1);
+      mbar_init(&sm.kv_empty[s], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&sm.s_full[i], 1);
+      mbar_init(&sm.s_free[i], kSoftmaxThreads);
+      mbar_init(&sm.p_full[i], kSoftmaxThreads);
+      mbar_init(&sm.pv_done[i], 1);
+    }
+    for (int i = 0; i < kQBufs; ++i) {
+      mbar_init(&sm.q_full[i], 1);
+      mbar_init(&sm.q_empty[i], 1);
+    }
+    for (int i = 0; i < kOBufs; ++i) {
+      mbar_init(&sm.o_full[i], 1);
+      mbar_init(&sm.o_empty[i], kEpilogueThreads);
+      mbar_init(&sm.seg_ready[i], kSoftmaxThreads);
+    }
+    mbar_init(&sm.fin, 1);
+    sm.abort = 0;
+    sm.pend_n[0] = sm.pend_n[1] = 0;
     fence_mbar_init();
   }
-  __syncthreads();
-
-  if (warp == kConsumerWarps) {
-    // ------------------------------------------------------------ producer --
-    const int32_t* bt = a.block_tables + static_cast<int64_t>(b) * a.bt_stride + split_blk0;
-    for (int i = lane; i < split_nblk; i += 32) {
-      int blk = bt[i];
-      if (blk < 0 || blk >= a.num_blocks) {
-        atomicOr(a.err, kErrBadBlockId);
-        blk = a.num_blocks;  // fully out of the tensor map: TMA fills zeros
+  // Zero the padded Q and P operands once (rows >= QPK are never written).
+  for (int i = tid; i < kQBufs * kQBytes / 16; i += kThreads) reinterpret_cast<uint4*>(sm.q[0])[i] = make_uint4(0, 0, 0, 0);
+  for (int i = tid; i < 2 * kQBytes / 16; i += kThreads) reinterpret_cast<uint4*>(sm.p[0])[i] = make_uint4(0, 0, 0, 0);
+  fence_proxy_async_smem();
+  if (warp == kMmaWarp) {
+    tmem_alloc(&sm.tmem_base, kTmemCols);
+    tmem_relinquish();
+  }
+  pdl_launch_dependents();
+  pdl_wait();  // nothing above reads global memory
+  // ---- per-sequence tile prefix: every CTA derives the same schedule ----
+  if (warp == 0) {
+    int carry = 0;
+    for (int base = 0; base < a.batch; base += 32) {
+      const int b = base + lane;
+      int n = 0;
+      if (b < a.batch) {
+        int len = a.context_lens[b];
+        if (len > a.max_blocks * a.block_size) {
+          if (c == 0) atomicOr(a.err, kErrContextTooLong);
+          len = a.max_blocks * a.block_size;
+        }
+        len = max(len, 0);
+        n = seq_tiles(len);
+        sm.last_rows[b] = static_cast<uint8_t>(len - (n - 1) * kTile);  // unused when n == 0
       }
-      sm.blocks[i] = blk;
+      int incl = n;
+#pragma unroll
+      for (int off = 1; off < 32; off <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, incl, off);
+        if (lane >= off) incl += y;
+      }
+      if (b < a.batch) sm.tiles_before[b] = carry + incl - n;
+      carry += __shfl_sync(0xffffffffu, incl, 31);
     }
-    __syncwarp();
+    if (lane == 0) {
+      sm.tiles_before[a.batch] = carry;
+      sm.total_tiles = carry * kvh;
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+
+  const int total = sm.total_tiles;
+  const Sched sc = make_sched(total, ctas);
+  const int lo = total > 0 ? range_lo(c, sc) : 0;
+  const int hi = total > 0 ? range_lo(c + 1, sc) : 0;
+  const uint32_t tmem = sm.tmem_base;
+
+  if (warp == kProducerWarp) {
+    // -------------------------------------------------------- producer ----
+    // The warp stages the block ids of up to kChunkTiles tiles in smem (one
+    // parallel round of loads), then lane 0 issues their TMA copies.
     if (lane == 0) {
       tma_prefetch_desc(&kmap);
       tma_prefetch_desc(&vmap);
-      int issued = 0;
-      bool ok = true;
-      for (int t = 0; t < ntiles; ++t) {
-        const int s = t % kStages;
-        if (t >= kStages && !mbar_wait(&sm.empty[s], ((t / kStages) - 1) & 1)) {
-          atomicOr(a.err, kErrWaitTimeout);
-          ok = false;
-          break;
+      tma_prefetch_desc(&qmap);
+    }
+    int j = 0, seg = 0;
+    bool ok = true;
+    SegIter it;
+    it.init(sm, a, lo, hi);
+    Segment s;
+    for (; ok && it.next(sm, a, s); ++seg) {
+      const int qb = seg % kQBufs;
+      if (lane == 0) {
+        if (seg >= kQBufs && !mbar_wait(&sm.q_empty[qb], ((seg / kQBufs) - 1) & 1)) ok = false;
+        if (ok) {
+          mbar_arrive_expect_tx(&sm.q_full[qb], static_cast<uint32_t>(2 * QPK * 128));
+          tma_load_3d(sm.q[qb], &qmap, &sm.q_full[qb], 0, s.g * QPK, s.b);
+          tma_load_3d(sm.q[qb] + kQHalf, &qmap, &sm.q_full[qb], 64, s.g * QPK, s.b);
         }
-        const int tile_tok = tok_begin + t * kTile;
-        const int nsub = min(kTile / a.sub_rows, (tok_end - tile_tok + a.sub_rows - 1) / a.sub_rows);
-        mbar_arrive_expect_tx(&sm.full[s], static_cast<uint32_t>(nsub * 4 * a.sub_rows * 128));
-        uint8_t* st = sm.stage[s];
-        for (int u = 0; u < nsub; ++u) {
-          const int tok = tile_tok + u * a.sub_rows;
-          const int blk = sm.blocks[(tok >> a.log2_bs) - split_blk0];
-          const int row = blk * a.block_size + (tok & (a.block_size - 1));
-          const int off = u * a.sub_rows * 128;
-          tma_load_3d(st + 0 * kHalfBytes + off, &kmap, &sm.full[s], 0, g, row);
-          tma_load_3d(st + 1 * kHalfBytes + off, &kmap, &sm.full[s], 64, g, row);
-          tma_load_3d(st + 2 * kHalfBytes + off, &vmap, &sm.full[s], 0, g, row);
-          tma_load_3d(st + 3 * kHalfBytes + off, &vmap, &sm.full[s], 64, g, row);
-        }
-        ++issued;
       }
-      if (!ok) {
-        // Drain: wait (bounded) for the copies this CTA still has in flight.
-        for (int t = max(0, issued - kStages); t < issued; ++t)
-          (void)mbar_wait(&sm.full[t % kStages], (t / kStages) & 1);
-      }
-    }
-    return;
-  }
-
-  // -------------------------------------------------------------- consumers --
-  int tok_in_pass, j;
-  if constexpr (LPT == 16) {
-    tok_in_pass = lane >> 4;
-    j = lane & 15;
-  } else {
-    const int qtr = lane >> 3, r = lane & 7;
-    j = r % LPT;
-    tok_in_pass = (qtr / LPT) * 8 + (qtr % LPT) + LPT * (r / LPT);
-  }
-
-  const int h0 = g * QPK;
-  float qr[QPK][DPL];
-#pragma unroll
-  for (int h = 0; h < QPK; ++h) {
-    const __nv_bfloat16* qh = a.q + (static_cast<int64_t>(b) * a.num_heads + h0 + h) * kD;
-#pragma unroll
-    for (int i = 0; i < NCH; ++i) {
-      const int gc = j + LPT * i;
-      const uint4 w = *reinterpret_cast<const uint4*>(qh + gc * 8);
-      const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        qr[h][i * 8 + 2 * e] = bf16lo_to_f32(ww[e]) * a.scale_log2;
-        qr[h][i * 8 + 2 * e + 1] = bf16hi_to_f32(ww[e]) * a.scale_log2;
-      }
-    }
-  }
-
-  float m_run[QPK], l_run[QPK], acc[QPK][DPL];
-#pragma unroll
-  for (int h = 0; h < QPK; ++h) {
-    m_run[h] = -INFINITY;
-    l_run[h] = 0.f;
-#pragma unroll
-    for (int k = 0; k < DPL; ++k) acc[h][k] = 0.f;
-  }
-
-  for (int t = 0; t < ntiles; ++t) {
-    const int s = t % kStages;
-    if (!mbar_wait(&sm.full[s], (t / kStages) & 1)) {
-      if (lane == 0) atomicOr(a.err, kErrWaitTimeout);
-      break;
-    }
-    const uint32_t base = smem_u32(sm.stage[s]);
-    const int tile_tok = tok_begin + t * kTile;
-
-    float sc[NP][QPK];
-#pragma unroll
-    for (int p = 0; p < NP; ++p) {
-      const int tl = warp * kTokPerWarp + p * TPP + tok_in_pass;
-      const uint32_t row = base + tl * 128;
-      const int sw = tl & 7;
-      float dot[QPK];
-#pragma unroll
-      for (int h = 0; h < QPK; ++h) dot[h] = 0.f;
-#pragma unroll
-      for (int i = 0; i < NCH; ++i) {
-        const int gc = j + LPT * i;
-        const uint4 kw = ld_shared_v4(row + (gc >> 3) * kHalfBytes + (((gc & 7) ^ sw) << 4));
-        const uint32_t ww[4] = {kw.x, kw.y, kw.z, kw.w};
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const float lo = bf16lo_to_f32(ww[e]), hi = bf16hi_to_f32(ww[e]);
-#pragma unroll
-          for (int h = 0; h < QPK; ++h) {
-            dot[h] = fmaf(lo, qr[h][i * 8 + 2 * e], dot[h]);
-            dot[h] = fmaf(hi, qr[h][i * 8 + 2 * e + 1], dot[h]);
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      const int32_t* bt = a.block_tables + static_cast<int64_t>(s.b) * a.bt_stride;
+      for (int i = s.i0; ok && i < s.i0 + s.ntiles; i += kChunkTiles) {
+        const int nt = min(kChunkTiles, s.i0 + s.ntiles - i);
+        const int blk0 = (i * kTile) >> a.log2_bs;
+        const int blk1 = (min((i + nt) * kTile, s.len) - 1) >> a.log2_bs;  // inclusive
+        for (int k = lane; k <= blk1 - blk0; k += 32) {
+          int blk = bt[blk0 + k];
+          if (blk < 0 || blk >= a.num_blocks) {
+            atomicOr(a.err, kErrBadBlockId);
+            blk = a.num_blocks;  // fully outside the tensor map: zero fill
           }
+          sm.blocks[k] = blk;
         }
-      }
-#pragma unroll
-      for (int h = 0; h < QPK; ++h) {
-#pragma unroll
-        for (int off = 1; off < LPT; off <<= 1) dot[h] += __shfl_xor_sync(0xffffffffu, dot[h], off);
-      }
-      const bool valid = tile_tok + tl < tok_end;
-#pragma unroll
-      for (int h = 0; h < QPK; ++h) sc[p][h] = valid ? dot[h] : -INFINITY;
-    }
-
-    // Warp-wide tile max per head; lazy rescale of the running state.
-#pragma unroll
-    for (int h = 0; h < QPK; ++h) {
-      float mx = sc[0][h];
-#pragma unroll
-      for (int p = 1; p < NP; ++p) mx = fmaxf(mx, sc[p][h]);
-#pragma unroll
-      for (int off = LPT; off < 32; off <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
-      if (mx > m_run[h] + kRescaleThreshold) {
-        const float alpha = fast_exp2(m_run[h] - mx);  // 0 when m_run = -inf
-        m_run[h] = mx;
-        l_run[h] *= alpha;
-#pragma unroll
-        for (int k = 0; k < DPL; ++k) acc[h][k] *= alpha;
-      }
-    }
-
-#pragma unroll
-    for (int p = 0; p < NP; ++p) {
-      const int tl = warp * kTokPerWarp + p * TPP + tok_in_pass;
-      if (tile_tok + tl < tok_end) {  // rows past the context may hold any bits
-        float pr[QPK];
-#pragma unroll
-        for (int h = 0; h < QPK; ++h) {
-          pr[h] = fast_exp2(sc[p][h] - m_run[h]);
-          l_run[h] += pr[h];
-        }
-        const uint32_t row = base + 2 * kHalfBytes + tl * 128;
-        const int sw = tl & 7;
-#pragma unroll
-        for (int i = 0; i < NCH; ++i) {
-          const int gc = j + LPT * i;
-          const uint4 vw = ld_shared_v4(row + (gc >> 3) * kHalfBytes + (((gc & 7) ^ sw) << 4));
-          const uint32_t ww[4] = {vw.x, vw.y, vw.z, vw.w};
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const float lo = bf16lo_to_f32(ww[e]), hi = bf16hi_to_f32(ww[e]);
-#pragma unroll
-            for (int h = 0; h < QPK; ++h) {
-              acc[h][i * 8 + 2 * e] = fmaf(pr[h], lo, acc[h][i * 8 + 2 * e]);
-              acc[h][i * 8 + 2 * e + 1] = fmaf(pr[h], hi, acc[h][i * 8 + 2 * e + 1]);
+        __syncwarp();
+        if (lane == 0) {
+          for (int ii = i; ii < i + nt; ++ii, ++j) {
+            const int st = j % kStages;
+            if (j >= kStages && !mbar_wait(&sm.kv_empty[st], ((j / kStages) - 1) & 1)) {
+              ok = false;
+              break;
+            }
+            const int tok0 = ii * kTile;
+            const int nvalid = min(kTile, s.len - tok0);
+            const int nsub = (nvalid + a.sub_rows - 1) / a.sub_rows;
+            const uint32_t bytes = static_cast<uint32_t>(nsub * a.sub_rows * 128 * 2);
+            mbar_arrive_expect_tx(&sm.full_k[st], bytes);
+            mbar_arrive_expect_tx(&sm.full_v[st], bytes);
+            for (int u = 0; u < nsub; ++u) {
+              const int tok = tok0 + u * a.sub_rows;
+              const int blk = sm.blocks[(tok >> a.log2_bs) - blk0];
+              const int row = blk * a.block_size + (tok & (a.block_size - 1));
+              const int off = u * a.sub_rows * 128;
+              tma_load_3d(sm.k[st] + off, &kmap, &sm.full_k[st], 0, s.g, row);
+              tma_load_3d(sm.k[st] + kHalf + off, &kmap, &sm.full_k[st], 64, s.g, row);
+              tma_load_3d(sm.v[st] + off, &vmap, &sm.full_v[st], 0, s.g, row);
+              tma_load_3d(sm.v[st] + kHalf + off, &vmap, &sm.full_v[st], 64, s.g, row);
             }
           }
         }
+        ok = __shfl_sync(0xffffffffu, ok, 0);
+        j = __shfl_sync(0xffffffffu, j, 0);
+        __syncwarp();  // sm.blocks is rewritten by the next chunk
       }
     }
+    if (lane == 0) {
+      if (!ok) flag_error(a, sm, kErrWaitTimeout);
+      // Drain: every copy this CTA issued lands before the CTA may exit.
+      for (int jj = max(0, j - kStages); jj < j; ++jj) {
+        (void)mbar_wait(&sm.full_k[jj % kStages], (jj / kStages) & 1);
+        (void)mbar_wait(&sm.full_v[jj % kStages], (jj / kStages) & 1);
+      }
+      for (int sg = max(0, seg - kQBufs); sg < seg; ++sg) (void)mbar_wait(&sm.q_full[sg % kQBufs], (sg / kQBufs) & 1);
+    }
+  } else if (warp == kMmaWarp) {
+    // ------------------------------------------------------------- MMA ----
+    // S(j+1) = K Q^T is issued before PV(j), so the softmax of tile j+1 can
+    // start as soon as tile j's probabilities are out.
+    if (lane == 0) {
+      constexpr uint32_t idesc_s = umma_idesc_bf16(kTile, kN, false);           // A = K, B = Qpad
+      constexpr uint32_t idesc_o = umma_idesc_bf16(kD, kN, false) | (1u << 15);  // A = V^T (MN-major), B = P^T
+      bool ok = true;
+      // Walk of the S side (one tile ahead) and of the PV side.
+      int js = 0, segs = 0, i_s = 0, left_s = 0;
+      Segment cur_s{};
+      SegIter it_s, it_p;
+      it_s.init(sm, a, lo, hi);
+      it_p.init(sm, a, lo, hi);
+      int jp = 0, segp = 0, left_p = 0;
+      Segment cur_p{};
+      auto issue_s = [&]() -> bool {  // S for the next tile of the S walk
+        if (left_s == 0) {
+          it_s.next(sm, a, cur_s);
+          left_s = cur_s.ntiles;
+          i_s = 0;
+          if (!mbar_wait(&sm.q_full[segs % kQBufs], (segs / kQBufs) & 1)) return false;
+          ++segs;
+        }
+        const int st = js % kStages, sb = js & 1;
+        if (!mbar_wait(&sm.full_k[st], (js / kStages) & 1)) return false;
+        if (js >= 2 && !mbar_wait(&sm.s_free[sb], ((js >> 1) - 1) & 1)) return false;
+        tc_fence_after();
+        const uint32_t k_addr = smem_u32(sm.k[st]);
+        const uint32_t q_addr = smem_u32(sm.q[(segs - 1) % kQBufs]);
+#pragma unroll
+        for (int kk = 0; kk < kD / 16; ++kk) {
+          const uint32_t koff = (kk >> 2) * kHalf + (kk & 3) * 32;
+          const uint32_t qoff = (kk >> 2) * kQHalf + (kk & 3) * 32;
+          umma_f16_ss(tmem + sb * kN, smem_desc_sw128(k_addr + koff, 16, 1024),
+                      smem_desc_sw128(q_addr + qoff, 16, 1024), idesc_s, kk > 0);
+        }
+        umma_commit(&sm.s_full[sb]);
+        ++js;
+        ++i_s;
+        --left_s;
+        return true;
+      };
+      const int ntiles_total = hi - lo;
+      if (ntiles_total > 0) ok = issue_s();
+      for (int n = 0; ok && n < ntiles_total; ++n) {
+        if (n + 1 < ntiles_total) {
+          ok = issue_s();
+          if (!ok) break;
+        }
+        if (left_p == 0) {
+          it_p.next(sm, a, cur_p);
+          left_p = cur_p.ntiles;
+          if (segp >= kOBufs && !mbar_wait(&sm.o_empty[segp % kOBufs], ((segp / kOBufs) - 1) & 1)) {
+            ok = false;
+            break;
+          }
+          ++segp;
+        }
+        const int i_in_seg = cur_p.ntiles - left_p;
+        const int st = jp % kStages, sb = jp & 1, ob = (segp - 1) % kOBufs;
+        if (!mbar_wait(&sm.p_full[sb], (jp >> 1) & 1) || !mbar_wait(&sm.full_v[st], (jp / kStages) & 1)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t v_addr = smem_u32(sm.v[st]);
+        const uint32_t p_addr = smem_u32(sm.p[sb]);
+        const uint32_t o_tmem = tmem + 32 + ob * kN;
+#pragma unroll
+        for (int kk = 0; kk < kTile / 16; ++kk) {
+          const uint64_t va = smem_desc_sw128(v_addr + kk * 16 * 128, kHalf, 1024);
+          const uint64_t pb = smem_desc_sw128(p_addr + (kk >> 2) * kQHalf + (kk & 3) * 32, 16, 1024);
+          umma_f16_ss(o_tmem, va, pb, idesc_o, (i_in_seg > 0 || kk > 0) ? 1u : 0u);
+        }
+        umma_commit(&sm.kv_empty[st]);
+        umma_commit(&sm.pv_done[sb]);
+        ++jp;
+        if (--left_p == 0) {
+          umma_commit(&sm.o_full[ob]);
+          umma_commit(&sm.q_empty[(segp - 1) % kQBufs]);
+        }
+      }
+      if (!ok) flag_error(a, sm, kErrWaitTimeout);
+      umma_commit(&sm.fin);  // every MMA of this CTA completes before TMEM is freed
+      (void)mbar_wait(&sm.fin, 0);
+    }
+  } else if (warp < 4) {
+    // --------------------------------------------------------- softmax ----
+    const uint32_t t_lane = static_cast<uint32_t>(warp * 32) << 16;
+    int j = 0, seg = 0;
+    bool all_ok = true;
+    SegIter it;
+    it.init(sm, a, lo, hi);
+    Segment s;
+    for (; all_ok && it.next(sm, a, s); ++seg) {
+      const int ob = seg % kOBufs;
+      const uint32_t o_tmem = tmem + 32 + ob * kN + t_lane;
+      float m_ref[QPK], l_t[QPK];
+#pragma unroll
+      for (int h = 0; h < QPK; ++h) {
+        m_ref[h] = -INFINITY;
+        l_t[h] = 0.f;
+      }
+      for (int i = s.i0; i < s.i0 + s.ntiles; ++i, ++j) {
+        const int st = j % kStages, sb = j & 1, rb = j & 1;
+        const int nvalid = min(kTile, s.len - i * kTile);
+        const bool valid = tid < nvalid;
+        // S(j) ready; P buffer sb free (PV(j-2) done); V(j) landed when rows
+        // past the context must be zeroed.
+        bool ok = mbar_wait(&sm.s_full[sb], (j >> 1) & 1);
+        if (j >= 2) ok = ok && mbar_wait(&sm.pv_done[sb], ((j - 2) >> 1) & 1);
+        if (nvalid < kTile) ok = ok && mbar_wait(&sm.full_v[st], (j / kStages) & 1);
+        ok = __all_sync(0xffffffffu, ok);  // tcgen05.ld below needs a converged warp
+        float sv8[8];
+        float sv[QPK];
+        if (ok) {
+          tc_fence_after();
+          tmem_ld_cols(tmem + sb * kN + t_lane, QPK, sv8);
+          tc_fence_before();
+          mbar_arrive(&sm.s_free[sb]);
+        }
+#pragma unroll
+        for (int h = 0; h < QPK; ++h) {
+          sv[h] = (ok && valid) ? sv8[h] * a.scale_log2 : -INFINITY;
+          float x = sv[h];
+#pragma unroll
+          for (int off = 16; off > 0; off >>= 1) x = fmaxf(x, __shfl_xor_sync(0xffffffffu, x, off));
+          if (lane == 0) sm.red[rb][warp][h] = x;
+        }
+        if (lane == 0) sm.warp_ok[rb][warp] = ok;
+        named_barrier_sync(1, kSoftmaxThreads);
+        all_ok = sm.warp_ok[rb][0] && sm.warp_ok[rb][1] && sm.warp_ok[rb][2] && sm.warp_ok[rb][3];
+        if (!all_ok) break;
+        bool any_resc = false;
+        float alpha[QPK];
+#pragma unroll
+        for (int h = 0; h < QPK; ++h) {
+          const float mt = fmaxf(fmaxf(sm.red[rb][0][h], sm.red[rb][1][h]), fmaxf(sm.red[rb][2][h], sm.red[rb][3][h]));
+          alpha[h] = 1.f;
+          if (mt > m_ref[h] + kRescaleThreshold) {
+            alpha[h] = fast_exp2(m_ref[h] - mt);  // 0 when m_ref = -inf
+            m_ref[h] = mt;
+            l_t[h] *= alpha[h];
+            any_resc = true;
+          }
+        }
+        if (any_resc && i > s.i0) {
+          // O^T lane t is dim t; PV(j-1) must be complete before O changes.
+          bool okr = __all_sync(0xffffffffu, mbar_wait(&sm.pv_done[(j - 1) & 1], ((j - 1) >> 1) & 1));
+          if (lane == 0) sm.resc_ok[warp] = okr;
+          named_barrier_sync(1, kSoftmaxThreads);
+          all_ok = sm.resc_ok[0] && sm.resc_ok[1] && sm.resc_ok[2] && sm.resc_ok[3];
+          if (!all_ok) break;
+          float o[8];
+          tc_fence_after();
+          tmem_ld_cols(o_tmem, QPK, o);
+#pragma unroll
+          for (int h = 0; h < QPK; ++h) o[h] *= alpha[h];
+          tmem_st_cols(o_tmem, QPK, o);
+        }
+        if (!valid) {
+          // Rows past the context hold arbitrary bits; P is 0 there, but the
+          // tensor core still multiplies them, so they become zeros.
+          const uint32_t vrow = smem_u32(sm.v[st]) + tid * 128;
+#pragma unroll
+          for (int cc = 0; cc < 8; ++cc) {
+            st_shared_v4(vrow + cc * 16, 0, 0, 0, 0);
+            st_shared_v4(vrow + kHalf + cc * 16, 0, 0, 0, 0);
+          }
+        }
+        // P^T[h][token], K-major SW128: tokens 0-63 in the first 2 KiB half.
+        const uint32_t p_base = smem_u32(sm.p[sb]) + (tid >> 6) * kQHalf + (tid & 7) * 2;
+        const int chunk = (tid & 63) >> 3;
+#pragma unroll
+        for (int h = 0; h < QPK; ++h) {
+          const float mu = (m_ref[h] == -INFINITY) ? 0.f : m_ref[h];
+          const float p = valid ? fast_exp2(sv[h] - mu) : 0.f;
+          l_t[h] += p;
+          const __nv_bfloat16 pb = __float2bfloat16_rn(p);
+          const uint32_t addr = p_base + h * 128 + ((chunk ^ (h & 7)) << 4);
+          asm volatile("st.shared.b16 [%0], %1;" ::"r"(addr), "h"(*reinterpret_cast<const uint16_t*>(&pb))
+                       : "memory");
+        }
+        fence_proxy_async_smem();
+        tc_fence_before();
+        mbar_arrive(&sm.p_full[sb]);
+      }
+      if (!all_ok) break;
+      // Hand the segment's (m, l) to the epilogue warps and go on streaming;
+      // the info slot is free once the epilogue released segment seg-2.
+      if (seg >= kOBufs && !__all_sync(0xffffffffu, mbar_wait(&sm.o_empty[ob], ((seg / kOBufs) - 1) & 1))) {
+        all_ok = false;
+        break;
+      }
+      typename Smem::SegInfo& info = sm.seg_info[ob];
+#pragma unroll
+      for (int h = 0; h < QPK; ++h) {
+        float x = l_t[h];
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) x += __shfl_xor_sync(0xffffffffu, x, off);
+        if (lane == 0) info.l_part[warp][h] = x;
+        if (tid == 0) info.m[h] = m_ref[h];
+      }
+      if (tid == 0) {
+        info.b = s.b;
+        info.g = s.g;
+        info.n = s.n;
+        info.ntiles = s.ntiles;
+        info.pair_t0 = s.pair_t0;
+        info.slot = (s.start == lo) ? 0 : 1;
+      }
+      mbar_arrive(&sm.seg_ready[ob]);
+    }
+    if (!all_ok) flag_error(a, sm, kErrWaitTimeout);
+  } else {
+    // ------------------------------------------------------- epilogue ----
+    // Warps 6-9: thread e owns dim d of O^T (TMEM lane d). Per segment:
+    // normalise and store, or keep a partial piece; then publish the pieces
+    // once and merge the pairs this CTA completes last.
+    const int ew = warp - kEpilogueWarp0;
+    const int e = ew * 32 + lane;
+    const int d = (warp & 3) * 32 + lane;
+    const uint32_t t_lane = static_cast<uint32_t>((warp & 3) * 32) << 16;
+    bool ok = true;
+    int seg = 0;
+    SegIter it;
+    it.init(sm, a, lo, hi);
+    Segment s;
+    // Never leaves the walk early: every epilogue warp must reach the publish
+    // barrier after the partial segments, even after a failed wait.
+    for (; it.next(sm, a, s); ++seg) {
+      const int ob = seg % kOBufs;
+      if (ok) ok = mbar_wait(&sm.seg_ready[ob], (seg / kOBufs) & 1) && mbar_wait(&sm.o_full[ob], (seg / kOBufs) & 1);
+      ok = __all_sync(0xffffffffu, ok);
+      if (ok) {
+        float o[8];
+        tc_fence_after();
+        tmem_ld_cols(tmem + 32 + ob * kN + t_lane, QPK, o);
+        const typename Smem::SegInfo& info = sm.seg_info[ob];
+        float l_sum[QPK], m_seg[QPK];
+#pragma unroll
+        for (int h = 0; h < QPK; ++h) {
+          l_sum[h] = info.l_part[0][h] + info.l_part[1][h] + info.l_part[2][h] + info.l_part[3][h];
+          m_seg[h] = info.m[h];
+        }
+        const int slot = info.slot;
+        tc_fence_before();
+        mbar_arrive(&sm.o_empty[ob]);
+        if (s.ntiles == s.n) {  // the whole pair lies in this CTA
+          __nv_bfloat16* out = a.out + (static_cast<int64_t>(s.b) * a.num_heads + s.g * QPK) * kD;
+#pragma unroll
+          for (int h = 0; h < QPK; ++h)
+            out[h * kD + d] = __float2bfloat16_rn(l_sum[h] > 0.f ? o[h] / l_sum[h] : 0.f);
+        } else {
+          // A piece of a pair shared with other CTAs: stored now, published
+          // with one ticket right after the partial segments.
+          const int64_t part = part_index(c, s.pair_t0, sc, QPK);
+#pragma unroll
+          for (int h = 0; h < QPK; ++h) {
+            a.ws_o[(part + h) * kD + d] = o[h];
+            if (e == 0) a.ws_ml[part + h] = make_float2(m_seg[h], l_sum[h]);
+          }
+          if (e == 0) {
+            sm.pend_pair[slot] = s.b * kvh + s.g;
+            sm.pend_t0[slot] = s.pair_t0;
+            sm.pend_n[slot] = s.n;
+            sm.pend_b[slot] = s.b;
+            sm.pend_g[slot] = s.g;
+          }
+        }
+      }
+      if (seg + 1 == it.npartial) {
+        if (lane == 0) sm.epi_ok[ew] = ok;
+        named_barrier_sync(2, kEpilogueThreads);  // every partial store of this CTA is issued
+        const bool all_ok = sm.epi_ok[0] && sm.epi_ok[1] && sm.epi_ok[2] && sm.epi_ok[3];
+        publish_and_merge<QPK>(sm, a, c, sc, e, d, all_ok);
+      }
+    }
+    if (!ok) flag_error(a, sm, kErrWaitTimeout);
+
+    // Sequences without context own no tile: their outputs are zeros.
+    for (int b = c; b < a.batch; b += ctas) {
+      if (sm.tiles_before[b + 1] == sm.tiles_before[b]) {
+        __nv_bfloat16* out = a.out + static_cast<int64_t>(b) * a.num_heads * kD;
+        for (int h = 0; h < a.num_heads; ++h) out[h * kD + e] = __float2bfloat16_rn(0.f);
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == kMmaWarp) {
     __syncwarp();
-    if (lane == 0) mbar_arrive(&sm.empty[s]);
+    tmem_dealloc(tmem, kTmemCols);
   }
-
-  // Reduce the token lanes of the warp (all lanes of one token hold the same l).
-#pragma unroll
-  for (int h = 0; h < QPK; ++h) {
-#pragma unroll
-    for (int off = LPT; off < 32; off <<= 1) {
-      l_run[h] += __shfl_xor_sync(0xffffffffu, l_run[h], off);
-#pragma unroll
-      for (int k = 0; k < DPL; ++k) acc[h][k] += __shfl_xor_sync(0xffffffffu, acc[h][k], off);
-    }
-  }
-  if (tok_in_pass == 0) {
-#pragma unroll
-    for (int h = 0; h < QPK; ++h) {
-#pragma unroll
-      for (int i = 0; i < NCH; ++i) {
-        const int gc = j + LPT * i;
-#pragma unroll
-        for (int e = 0; e < 8; ++e) sm.red_o[warp][h][gc * 8 + e] = acc[h][i * 8 + e];
-      }
-    }
-  }
-  if (lane == 0) {
-#pragma unroll
-    for (int h = 0; h < QPK; ++h) {
-      sm.red_m[warp][h] = m_run[h];
-      sm.red_l[warp][h] = l_run[h];
-    }
-  }
-  named_barrier_sync(1, kConsumerWarps * 32);
-
-  // Merge the 4 warps: thread d owns output dim d of every head in the group.
-  const int d = threadIdx.x;
-  float o_cta[QPK], m_cta[QPK], l_cta[QPK];
-#pragma unroll
-  for (int h = 0; h < QPK; ++h) {
-    float M = -INFINITY;
-#pragma unroll
-    for (int w = 0; w < kConsumerWarps; ++w) M = fmaxf(M, sm.red_m[w][h]);
-    float o = 0.f, l = 0.f;
-    if (M != -INFINITY) {
-#pragma unroll
-      for (int w = 0; w < kConsumerWarps; ++w) {
-        const float mw = sm.red_m[w][h];
-        const float sc_w = (mw == -INFINITY) ? 0.f : fast_exp2(mw - M);
-        o = fmaf(sc_w, sm.red_o[w][h][d], o);
-        l = fmaf(sc_w, sm.red_l[w][h], l);
-      }
-    }
-    o_cta[h] = o;
-    m_cta[h] = M;
-    l_cta[h] = l;
-  }
-
-  __nv_bfloat16* out = a.out + (static_cast<int64_t>(b) * a.num_heads + h0) * kD;
-  if (nsplit == 1) {
-#pragma unroll
-    for (int h = 0; h < QPK; ++h) out[h * kD + d] = __float2bfloat16_rn(l_cta[h] > 0.f ? o_cta[h] / l_cta[h] : 0.f);
-    return;
-  }
-
-  const int64_t pair = static_cast<int64_t>(b) * a.num_kv_heads + g;
-  const int64_t part0 = pair * a.max_splits * QPK;
-#pragma unroll
-  for (int h = 0; h < QPK; ++h) {
-    const int64_t idx = part0 + static_cast<int64_t>(split) * QPK + h;
-    a.ws_o[idx * kD + d] = o_cta[h];
-    if (d == 0) a.ws_ml[idx] = make_float2(m_cta[h], l_cta[h]);
-  }
-  __threadfence();
-  named_barrier_sync(1, kConsumerWarps * 32);
-  if (d == 0) sm.last = (atomicAdd(a.ws_cnt + pair, 1) == nsplit - 1);
-  named_barrier_sync(1, kConsumerWarps * 32);
-  if (!sm.last) return;
-  __threadfence();
-
-#pragma unroll
-  for (int h = 0; h < QPK; ++h) {
-    float M = -INFINITY;
-    for (int sp = 0; sp < nsplit; ++sp) M = fmaxf(M, __ldcg(&a.ws_ml[part0 + sp * QPK + h]).x);
-    float o = 0.f, l = 0.f;
-    if (M != -INFINITY) {
-      for (int sp = 0; sp < nsplit; ++sp) {
-        const float2 ml = __ldcg(&a.ws_ml[part0 + sp * QPK + h]);
-        const float w = (ml.x == -INFINITY) ? 0.f : fast_exp2(ml.x - M);
-        o = fmaf(w, __ldcg(&a.ws_o[(part0 + sp * QPK + h) * kD + d]), o);
-        l = fmaf(w, ml.y, l);
-      }
-    }
-    out[h * kD + d] = __float2bfloat16_rn(l > 0.f ? o / l : 0.f);
-  }
-  if (d == 0) a.ws_cnt[pair] = 0;
 }
+
+static_assert(sizeof(Smem) + 1024 <= 232448, "decode shared memory exceeds the 227 KB per-CTA limit");
 
 struct WsLayout {
   size_t cnt_off, ml_off, o_off, total;
 };
 
-WsLayout ws_layout(int batch, int num_heads, int num_kv_heads, int max_splits) {
+// [0, 256): error word | tickets [batch * KVH], one per 128-byte line | (m, l) [C][2][QPK] | o [C][2][QPK][128]
+WsLayout ws_layout(int batch, int num_heads, int num_kv_heads, int ctas) {
   auto up = [](size_t x) { return (x + 255) & ~size_t(255); };
   const int qpk = num_heads / num_kv_heads;
-  const size_t pairs = static_cast<size_t>(batch) * num_kv_heads;
-  const size_t parts = pairs * static_cast<size_t>(max_splits) * qpk;
+  const size_t parts = static_cast<size_t>(ctas) * 2 * qpk;
   WsLayout w;
-  w.cnt_off = 256;  // [0, 256): device error word
-  w.ml_off = w.cnt_off + up(pairs * sizeof(int));
+  w.cnt_off = 256;
+  w.ml_off = w.cnt_off + up(static_cast<size_t>(batch) * num_kv_heads * kTicketStride * sizeof(int));
   w.o_off = w.ml_off + up(parts * sizeof(float2));
   w.total = w.o_off + up(parts * kD * sizeof(float));
   return w;
 }
 
-template <int QPK>
-int launch(const CUtensorMap& km, const CUtensorMap& vm, const DecodeArgs& a, int batch, cudaStream_t stream) {
-  const size_t smem = sizeof(Smem<QPK>) + 1024;
-  int rc = ensure_dynamic_smem(reinterpret_cast<const void*>(&paged_decode_kernel<QPK>), smem);
-  if (rc != NVK_OK) return rc;
-  const dim3 grid(a.max_splits, a.num_kv_heads, batch);
-  paged_decode_kernel<QPK><<<grid, kThreads, smem, stream>>>(km, vm, a);
-  return check_cuda(cudaGetLastError(), "paged_decode launch");
+int resolve_ctas(int num_ctas, int* out) {
+  if (num_ctas > 0) {
+    *out = num_ctas;
+    return NVK_OK;
+  }
+  int dev = 0, sms = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  if (e != cudaSuccess) return check_cuda(e, "paged_decode: SM count");
+  *out = sms;
+  return NVK_OK;
 }
 
 }  // namespace
 }  // namespace nvk
 
 extern "C" int nvk_paged_decode_workspace_size(int batch, int num_heads, int num_kv_heads, int head_dim,
-                                               int max_splits, size_t* bytes) {
+                                               int num_ctas, size_t* bytes) {
   using namespace nvk;
   if (!bytes) return fail(NVK_ERR_INVALID_ARGUMENT, "workspace_size: null output pointer");
-  if (batch < 0 || num_heads <= 0 || num_kv_heads <= 0 || max_splits <= 0 || num_heads % num_kv_heads != 0)
-    return fail(NVK_ERR_INVALID_ARGUMENT, "workspace_size: bad sizes (batch=%d heads=%d kv_heads=%d splits=%d)",
-                batch, num_heads, num_kv_heads, max_splits);
+  if (batch < 0 || num_heads <= 0 || num_kv_heads <= 0 || num_ctas < 0 || num_heads % num_kv_heads != 0)
+    return fail(NVK_ERR_INVALID_ARGUMENT, "workspace_size: bad sizes (batch=%d heads=%d kv_heads=%d ctas=%d)",
+                batch, num_heads, num_kv_heads, num_ctas);
   if (head_dim != kD) return fail(NVK_ERR_UNSUPPORTED, "workspace_size: head_dim %d unsupported (128 only)", head_dim);
-  *bytes = ws_layout(batch, num_heads, num_kv_heads, max_splits).total;
+  int ctas = 0;
+  const int rc = resolve_ctas(num_ctas, &ctas);
+  if (rc != NVK_OK) return rc;
+  *bytes = ws_layout(batch, num_heads, num_kv_heads, ctas).total;
   return NVK_OK;
 }
 
 extern "C" int nvk_paged_decode(void* out, const void* query, const void* key_cache, const void* value_cache,
                                 int num_blocks, int block_size, const int32_t* block_tables, int block_table_stride,
                                 int max_blocks_per_seq, const int32_t* context_lens, int batch, int num_heads,
-                                int num_kv_heads, int head_dim, float scale, int blocks_per_split, int max_splits,
-                                void* workspace, size_t workspace_bytes, nvk_stream_t stream) {
+                                int num_kv_heads, int head_dim, float scale, int num_ctas, void* workspace,
+                                size_t workspace_bytes, nvk_stream_t stream) {
   using namespace nvk;
-  if (batch < 0 || num_blocks <= 0 || num_heads <= 0 || num_kv_heads <= 0)
-    return fail(NVK_ERR_INVALID_ARGUMENT, "paged_decode: bad sizes (batch=%d blocks=%d heads=%d kv_heads=%d)", batch,
-                num_blocks, num_heads, num_kv_heads);
+  if (batch < 0 || num_blocks <= 0 || num_heads <= 0 || num_kv_heads <= 0 || num_ctas < 0)
+    return fail(NVK_ERR_INVALID_ARGUMENT, "paged_decode: bad sizes (batch=%d blocks=%d heads=%d kv_heads=%d ctas=%d)",
+                batch, num_blocks, num_heads, num_kv_heads, num_ctas);
   if (batch == 0) return NVK_OK;
   if (head_dim != kD) return fail(NVK_ERR_UNSUPPORTED, "paged_decode: head_dim %d unsupported (128 only)", head_dim);
   if (num_heads % num_kv_heads != 0)
@@ -464,63 +956,72 @@ extern "C" int nvk_paged_decode(void* out, const void* query, const void* key_ca
   if (block_size < 16 || block_size > 256 || (block_size & (block_size - 1)) != 0)
     return fail(NVK_ERR_UNSUPPORTED, "paged_decode: block_size %d unsupported (power of two in [16, 256])",
                 block_size);
-  if (blocks_per_split <= 0 || blocks_per_split > kMaxSplitBlocks)
-    return fail(NVK_ERR_INVALID_ARGUMENT, "paged_decode: blocks_per_split %d outside [1, %d]", blocks_per_split,
-                kMaxSplitBlocks);
   if (max_blocks_per_seq <= 0 || block_table_stride < max_blocks_per_seq)
     return fail(NVK_ERR_INVALID_ARGUMENT, "paged_decode: block table width %d / stride %d invalid",
                 max_blocks_per_seq, block_table_stride);
-  if (max_splits < (max_blocks_per_seq + blocks_per_split - 1) / blocks_per_split || max_splits > 65535)
-    return fail(NVK_ERR_INVALID_ARGUMENT, "paged_decode: max_splits %d < ceil(%d / %d)", max_splits,
-                max_blocks_per_seq, blocks_per_split);
-  if (batch > 65535 || num_kv_heads > 65535)
-    return fail(NVK_ERR_UNSUPPORTED, "paged_decode: batch %d or kv heads %d above grid limit", batch, num_kv_heads);
   if (!out || !query || !key_cache || !value_cache || !block_tables || !context_lens)
     return fail(NVK_ERR_INVALID_ARGUMENT, "paged_decode: null pointer");
   if (!aligned16(out) || !aligned16(query))
     return fail(NVK_ERR_INVALID_ARGUMENT, "paged_decode: q/out must be 16-byte aligned");
-  const WsLayout wl = ws_layout(batch, num_heads, num_kv_heads, max_splits);
+  int ctas = 0;
+  int rc = resolve_ctas(num_ctas, &ctas);
+  if (rc != NVK_OK) return rc;
+  const WsLayout wl = ws_layout(batch, num_heads, num_kv_heads, ctas);
   if (!workspace || workspace_bytes < wl.total || !aligned16(workspace))
     return fail(NVK_ERR_WORKSPACE, "paged_decode: workspace %zu bytes < %zu needed (or misaligned)", workspace_bytes,
                 wl.total);
 
   const int64_t rows = static_cast<int64_t>(num_blocks) * block_size;
   const int sub_rows = block_size < 32 ? block_size : 32;
-  CUtensorMap km, vm;
-  int rc = kv_tensor_map(&km, key_cache, rows, num_kv_heads, sub_rows);
-  if (rc != NVK_OK) return rc;
-  rc = kv_tensor_map(&vm, value_cache, rows, num_kv_heads, sub_rows);
+  CUtensorMap km, vm, qm;
+  if ((rc = kv_tensor_map(&km, key_cache, rows, num_kv_heads, sub_rows)) != NVK_OK) return rc;
+  if ((rc = kv_tensor_map(&vm, value_cache, rows, num_kv_heads, sub_rows)) != NVK_OK) return rc;
+  const size_t smem = sizeof(Smem) + 1024;
+  const void* kernel = qpk == 1   ? reinterpret_cast<const void*>(&paged_decode_kernel<1>)
+                       : qpk == 2 ? reinterpret_cast<const void*>(&paged_decode_kernel<2>)
+                       : qpk == 4 ? reinterpret_cast<const void*>(&paged_decode_kernel<4>)
+                                  : reinterpret_cast<const void*>(&paged_decode_kernel<8>);
+  rc = ensure_dynamic_smem(kernel, smem);
   if (rc != NVK_OK) return rc;
 
   uint8_t* ws = static_cast<uint8_t*>(workspace);
-  DecodeArgs a;
-  a.out = static_cast<__nv_bfloat16*>(out);
-  a.q = static_cast<const __nv_bfloat16*>(query);
-  a.block_tables = block_tables;
-  a.context_lens = context_lens;
-  a.err = reinterpret_cast<int*>(ws);
-  a.ws_cnt = reinterpret_cast<int*>(ws + wl.cnt_off);
-  a.ws_ml = reinterpret_cast<float2*>(ws + wl.ml_off);
-  a.ws_o = reinterpret_cast<float*>(ws + wl.o_off);
-  a.bt_stride = block_table_stride;
-  a.max_blocks = max_blocks_per_seq;
-  a.num_blocks = num_blocks;
-  a.block_size = block_size;
-  a.log2_bs = __builtin_ctz(static_cast<unsigned>(block_size));
-  a.sub_rows = sub_rows;
-  a.num_heads = num_heads;
-  a.num_kv_heads = num_kv_heads;
-  a.blocks_per_split = blocks_per_split;
-  a.max_splits = max_splits;
-  a.scale_log2 = scale * 1.4426950408889634f;
-
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  switch (qpk) {
-    case 1: return launch<1>(km, vm, a, batch, st);
-    case 2: return launch<2>(km, vm, a, batch, st);
-    case 4: return launch<4>(km, vm, a, batch, st);
-    default: return launch<8>(km, vm, a, batch, st);
+  // Sequences go in chunks of kMaxSeqs launches (the schedule lives in smem).
+  for (int b0 = 0; b0 < batch; b0 += kMaxSeqs) {
+    const int nb = batch - b0 < kMaxSeqs ? batch - b0 : kMaxSeqs;
+    const void* qb = static_cast<const uint8_t*>(query) + static_cast<size_t>(b0) * num_heads * kD * 2;
+    // q as [nb, heads, 128]: box {64 dims, QPK heads, 1 sequence}
+    if ((rc = kv_tensor_map(&qm, qb, nb, num_heads, 1, 0, qpk)) != NVK_OK) return rc;
+    DecodeArgs a;
+    a.out = static_cast<__nv_bfloat16*>(out) + static_cast<size_t>(b0) * num_heads * kD;
+    a.block_tables = block_tables + static_cast<int64_t>(b0) * block_table_stride;
+    a.context_lens = context_lens + b0;
+    a.err = reinterpret_cast<int*>(ws);
+    a.ws_cnt = reinterpret_cast<int*>(ws + wl.cnt_off) + static_cast<size_t>(b0) * num_kv_heads * kTicketStride;
+    a.ws_ml = reinterpret_cast<float2*>(ws + wl.ml_off);
+    a.ws_o = reinterpret_cast<float*>(ws + wl.o_off);
+    a.batch = nb;
+    a.bt_stride = block_table_stride;
+    a.max_blocks = max_blocks_per_seq;
+    a.num_blocks = num_blocks;
+    a.block_size = block_size;
+    a.log2_bs = __builtin_ctz(static_cast<unsigned>(block_size));
+    a.sub_rows = sub_rows;
+    a.num_heads = num_heads;
+    a.num_kv_heads = num_kv_heads;
+    a.qpk = qpk;
+    a.scale_log2 = scale * 1.4426950408889634f;
+    cudaError_t e;
+    switch (qpk) {
+      case 1: e = launch_pdl(paged_decode_kernel<1>, dim3(ctas), dim3(kThreads), smem, st, km, vm, qm, a); break;
+      case 2: e = launch_pdl(paged_decode_kernel<2>, dim3(ctas), dim3(kThreads), smem, st, km, vm, qm, a); break;
+      case 4: e = launch_pdl(paged_decode_kernel<4>, dim3(ctas), dim3(kThreads), smem, st, km, vm, qm, a); break;
+      default: e = launch_pdl(paged_decode_kernel<8>, dim3(ctas), dim3(kThreads), smem, st, km, vm, qm, a); break;
+    }
+    rc = check_cuda(e, "paged_decode launch");
+    if (rc != NVK_OK) return rc;
   }
+  return NVK_OK;
 }
 
 // ---------------------------------------------------------------------------
@@ -574,34 +1075,34 @@ extern "C" int nvk_paged_decode_noalloc(void* out, const void* query, const void
                                         const void* value_cache, int num_blocks, int block_size,
                                         const int32_t* block_tables, int block_table_stride, int max_blocks_per_seq,
                                         const int32_t* context_lens, int batch, int num_heads, int num_kv_heads,
-                                        int head_dim, float scale, int blocks_per_split, int max_splits,
-                                        nvk_stream_t stream) {
+                                        int head_dim, float scale, int num_ctas, nvk_stream_t stream) {
   using namespace nvk;
-  size_t need = 0;
   size_t header = 0;
   const bool sane = batch > 0 && num_heads > 0 && num_kv_heads > 0 && num_heads % num_kv_heads == 0 &&
-                    max_splits > 0 && head_dim == kD;
+                    num_ctas >= 0 && head_dim == kD;
   if (sane) {
-    const WsLayout wl = ws_layout(batch, num_heads, num_kv_heads, max_splits);
-    need = wl.total;
-    header = wl.ml_off;  // error word + arrival counters
-    if (need > kNoAllocScratchBytes)
+    int ctas = 0;
+    const int rc = resolve_ctas(num_ctas, &ctas);
+    if (rc != NVK_OK) return rc;
+    const WsLayout wl = ws_layout(batch, num_heads, num_kv_heads, ctas);
+    header = wl.ml_off;  // error word + arrival tickets
+    if (wl.total > kNoAllocScratchBytes)
       return fail(NVK_ERR_UNSUPPORTED,
                   "paged_decode_noalloc: %zu bytes of split-K scratch needed, the static scratch holds %zu "
-                  "(fewer splits, a smaller batch, or nvk_paged_decode with a caller workspace)",
-                  need, kNoAllocScratchBytes);
+                  "(a smaller batch, or nvk_paged_decode with a caller workspace)",
+                  wl.total, kNoAllocScratchBytes);
   }
   void* scratch = nullptr;
   int rc = noalloc_scratch(&scratch);
   if (rc != NVK_OK) return rc;
   if (sane) {
     // The array keeps the previous call's contents: clear the error word and
-    // the arrival counters, which must start at zero.
+    // the arrival tickets, which must start at zero.
     rc = check_cuda(cudaMemsetAsync(scratch, 0, header, reinterpret_cast<cudaStream_t>(stream)),
                     "paged_decode_noalloc: clear scratch header");
     if (rc != NVK_OK) return rc;
   }
   return nvk_paged_decode(out, query, key_cache, value_cache, num_blocks, block_size, block_tables,
                           block_table_stride, max_blocks_per_seq, context_lens, batch, num_heads, num_kv_heads,
-                          head_dim, scale, blocks_per_split, max_splits, scratch, kNoAllocScratchBytes, stream);
+                          head_dim, scale, num_ctas, scratch, kNoAllocScratchBytes, stream);
 }

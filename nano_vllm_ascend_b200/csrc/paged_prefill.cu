@@ -85,6 +85,8 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
                                                               const PrefillArgs a) {
   const int qt = gridDim.x - 1 - blockIdx.x;  // heaviest (last) query tiles first
   const int h = blockIdx.y, b = blockIdx.z;
+  pdl_launch_dependents();
+  pdl_wait();
   const int q0 = a.cu_q[b];
   const int lq = a.cu_q[b + 1] - q0;
   if (qt * kRows >= lq) return;
@@ -333,8 +335,7 @@ int launch_prefill(const CUtensorMap& qm, const CUtensorMap& km, const CUtensorM
   int rc = ensure_dynamic_smem(reinterpret_cast<const void*>(&prefill_kernel), smem);
   if (rc != NVK_OK) return rc;
   const dim3 grid((max_q_len + kRows - 1) / kRows, a.num_heads, batch);
-  prefill_kernel<<<grid, kThreads, smem, stream>>>(qm, km, vm, a);
-  return check_cuda(cudaGetLastError(), "prefill launch");
+  return check_cuda(launch_pdl(prefill_kernel, grid, dim3(kThreads), smem, stream, qm, km, vm, a), "prefill launch");
 }
 
 int check_common(const void* out, const void* query, int batch, int total_q, int max_q_len, int num_heads,

@@ -11,8 +11,8 @@ What changes on CUDA: ``context_lens`` lives in a static DEVICE buffer that the
 decode kernel reads, so a replay needs no per-layer "task update" (the
 reference re-issues every paged-attention task before each replay,
 :221-247). ``updates`` therefore counts the metadata refreshes done before a
-replay. The split-K workspace and split policy are fixed per entry at capture
-time (the reference's per-task workspace, :229-242).
+replay. The decode workspace is fixed per entry at capture time (the
+reference's per-task workspace, :229-242).
 """
 
 from __future__ import annotations
@@ -39,7 +39,6 @@ class PagedAttentionGraphTask:
     context_lens: torch.Tensor
     output: torch.Tensor
     workspace: Any
-    blocks_per_split: int = 0
 
 
 @dataclass
@@ -54,9 +53,6 @@ class DecodeGraphEntry:
     logits: torch.Tensor | None = None
     tasks: list[PagedAttentionGraphTask] = field(default_factory=list)
     workspace: torch.Tensor | None = None
-    blocks_per_split: int | None = None
-    max_splits: int | None = None
-    host_context_lens: torch.Tensor | None = None
 
     def copy_inputs(self, input_ids: torch.Tensor, position_ids: torch.Tensor, attn_metadata) -> None:
         self.input_ids.copy_(input_ids)
@@ -65,28 +61,15 @@ class DecodeGraphEntry:
         self.context_lens.copy_(attn_metadata.context_lens)
         self.slot_mapping.copy_(attn_metadata.slot_mapping)
 
-    def decode_plan(self, attn, block_size: int, block_tables: torch.Tensor,
-                    context_lens: torch.Tensor) -> tuple[int, int, torch.Tensor]:
-        """Split policy + workspace of this entry; fixed at the first (eager)
-        warm-up call so that the captured kernels and later replays agree."""
-        from . import ops
-
-        width = block_tables.shape[1]
-        if self.blocks_per_split is None:
-            host_ctx = self.host_context_lens if self.host_context_lens is not None else context_lens
-            bps, _ = attn.split_policy(block_tables.device, self.batch_size, block_size, block_tables,
-                                       host_ctx.cpu() if host_ctx.is_cuda else host_ctx)
-            self.blocks_per_split = bps
-        bps = self.blocks_per_split
-        max_splits = math.ceil(width / bps)
-        self.max_splits = max(self.max_splits or 0, max_splits)
-        need = ops.decode_workspace_bytes(self.batch_size, attn.num_heads, attn.num_key_value_heads, attn.head_dim,
-                                          self.max_splits)
+    def decode_workspace(self, attn) -> torch.Tensor:
+        """This entry's decode workspace, sized and zeroed by the eager warm-up
+        run before capture so that captured kernels and replays share it."""
+        need = attn.workspace_bytes(self.batch_size)
         if self.workspace is None or self.workspace.numel() < need:
             if torch.cuda.is_current_stream_capturing():
                 raise RuntimeError("decode workspace must be sized by the warm-up run before capture")
-            self.workspace = torch.zeros(need, dtype=torch.uint8, device=block_tables.device)
-        return bps, max_splits, self.workspace
+            self.workspace = torch.zeros(need, dtype=torch.uint8, device=self.block_tables.device)
+        return self.workspace
 
 
 class DecodeGraphStats:
@@ -221,7 +204,6 @@ class DecodeGraphRunner:
                 context_lens=ctx_dev.clone(),
                 slot_mapping=attn_metadata.slot_mapping.clone(),
                 graph=graph,
-                host_context_lens=attn_metadata.context_lens,
             )
             static_md = self._static_metadata(entry, attn_metadata)
             self._synchronize()

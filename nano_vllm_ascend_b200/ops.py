@@ -8,7 +8,6 @@ here computes on the host: there is no non-CUDA path.
 from __future__ import annotations
 
 import ctypes
-import math
 
 import torch
 
@@ -80,35 +79,12 @@ def kv_append(
 
 
 # ----------------------------------------------------------------- decode ---
-def decode_workspace_bytes(batch: int, num_heads: int, num_kv_heads: int, head_dim: int, max_splits: int) -> int:
+def decode_workspace_bytes(batch: int, num_heads: int, num_kv_heads: int, head_dim: int, num_ctas: int = 0) -> int:
+    """Workspace bytes of paged_decode (num_ctas 0 = one CTA per SM of the current device)."""
     out = ctypes.c_size_t(0)
-    _lib.call("nvk_paged_decode_workspace_size", batch, num_heads, num_kv_heads, head_dim, max_splits,
+    _lib.call("nvk_paged_decode_workspace_size", batch, num_heads, num_kv_heads, head_dim, num_ctas,
               ctypes.byref(out))
     return int(out.value)
-
-
-def choose_blocks_per_split(
-    num_kv_heads: int,
-    max_blocks_per_seq: int,
-    total_blocks: int | None,
-    batch: int,
-    num_sms: int = 148,
-    ctas_per_sm: int = 2,
-    waves: int = 4,
-    max_blocks_per_cta: int = 16,
-) -> int:
-    """Picks how many pool blocks one decode CTA walks.
-
-    Aims for at least ``waves`` full waves of CTAs (so the tail wave is short)
-    while capping one CTA's work, which bounds the load imbalance at the end
-    of the grid. ``total_blocks`` is the sum of ceil(ctx/bs) over the batch
-    when known (CPU context lengths), else half the table width per sequence.
-    """
-    if total_blocks is None:
-        total_blocks = max(1, batch * max(1, max_blocks_per_seq // 2))
-    target = num_sms * ctas_per_sm * waves
-    bps = math.ceil(num_kv_heads * total_blocks / target)
-    return int(max(1, min(bps, max_blocks_per_cta, max(1, max_blocks_per_seq))))
 
 
 def paged_decode(
@@ -120,10 +96,13 @@ def paged_decode(
     context_lens: torch.Tensor,
     scale: float,
     workspace: torch.Tensor,
-    blocks_per_split: int,
-    max_splits: int | None = None,
+    num_ctas: int = 0,
 ) -> torch.Tensor:
-    """Paged GQA decode attention into ``out`` ([B, H, D] bf16)."""
+    """Paged GQA decode attention into ``out`` ([B, H, D] bf16).
+
+    ``workspace`` (uint8, zeroed once) must hold decode_workspace_bytes(B, H,
+    KVH, D, num_ctas); calls sharing it must be ordered on one stream.
+    """
     dev = query.device
     for name, t in (("out", out), ("query", query), ("key_cache", key_cache), ("value_cache", value_cache),
                     ("block_tables", block_tables), ("context_lens", context_lens), ("workspace", workspace)):
@@ -142,13 +121,10 @@ def paged_decode(
         raise ValueError("paged_decode: block_tables must be int32 [batch, max_blocks] with unit column stride")
     if context_lens.dtype != torch.int32 or context_lens.numel() != batch or not context_lens.is_contiguous():
         raise ValueError("paged_decode: context_lens must be a contiguous int32 [batch] device tensor")
-    width = block_tables.shape[1]
-    if max_splits is None:
-        max_splits = math.ceil(width / blocks_per_split)
     _lib.call(
         "nvk_paged_decode", _ptr(out), _ptr(query), _ptr(key_cache), _ptr(value_cache), num_blocks, block_size,
-        _ptr(block_tables), block_tables.stride(0), width, _ptr(context_lens), batch, num_heads, kvh, head_dim,
-        float(scale), blocks_per_split, max_splits, _ptr(workspace), workspace.numel() * workspace.element_size(),
+        _ptr(block_tables), block_tables.stride(0), block_tables.shape[1], _ptr(context_lens), batch, num_heads,
+        kvh, head_dim, float(scale), int(num_ctas), _ptr(workspace), workspace.numel() * workspace.element_size(),
         _stream(dev),
     )
     return out

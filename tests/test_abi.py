@@ -46,30 +46,31 @@ def test_library_exports_every_declared_symbol():
 
 def test_version_and_error_string():
     lib = _lib.load()
-    assert lib.nvk_abi_version() == 1
+    assert lib.nvk_abi_version() == 2
     assert isinstance(lib.nvk_last_error(), bytes)
 
 
 def test_host_side_validation_codes():
     lib = _lib.load()
     n = ctypes.c_void_p(0)
+    # args: out q kc vc num_blocks block_size tables stride width ctx batch H KVH D scale ctas ws bytes stream
     # unsupported head_dim -> NVK_ERR_UNSUPPORTED with a message
-    rc = lib.nvk_paged_decode(n, n, n, n, 8, 128, n, 4, 4, n, 2, 16, 8, 64, 0.1, 1, 4, n, 0, n)
+    rc = lib.nvk_paged_decode(n, n, n, n, 8, 128, n, 4, 4, n, 2, 16, 8, 64, 0.1, 0, n, 0, n)
     assert rc == _lib.NVK_ERR_UNSUPPORTED and b"head_dim" in lib.nvk_last_error()
     # GQA ratio 3 unsupported
-    rc = lib.nvk_paged_decode(n, n, n, n, 8, 128, n, 4, 4, n, 2, 24, 8, 128, 0.1, 1, 4, n, 0, n)
+    rc = lib.nvk_paged_decode(n, n, n, n, 8, 128, n, 4, 4, n, 2, 24, 8, 128, 0.1, 0, n, 0, n)
     assert rc == _lib.NVK_ERR_UNSUPPORTED
     # block size not a power of two
-    rc = lib.nvk_paged_decode(n, n, n, n, 8, 96, n, 4, 4, n, 2, 16, 8, 128, 0.1, 1, 4, n, 0, n)
+    rc = lib.nvk_paged_decode(n, n, n, n, 8, 96, n, 4, 4, n, 2, 16, 8, 128, 0.1, 0, n, 0, n)
     assert rc == _lib.NVK_ERR_UNSUPPORTED and b"block_size" in lib.nvk_last_error()
-    # too few splits for the table width
-    rc = lib.nvk_paged_decode(n, n, n, n, 8, 128, n, 8, 8, n, 2, 16, 8, 128, 0.1, 2, 3, n, 0, n)
-    assert rc == _lib.NVK_ERR_INVALID_ARGUMENT and b"max_splits" in lib.nvk_last_error()
+    # table stride narrower than the table
+    rc = lib.nvk_paged_decode(n, n, n, n, 8, 128, n, 2, 4, n, 2, 16, 8, 128, 0.1, 0, n, 0, n)
+    assert rc == _lib.NVK_ERR_INVALID_ARGUMENT
     # null pointers are rejected before any launch
-    rc = lib.nvk_paged_decode(n, n, n, n, 8, 128, n, 4, 4, n, 2, 16, 8, 128, 0.1, 1, 4, n, 0, n)
+    rc = lib.nvk_paged_decode(n, n, n, n, 8, 128, n, 4, 4, n, 2, 16, 8, 128, 0.1, 0, n, 0, n)
     assert rc == _lib.NVK_ERR_INVALID_ARGUMENT
     # batch 0 is a no-op
-    rc = lib.nvk_paged_decode(n, n, n, n, 8, 128, n, 4, 4, n, 0, 16, 8, 128, 0.1, 1, 4, n, 0, n)
+    rc = lib.nvk_paged_decode(n, n, n, n, 8, 128, n, 4, 4, n, 0, 16, 8, 128, 0.1, 0, n, 0, n)
     assert rc == _lib.NVK_OK
     # append: row not a multiple of 16 bytes, zero tokens is a no-op
     rc = lib.nvk_kv_append(n, n, 3, 3, n, n, n, 1, 8, 1, 3, n, n)
@@ -77,18 +78,25 @@ def test_host_side_validation_codes():
     assert lib.nvk_kv_append(n, n, 1024, 1024, n, n, n, 0, 8, 8, 128, n, n) == _lib.NVK_OK
     rc = lib.nvk_kv_append(n, n, 1024, 1024, n, n, n, 4, 8, 8, 128, n, n)
     assert rc == _lib.NVK_ERR_INVALID_ARGUMENT
+    # prefill: block size other than 128 and head_dim other than 128
+    rc = lib.nvk_paged_prefill(n, n, n, n, 8, 64, n, 4, n, n, 1, 8, 8, 16, 8, 128, 0.1, n, n)
+    assert rc == _lib.NVK_ERR_INVALID_ARGUMENT  # null q/out checked first
+    rc = lib.nvk_dense_prefill(n, n, n, n, n, n, 1, 8, 8, 8, 16, 8, 64, 0.1, n, n)
+    assert rc == _lib.NVK_ERR_UNSUPPORTED
 
 
-def test_workspace_size_is_monotone():
+def test_workspace_size_grows_with_grid_and_batch():
     sz = ctypes.c_size_t()
     lib = _lib.load()
     sizes = []
-    for splits in (1, 2, 8):
-        assert lib.nvk_paged_decode_workspace_size(32, 16, 8, 128, splits, ctypes.byref(sz)) == 0
+    for ctas in (1, 148, 296):
+        assert lib.nvk_paged_decode_workspace_size(32, 16, 8, 128, ctas, ctypes.byref(sz)) == 0
         sizes.append(sz.value)
     assert sizes[0] < sizes[1] < sizes[2]
-    # 32 seqs x 8 kv heads x 8 splits x 2 q heads x 128 floats is the bulk
-    assert sizes[2] >= 32 * 8 * 8 * 2 * 128 * 4
+    # 148 CTAs x 2 partial slots x 2 query heads x 128 floats is the bulk
+    assert sizes[1] >= 148 * 2 * 2 * 128 * 4
+    assert lib.nvk_paged_decode_workspace_size(1024, 16, 8, 128, 148, ctypes.byref(sz)) == 0
+    assert sz.value >= 1024 * 8 * 4
     assert lib.nvk_paged_decode_workspace_size(32, 16, 8, 64, 1, ctypes.byref(sz)) == _lib.NVK_ERR_UNSUPPORTED
 
 

@@ -4,13 +4,13 @@
   and vs the oracle on strided / ragged inputs;
 * decode: within max-abs 2e-2 / max-rel 1e-2 of the fp32 oracle over GQA
   ratios 1/2/4/8, block sizes 16..256, ragged and edge context lengths
-  (0, 1, block-1, block, block+1, long), 1..many splits, repeated calls on one
+  (0, 1, block-1, block, block+1, long), persistent grids from 1 CTA to more
+  CTAs than tiles (pairs split across CTAs and merged), repeated calls on one
   workspace, and CUDA-graph replay with new inputs.
 """
 
 import hashlib
 import json
-import math
 from pathlib import Path
 
 import numpy as np
@@ -80,7 +80,7 @@ def test_append_out_of_range_slot_is_skipped_and_flagged(cuda_device):
 
 
 # ----------------------------------------------------------------- decode ---
-def run_decode(cuda_device, ctx, h=16, kvh=8, bs=128, nb=None, seed=0, bps=None, width=None, q_scale=1.0):
+def run_decode(cuda_device, ctx, h=16, kvh=8, bs=128, nb=None, seed=0, num_ctas=0, width=None, q_scale=1.0):
     need = sum((n + bs - 1) // bs for n in ctx)
     nb = nb or max(need + 3, 4)
     kc, vc = random_pool(nb, bs, kvh, 128, cuda_device, seed)
@@ -89,12 +89,10 @@ def run_decode(cuda_device, ctx, h=16, kvh=8, bs=128, nb=None, seed=0, bps=None,
     q = (torch.randn(len(ctx), h, 128, generator=g, device=cuda_device) * q_scale).to(torch.bfloat16)
     ctx_t = torch.tensor(ctx, dtype=torch.int32, device=cuda_device)
     scale = 128 ** -0.5
-    bps = bps or ops.choose_blocks_per_split(kvh, tables.shape[1], need, len(ctx))
-    splits = math.ceil(tables.shape[1] / bps)
-    ws = torch.zeros(ops.decode_workspace_bytes(len(ctx), h, kvh, 128, splits), dtype=torch.uint8,
+    ws = torch.zeros(ops.decode_workspace_bytes(len(ctx), h, kvh, 128, num_ctas), dtype=torch.uint8,
                      device=cuda_device)
-    out = torch.empty_like(q)
-    ops.paged_decode(out, q, kc, vc, tables, ctx_t, scale, ws, bps)
+    out = torch.full_like(q, float("nan"))
+    ops.paged_decode(out, q, kc, vc, tables, ctx_t, scale, ws, num_ctas)
     torch.cuda.synchronize()
     assert ops.decode_error_word(ws) == 0
     want = orc.paged_decode(bits(q), bits(kc), bits(vc), tables.cpu().numpy(), np.array(ctx), scale)
@@ -120,11 +118,26 @@ def test_decode_block_sizes(cuda_device, bs):
     assert_close(got, want, f"bs={bs}")
 
 
-@pytest.mark.parametrize("bps", [1, 2, 3, 16, 64])
-def test_decode_split_counts(cuda_device, bps):
+@pytest.mark.parametrize("num_ctas", [1, 3, 7, 148, 1000])
+def test_decode_persistent_grid_sizes(cuda_device, num_ctas):
+    # 1 CTA walks everything; 1000 CTAs is more CTAs than tiles (empty ranges,
+    # pairs split over many CTAs and merged by the last to finish)
     ctx = [5000, 1, 2304, 129, 4097]
-    got, want, _ = run_decode(cuda_device, ctx, seed=bps, bps=bps)
-    assert_close(got, want, f"bps={bps}")
+    got, want, _ = run_decode(cuda_device, ctx, seed=num_ctas, num_ctas=num_ctas)
+    assert_close(got, want, f"num_ctas={num_ctas}")
+
+
+def test_decode_single_long_sequence_split_over_all_sms(cuda_device):
+    got, want, _ = run_decode(cuda_device, [30000], h=32, kvh=8, seed=17)
+    assert_close(got, want, "one long sequence")
+
+
+def test_decode_large_batch_above_one_launch_chunk(cuda_device):
+    # more sequences than one launch's schedule holds (1024): chunked launches
+    rng = np.random.default_rng(5)
+    ctx = rng.integers(0, 65, size=1100).tolist()
+    got, want, _ = run_decode(cuda_device, ctx, bs=16, seed=23)
+    assert_close(got, want, "1100 sequences")
 
 
 def test_decode_zero_context_gives_zeros(cuda_device):
@@ -141,17 +154,17 @@ def test_decode_peaked_softmax_rescaling(cuda_device):
 
 def test_decode_workspace_reuse_across_calls(cuda_device):
     ctx = [3000, 10, 1500, 700]
-    got1, want1, ws = run_decode(cuda_device, ctx, seed=21, bps=2)
-    cnt = ws[256:256 + 4 * 4 * 8].view(torch.int32)
-    assert int(cnt.abs().sum()) == 0, "arrival counters must return to zero"
+    got1, want1, ws = run_decode(cuda_device, ctx, seed=21, num_ctas=6)
+    tickets = ws[256:256 + 4 * 8 * 32 * 4].view(torch.int32)  # one 128-byte line per (sequence, kv head)
+    assert int(tickets.abs().sum()) == 0, "arrival tickets must return to zero"
     assert_close(got1, want1, "first")
-    got2, want2, _ = run_decode(cuda_device, ctx, seed=22, bps=2)
+    got2, want2, _ = run_decode(cuda_device, ctx, seed=22, num_ctas=6)
     assert_close(got2, want2, "second")
 
 
 def test_decode_wide_padded_table(cuda_device):
     # graph-style static table: much wider than any context
-    got, want, _ = run_decode(cuda_device, [130, 9], width=64, bps=4, seed=4)
+    got, want, _ = run_decode(cuda_device, [130, 9], width=64, seed=4)
     assert_close(got, want, "wide table")
 
 
@@ -159,16 +172,16 @@ def test_decode_under_cuda_graph_replay(cuda_device):
     bs, kvh, h, nb = 128, 8, 16, 80
     kc, vc = random_pool(nb, bs, kvh, 128, cuda_device, 31)
     width = 16
-    ws = torch.zeros(ops.decode_workspace_bytes(4, h, kvh, 128, 8), dtype=torch.uint8, device=cuda_device)
+    ws = torch.zeros(ops.decode_workspace_bytes(4, h, kvh, 128), dtype=torch.uint8, device=cuda_device)
     q = torch.zeros(4, h, 128, dtype=torch.bfloat16, device=cuda_device)
     tables = torch.zeros(4, width, dtype=torch.int32, device=cuda_device)
     ctx = torch.ones(4, dtype=torch.int32, device=cuda_device)
     out = torch.empty_like(q)
-    ops.paged_decode(out, q, kc, vc, tables, ctx, 128 ** -0.5, ws, 2)  # warm-up
+    ops.paged_decode(out, q, kc, vc, tables, ctx, 128 ** -0.5, ws)  # warm-up
     torch.cuda.synchronize()
     graph = torch.cuda.CUDAGraph()
     with torch.cuda.graph(graph):
-        ops.paged_decode(out, q, kc, vc, tables, ctx, 128 ** -0.5, ws, 2)
+        ops.paged_decode(out, q, kc, vc, tables, ctx, 128 ** -0.5, ws)
     for seed, lens in ((1, [100, 2000, 1, 640]), (2, [1999, 5, 1024, 129])):
         g = torch.Generator(device=cuda_device).manual_seed(seed)
         q.copy_(torch.randn(4, h, 128, generator=g, device=cuda_device).to(torch.bfloat16))
