@@ -19,11 +19,15 @@
 //    into a zero-padded 16-row operand; per tile, TMA loads of the K and V
 //    tile (box {64 dims, 1 head, <=32 tokens}, 128-byte swizzle, only the
 //    sub-boxes that hold context tokens) into a 3-stage ring.
-//  * warp 5 (MMA): S^T[128 tok x 16] = K[128 x 128] . Qpad^T (A and B
-//    K-major) and O^T[128 dims x 16] += V^T . P^T (A = the V tile read
-//    MN-major, B = P^T K-major): M=128 N=16 K=16 UMMAs with f32 accumulators
-//    in TMEM (S double buffered, O and the query operand four deep, so short
-//    segments do not wait on each other), completion via tcgen05.commit.
+//  * warps 5 and 10 (MMA issuers, one elected thread each): warp 5 issues
+//    S^T[128 tok x 16] = K[128 x 128] . Qpad^T (A and B K-major), warp 10
+//    O^T[128 dims x 16] += V^T . P^T (A = the V tile read MN-major, B = P^T
+//    K-major): M=128 N=16 K=16 UMMAs with f32 accumulators in TMEM (S double
+//    buffered, O and the query operand four deep, so short segments do not
+//    wait on each other), completion via tcgen05.commit. Two issuers keep the
+//    S of later tiles flowing while PV waits for the softmax; the producer
+//    publishes each tile's segment facts beside its K/V stage, so neither
+//    issuer walks the schedule.
 //  * warps 0-3 (softmax): thread t owns token t of S^T (and dim t of O^T).
 //    Base-2 online softmax per query head with lazy rescaling (the reference
 //    max moves only when a tile max exceeds it by more than 2^8); the tile
@@ -52,15 +56,19 @@ constexpr int kQBytes = 2 * kQHalf;
 constexpr int kMaxSeqs = 1024;      // sequences per launch (tile prefix in smem)
 constexpr int kSoftmaxThreads = 128;
 constexpr int kProducerWarp = 4;
-constexpr int kMmaWarp = 5;
+constexpr int kMmaWarp = 5;                 // issues S = K Q^T
 constexpr int kEpilogueWarp0 = 6;           // warps 6-9: one per TMEM lane quarter
 constexpr int kEpilogueThreads = 128;
-constexpr int kThreads = 10 * 32;
+constexpr int kPvWarp = 10;                 // issues O += V^T P^T
+constexpr int kSchedWarp = 11;              // walks the schedule, stages block ids, loads queries
+constexpr int kThreads = 12 * 32;
 constexpr int kQBufs = 4;           // query operands in flight (one per segment)
 constexpr int kOBufs = 4;           // O accumulators in flight (one per segment)
 constexpr uint32_t kTmemCols = 128; // S: 0-31 (2 x 16), O: 32-95 (4 x 16)
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
-constexpr int kChunkTiles = 32;            // tiles whose block ids the producer stages at once
+constexpr int kChunkTiles = 32;            // most tiles per staged chunk of block ids
+constexpr int kRingSlots = 4;              // staged chunks in flight between scheduler and producer
+constexpr int kSlotIds = 64;               // block ids per chunk
 constexpr int kMaxMergePieces = 32;        // pieces staged per merge pass
 constexpr int kTicketStride = 32;          // ints: one 128-byte line per ticket (no shared lines)
 
@@ -79,10 +87,29 @@ struct DecodeArgs {
   int block_size;
   int log2_bs;
   int sub_rows;
+  int chunk_tiles;  // tiles per chunk: every chunk's block ids fit in kSlotIds
   int num_heads;
   int num_kv_heads;
   int qpk;
   float scale_log2;
+};
+
+// What the producer knows about the tile in a K/V stage, published with the
+// stage's TMA transaction (written before the arrive that sets its byte count,
+// read after a wait on that barrier) so that no other role walks segments.
+enum TileFlags : int { kFirstTile = 1, kLastTile = 2 };
+struct TileInfo {
+  int seg;     // segment ordinal within this CTA
+  int flags;   // kFirstTile / kLastTile of the segment
+  int nvalid;  // context tokens in the tile (1..128)
+  int b, g, n, ntiles, pair_t0, slot;
+};
+
+// One chunk of a segment (at most chunk_tiles tiles), staged by the scheduler
+// warp for the producer: where it lies and its block ids. nt == 0 ends the walk.
+struct Chunk {
+  int seg, b, g, len, i, nt, seg_i0, seg_ntiles, n, pair_t0, slot, blk0;
+  int ids[kSlotIds];
 };
 
 struct Smem {
@@ -92,10 +119,12 @@ struct Smem {
   alignas(1024) uint8_t p[2][kQBytes];
   int tiles_before[kMaxSeqs + 1];
   uint8_t last_rows[kMaxSeqs];           // context tokens in each sequence's last tile (1..128)
-  int blocks[kChunkTiles * kTile / 16];  // block ids of up to kChunkTiles tiles
+  Chunk ring[kRingSlots];
+  uint64_t ring_full[kRingSlots], ring_empty[kRingSlots];
   float red[2][4][8];
   int warp_ok[2][4];
   int resc_ok[4];  // rescale-path exchange (its own slot: warp_ok[] belongs to the tile)
+  TileInfo info[kStages];
   uint64_t full_k[kStages], full_v[kStages], kv_empty[kStages];
   uint64_t q_full[kQBufs], q_empty[kQBufs];
   uint64_t s_full[2], s_free[2], p_full[2], pv_done[2];
@@ -454,7 +483,11 @@ __global__ void __launch_bounds__(kThreads, 1) paged_decode_kernel(const __grid_
       mbar_init(&sm.o_empty[i], kEpilogueThreads);
       mbar_init(&sm.seg_ready[i], kSoftmaxThreads);
     }
-    mbar_init(&sm.fin, 1);
+    for (int i = 0; i < kRingSlots; ++i) {
+      mbar_init(&sm.ring_full[i], 32);  // every scheduler lane, after its own id stores
+      mbar_init(&sm.ring_empty[i], 1);
+    }
+    mbar_init(&sm.fin, 2);  // one commit from each MMA-issuing thread
     sm.abort = 0;
     sm.pend_n[0] = sm.pend_n[1] = 0;
     fence_mbar_init();
@@ -509,20 +542,22 @@ __global__ void __launch_bounds__(kThreads, 1) paged_decode_kernel(const __grid_
   const int hi = total > 0 ? range_lo(c + 1, sc) : 0;
   const uint32_t tmem = sm.tmem_base;
 
-  if (warp == kProducerWarp) {
-    // -------------------------------------------------------- producer ----
-    // The warp stages the block ids of up to kChunkTiles tiles in smem (one
-    // parallel round of loads), then lane 0 issues their TMA copies.
-    if (lane == 0) {
-      tma_prefetch_desc(&kmap);
-      tma_prefetch_desc(&vmap);
-      tma_prefetch_desc(&qmap);
-    }
-    int j = 0, seg = 0;
+  if (warp == kSchedWarp) {
+    // ------------------------------------------------------- scheduler ----
+    // Walks this CTA's segments ahead of the producer: per segment the TMA
+    // load of the group's query rows; per chunk of tiles, one parallel round
+    // of block-id loads into a ring slot. The producer then only issues K/V
+    // copies, so no segment start waits on a global round trip.
+    if (lane == 0) tma_prefetch_desc(&qmap);
+    int chunk = 0, seg = 0;
     bool ok = true;
     SegIter it;
     it.init(sm, a, lo, hi);
     Segment s;
+    auto claim = [&](int ch) -> bool {  // ring slot of chunk ch is free
+      if (ch < kRingSlots) return true;
+      return __all_sync(0xffffffffu, mbar_wait(&sm.ring_empty[ch % kRingSlots], ((ch / kRingSlots) - 1) & 1));
+    };
     for (; ok && it.next(sm, a, s); ++seg) {
       const int qb = seg % kQBufs;
       if (lane == 0) {
@@ -535,88 +570,137 @@ __global__ void __launch_bounds__(kThreads, 1) paged_decode_kernel(const __grid_
       }
       ok = __shfl_sync(0xffffffffu, ok, 0);
       const int32_t* bt = a.block_tables + static_cast<int64_t>(s.b) * a.bt_stride;
-      for (int i = s.i0; ok && i < s.i0 + s.ntiles; i += kChunkTiles) {
-        const int nt = min(kChunkTiles, s.i0 + s.ntiles - i);
+      for (int i = s.i0; ok && i < s.i0 + s.ntiles; i += a.chunk_tiles, ++chunk) {
+        if (!claim(chunk)) {
+          ok = false;
+          break;
+        }
+        Chunk& ck = sm.ring[chunk % kRingSlots];
+        const int nt = min(a.chunk_tiles, s.i0 + s.ntiles - i);
         const int blk0 = (i * kTile) >> a.log2_bs;
-        const int blk1 = (min((i + nt) * kTile, s.len) - 1) >> a.log2_bs;  // inclusive
+        const int blk1 = (min((i + nt) * kTile, s.len) - 1) >> a.log2_bs;  // inclusive, blk1 - blk0 < kSlotIds
         for (int k = lane; k <= blk1 - blk0; k += 32) {
           int blk = bt[blk0 + k];
           if (blk < 0 || blk >= a.num_blocks) {
             atomicOr(a.err, kErrBadBlockId);
             blk = a.num_blocks;  // fully outside the tensor map: zero fill
           }
-          sm.blocks[k] = blk;
+          ck.ids[k] = blk;
         }
-        __syncwarp();
         if (lane == 0) {
-          for (int ii = i; ii < i + nt; ++ii, ++j) {
-            const int st = j % kStages;
-            if (j >= kStages && !mbar_wait(&sm.kv_empty[st], ((j / kStages) - 1) & 1)) {
-              ok = false;
-              break;
-            }
-            const int tok0 = ii * kTile;
-            const int nvalid = min(kTile, s.len - tok0);
-            const int nsub = (nvalid + a.sub_rows - 1) / a.sub_rows;
-            const uint32_t bytes = static_cast<uint32_t>(nsub * a.sub_rows * 128 * 2);
-            mbar_arrive_expect_tx(&sm.full_k[st], bytes);
-            mbar_arrive_expect_tx(&sm.full_v[st], bytes);
-            for (int u = 0; u < nsub; ++u) {
-              const int tok = tok0 + u * a.sub_rows;
-              const int blk = sm.blocks[(tok >> a.log2_bs) - blk0];
-              const int row = blk * a.block_size + (tok & (a.block_size - 1));
-              const int off = u * a.sub_rows * 128;
-              tma_load_3d(sm.k[st] + off, &kmap, &sm.full_k[st], 0, s.g, row);
-              tma_load_3d(sm.k[st] + kHalf + off, &kmap, &sm.full_k[st], 64, s.g, row);
-              tma_load_3d(sm.v[st] + off, &vmap, &sm.full_v[st], 0, s.g, row);
-              tma_load_3d(sm.v[st] + kHalf + off, &vmap, &sm.full_v[st], 64, s.g, row);
-            }
-          }
+          ck.seg = seg;
+          ck.b = s.b;
+          ck.g = s.g;
+          ck.len = s.len;
+          ck.i = i;
+          ck.nt = nt;
+          ck.seg_i0 = s.i0;
+          ck.seg_ntiles = s.ntiles;
+          ck.n = s.n;
+          ck.pair_t0 = s.pair_t0;
+          ck.slot = (s.start == lo) ? 0 : 1;
+          ck.blk0 = blk0;
         }
-        ok = __shfl_sync(0xffffffffu, ok, 0);
-        j = __shfl_sync(0xffffffffu, j, 0);
-        __syncwarp();  // sm.blocks is rewritten by the next chunk
+        mbar_arrive(&sm.ring_full[chunk % kRingSlots]);
       }
     }
+    // End marker (skipped when a wait failed: the producer's own wait then
+    // runs out and it stops too).
+    if (ok && claim(chunk)) {
+      if (lane == 0) sm.ring[chunk % kRingSlots].nt = 0;
+      mbar_arrive(&sm.ring_full[chunk % kRingSlots]);
+    }
     if (lane == 0) {
+      if (!ok) flag_error(a, sm, kErrWaitTimeout);
+      // Drain: every query copy lands before the CTA may exit.
+      for (int sg = max(0, seg - kQBufs); sg < seg; ++sg) (void)mbar_wait(&sm.q_full[sg % kQBufs], (sg / kQBufs) & 1);
+    }
+  } else if (warp == kProducerWarp) {
+    // -------------------------------------------------------- producer ----
+    // Lane 0 turns each staged chunk into K and V tile copies (one per
+    // sub-box holding context tokens) and publishes each tile's segment
+    // facts with its stage.
+    if (lane == 0) {
+      tma_prefetch_desc(&kmap);
+      tma_prefetch_desc(&vmap);
+      int j = 0;
+      bool ok = true;
+      for (int chunk = 0; ok; ++chunk) {
+        const int rs = chunk % kRingSlots;
+        if (!mbar_wait(&sm.ring_full[rs], (chunk / kRingSlots) & 1)) {
+          ok = false;
+          break;
+        }
+        const Chunk& ck = sm.ring[rs];
+        const int nt = ck.nt;
+        if (nt == 0) break;
+        const int seg = ck.seg, b = ck.b, g = ck.g, len = ck.len, seg_i0 = ck.seg_i0, seg_last = ck.seg_i0 + ck.seg_ntiles - 1;
+        const int blk0 = ck.blk0;
+        for (int ii = ck.i; ii < ck.i + nt; ++ii, ++j) {
+          const int st = j % kStages;
+          if (j >= kStages && !mbar_wait(&sm.kv_empty[st], ((j / kStages) - 1) & 1)) {
+            ok = false;
+            break;
+          }
+          const int tok0 = ii * kTile;
+          const int nvalid = min(kTile, len - tok0);
+          const int nsub = (nvalid + a.sub_rows - 1) / a.sub_rows;
+          const uint32_t bytes = static_cast<uint32_t>(nsub * a.sub_rows * 128 * 2);
+          TileInfo& ti = sm.info[st];
+          ti.seg = seg;
+          ti.flags = (ii == seg_i0 ? kFirstTile : 0) | (ii == seg_last ? kLastTile : 0);
+          ti.nvalid = nvalid;
+          ti.b = b;
+          ti.g = g;
+          ti.n = ck.n;
+          ti.ntiles = ck.seg_ntiles;
+          ti.pair_t0 = ck.pair_t0;
+          ti.slot = ck.slot;
+          mbar_arrive_expect_tx(&sm.full_k[st], bytes);
+          mbar_arrive_expect_tx(&sm.full_v[st], bytes);
+          for (int u = 0; u < nsub; ++u) {
+            const int tok = tok0 + u * a.sub_rows;
+            const int blk = ck.ids[(tok >> a.log2_bs) - blk0];
+            const int row = blk * a.block_size + (tok & (a.block_size - 1));
+            const int off = u * a.sub_rows * 128;
+            tma_load_3d(sm.k[st] + off, &kmap, &sm.full_k[st], 0, g, row);
+            tma_load_3d(sm.k[st] + kHalf + off, &kmap, &sm.full_k[st], 64, g, row);
+            tma_load_3d(sm.v[st] + off, &vmap, &sm.full_v[st], 0, g, row);
+            tma_load_3d(sm.v[st] + kHalf + off, &vmap, &sm.full_v[st], 64, g, row);
+          }
+        }
+        mbar_arrive(&sm.ring_empty[rs]);  // the chunk's ids are no longer read
+      }
       if (!ok) flag_error(a, sm, kErrWaitTimeout);
       // Drain: every copy this CTA issued lands before the CTA may exit.
       for (int jj = max(0, j - kStages); jj < j; ++jj) {
         (void)mbar_wait(&sm.full_k[jj % kStages], (jj / kStages) & 1);
         (void)mbar_wait(&sm.full_v[jj % kStages], (jj / kStages) & 1);
       }
-      for (int sg = max(0, seg - kQBufs); sg < seg; ++sg) (void)mbar_wait(&sm.q_full[sg % kQBufs], (sg / kQBufs) & 1);
     }
   } else if (warp == kMmaWarp) {
-    // ------------------------------------------------------------- MMA ----
-    // S(j+1) = K Q^T is issued before PV(j), so the softmax of tile j+1 can
-    // start as soon as tile j's probabilities are out.
+    // -------------------------------------------------------- MMA: S ----
+    // S^T(j) = K(j) Qpad^T into S buffer j % 2, as soon as K(j) has landed and
+    // the softmax has read S(j-2). Runs ahead of the PV issuer.
     if (lane == 0) {
-      constexpr uint32_t idesc_s = umma_idesc_bf16(kTile, kN, false);           // A = K, B = Qpad
-      constexpr uint32_t idesc_o = umma_idesc_bf16(kD, kN, false) | (1u << 15);  // A = V^T (MN-major), B = P^T
+      constexpr uint32_t idesc_s = umma_idesc_bf16(kTile, kN, false);  // A = K, B = Qpad
       bool ok = true;
-      // Walk of the S side (one tile ahead) and of the PV side.
-      int js = 0, segs = 0, i_s = 0, left_s = 0;
-      Segment cur_s{};
-      SegIter it_s, it_p;
-      it_s.init(sm, a, lo, hi);
-      it_p.init(sm, a, lo, hi);
-      int jp = 0, segp = 0, left_p = 0;
-      Segment cur_p{};
-      auto issue_s = [&]() -> bool {  // S for the next tile of the S walk
-        if (left_s == 0) {
-          it_s.next(sm, a, cur_s);
-          left_s = cur_s.ntiles;
-          i_s = 0;
-          if (!mbar_wait(&sm.q_full[segs % kQBufs], (segs / kQBufs) & 1)) return false;
-          ++segs;
+      for (int j = 0; j < hi - lo; ++j) {
+        const int st = j % kStages, sb = j & 1;
+        if (!mbar_wait(&sm.full_k[st], (j / kStages) & 1)) {
+          ok = false;
+          break;
         }
-        const int st = js % kStages, sb = js & 1;
-        if (!mbar_wait(&sm.full_k[st], (js / kStages) & 1)) return false;
-        if (js >= 2 && !mbar_wait(&sm.s_free[sb], ((js >> 1) - 1) & 1)) return false;
+        const int seg = sm.info[st].seg, flags = sm.info[st].flags;
+        const int qb = seg % kQBufs;
+        if (((flags & kFirstTile) && !mbar_wait(&sm.q_full[qb], (seg / kQBufs) & 1)) ||
+            (j >= 2 && !mbar_wait(&sm.s_free[sb], ((j >> 1) - 1) & 1))) {
+          ok = false;
+          break;
+        }
         tc_fence_after();
         const uint32_t k_addr = smem_u32(sm.k[st]);
-        const uint32_t q_addr = smem_u32(sm.q[(segs - 1) % kQBufs]);
+        const uint32_t q_addr = smem_u32(sm.q[qb]);
 #pragma unroll
         for (int kk = 0; kk < kD / 16; ++kk) {
           const uint32_t koff = (kk >> 2) * kHalf + (kk & 3) * 32;
@@ -625,30 +709,28 @@ __global__ void __launch_bounds__(kThreads, 1) paged_decode_kernel(const __grid_
                       smem_desc_sw128(q_addr + qoff, 16, 1024), idesc_s, kk > 0);
         }
         umma_commit(&sm.s_full[sb]);
-        ++js;
-        ++i_s;
-        --left_s;
-        return true;
-      };
-      const int ntiles_total = hi - lo;
-      if (ntiles_total > 0) ok = issue_s();
-      for (int n = 0; ok && n < ntiles_total; ++n) {
-        if (n + 1 < ntiles_total) {
-          ok = issue_s();
-          if (!ok) break;
+        if (flags & kLastTile) umma_commit(&sm.q_empty[qb]);  // the segment's query is no longer read
+      }
+      if (!ok) flag_error(a, sm, kErrWaitTimeout);
+      umma_commit(&sm.fin);
+      (void)mbar_wait(&sm.fin, 0);  // every MMA of both issuers completes before TMEM is freed
+    }
+  } else if (warp == kPvWarp) {
+    // ------------------------------------------------------- MMA: PV ----
+    // O^T(seg) += V(j)^T P^T(j) once the softmax has written P(j). Its commit
+    // frees the K/V stage: P(j) exists only after S(j), hence K(j), is done.
+    if (lane == 0) {
+      constexpr uint32_t idesc_o = umma_idesc_bf16(kD, kN, false) | (1u << 15);  // A = V^T (MN-major), B = P^T
+      bool ok = true;
+      for (int j = 0; j < hi - lo; ++j) {
+        const int st = j % kStages, sb = j & 1;
+        if (!mbar_wait(&sm.p_full[sb], (j >> 1) & 1) || !mbar_wait(&sm.full_v[st], (j / kStages) & 1)) {
+          ok = false;
+          break;
         }
-        if (left_p == 0) {
-          it_p.next(sm, a, cur_p);
-          left_p = cur_p.ntiles;
-          if (segp >= kOBufs && !mbar_wait(&sm.o_empty[segp % kOBufs], ((segp / kOBufs) - 1) & 1)) {
-            ok = false;
-            break;
-          }
-          ++segp;
-        }
-        const int i_in_seg = cur_p.ntiles - left_p;
-        const int st = jp % kStages, sb = jp & 1, ob = (segp - 1) % kOBufs;
-        if (!mbar_wait(&sm.p_full[sb], (jp >> 1) & 1) || !mbar_wait(&sm.full_v[st], (jp / kStages) & 1)) {
+        const int seg = sm.info[st].seg, flags = sm.info[st].flags;
+        const int ob = seg % kOBufs;
+        if ((flags & kFirstTile) && seg >= kOBufs && !mbar_wait(&sm.o_empty[ob], ((seg / kOBufs) - 1) & 1)) {
           ok = false;
           break;
         }
@@ -656,128 +738,128 @@ __global__ void __launch_bounds__(kThreads, 1) paged_decode_kernel(const __grid_
         const uint32_t v_addr = smem_u32(sm.v[st]);
         const uint32_t p_addr = smem_u32(sm.p[sb]);
         const uint32_t o_tmem = tmem + 32 + ob * kN;
+        const uint32_t acc0 = (flags & kFirstTile) ? 0u : 1u;
 #pragma unroll
         for (int kk = 0; kk < kTile / 16; ++kk) {
           const uint64_t va = smem_desc_sw128(v_addr + kk * 16 * 128, kHalf, 1024);
           const uint64_t pb = smem_desc_sw128(p_addr + (kk >> 2) * kQHalf + (kk & 3) * 32, 16, 1024);
-          umma_f16_ss(o_tmem, va, pb, idesc_o, (i_in_seg > 0 || kk > 0) ? 1u : 0u);
+          umma_f16_ss(o_tmem, va, pb, idesc_o, kk > 0 ? 1u : acc0);
         }
         umma_commit(&sm.kv_empty[st]);
         umma_commit(&sm.pv_done[sb]);
-        ++jp;
-        if (--left_p == 0) {
-          umma_commit(&sm.o_full[ob]);
-          umma_commit(&sm.q_empty[(segp - 1) % kQBufs]);
-        }
+        if (flags & kLastTile) umma_commit(&sm.o_full[ob]);
       }
       if (!ok) flag_error(a, sm, kErrWaitTimeout);
-      umma_commit(&sm.fin);  // every MMA of this CTA completes before TMEM is freed
-      (void)mbar_wait(&sm.fin, 0);
+      umma_commit(&sm.fin);
     }
   } else if (warp < 4) {
     // --------------------------------------------------------- softmax ----
     const uint32_t t_lane = static_cast<uint32_t>(warp * 32) << 16;
-    int j = 0, seg = 0;
     bool all_ok = true;
-    SegIter it;
-    it.init(sm, a, lo, hi);
-    Segment s;
-    for (; all_ok && it.next(sm, a, s); ++seg) {
-      const int ob = seg % kOBufs;
+    float m_ref[QPK], l_t[QPK];
+#pragma unroll
+    for (int h = 0; h < QPK; ++h) {
+      m_ref[h] = -INFINITY;
+      l_t[h] = 0.f;
+    }
+    for (int j = 0; j < hi - lo; ++j) {
+      const int st = j % kStages, sb = j & 1, rb = j & 1;
+      // K(j) landed (and with it the tile info); S(j) ready; P buffer sb free
+      // (PV(j-2) done); V(j) landed when rows past the context must be zeroed.
+      bool ok = mbar_wait(&sm.full_k[st], (j / kStages) & 1) && mbar_wait(&sm.s_full[sb], (j >> 1) & 1);
+      if (j >= 2) ok = ok && mbar_wait(&sm.pv_done[sb], ((j - 2) >> 1) & 1);
+      TileInfo ti{};
+      if (ok) ti = sm.info[st];  // read before p_full(j): the stage is refilled only after PV(j)
+      if (ok && ti.nvalid < kTile) ok = mbar_wait(&sm.full_v[st], (j / kStages) & 1);
+      ok = __all_sync(0xffffffffu, ok);  // tcgen05.ld below needs a converged warp
+      const bool first = (ti.flags & kFirstTile) != 0;
+      const int ob = ti.seg % kOBufs;
       const uint32_t o_tmem = tmem + 32 + ob * kN + t_lane;
-      float m_ref[QPK], l_t[QPK];
+      const bool valid = tid < ti.nvalid;
+      if (first) {
+#pragma unroll
+        for (int h = 0; h < QPK; ++h) {
+          m_ref[h] = -INFINITY;
+          l_t[h] = 0.f;
+        }
+      }
+      float sv8[8];
+      float sv[QPK];
+      if (ok) {
+        tc_fence_after();
+        tmem_ld_cols(tmem + sb * kN + t_lane, QPK, sv8);
+        tc_fence_before();
+        mbar_arrive(&sm.s_free[sb]);
+      }
 #pragma unroll
       for (int h = 0; h < QPK; ++h) {
-        m_ref[h] = -INFINITY;
-        l_t[h] = 0.f;
+        sv[h] = (ok && valid) ? sv8[h] * a.scale_log2 : -INFINITY;
+        float x = sv[h];
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) x = fmaxf(x, __shfl_xor_sync(0xffffffffu, x, off));
+        if (lane == 0) sm.red[rb][warp][h] = x;
       }
-      for (int i = s.i0; i < s.i0 + s.ntiles; ++i, ++j) {
-        const int st = j % kStages, sb = j & 1, rb = j & 1;
-        const int nvalid = min(kTile, s.len - i * kTile);
-        const bool valid = tid < nvalid;
-        // S(j) ready; P buffer sb free (PV(j-2) done); V(j) landed when rows
-        // past the context must be zeroed.
-        bool ok = mbar_wait(&sm.s_full[sb], (j >> 1) & 1);
-        if (j >= 2) ok = ok && mbar_wait(&sm.pv_done[sb], ((j - 2) >> 1) & 1);
-        if (nvalid < kTile) ok = ok && mbar_wait(&sm.full_v[st], (j / kStages) & 1);
-        ok = __all_sync(0xffffffffu, ok);  // tcgen05.ld below needs a converged warp
-        float sv8[8];
-        float sv[QPK];
-        if (ok) {
-          tc_fence_after();
-          tmem_ld_cols(tmem + sb * kN + t_lane, QPK, sv8);
-          tc_fence_before();
-          mbar_arrive(&sm.s_free[sb]);
-        }
-#pragma unroll
-        for (int h = 0; h < QPK; ++h) {
-          sv[h] = (ok && valid) ? sv8[h] * a.scale_log2 : -INFINITY;
-          float x = sv[h];
-#pragma unroll
-          for (int off = 16; off > 0; off >>= 1) x = fmaxf(x, __shfl_xor_sync(0xffffffffu, x, off));
-          if (lane == 0) sm.red[rb][warp][h] = x;
-        }
-        if (lane == 0) sm.warp_ok[rb][warp] = ok;
-        named_barrier_sync(1, kSoftmaxThreads);
-        all_ok = sm.warp_ok[rb][0] && sm.warp_ok[rb][1] && sm.warp_ok[rb][2] && sm.warp_ok[rb][3];
-        if (!all_ok) break;
-        bool any_resc = false;
-        float alpha[QPK];
-#pragma unroll
-        for (int h = 0; h < QPK; ++h) {
-          const float mt = fmaxf(fmaxf(sm.red[rb][0][h], sm.red[rb][1][h]), fmaxf(sm.red[rb][2][h], sm.red[rb][3][h]));
-          alpha[h] = 1.f;
-          if (mt > m_ref[h] + kRescaleThreshold) {
-            alpha[h] = fast_exp2(m_ref[h] - mt);  // 0 when m_ref = -inf
-            m_ref[h] = mt;
-            l_t[h] *= alpha[h];
-            any_resc = true;
-          }
-        }
-        if (any_resc && i > s.i0) {
-          // O^T lane t is dim t; PV(j-1) must be complete before O changes.
-          bool okr = __all_sync(0xffffffffu, mbar_wait(&sm.pv_done[(j - 1) & 1], ((j - 1) >> 1) & 1));
-          if (lane == 0) sm.resc_ok[warp] = okr;
-          named_barrier_sync(1, kSoftmaxThreads);
-          all_ok = sm.resc_ok[0] && sm.resc_ok[1] && sm.resc_ok[2] && sm.resc_ok[3];
-          if (!all_ok) break;
-          float o[8];
-          tc_fence_after();
-          tmem_ld_cols(o_tmem, QPK, o);
-#pragma unroll
-          for (int h = 0; h < QPK; ++h) o[h] *= alpha[h];
-          tmem_st_cols(o_tmem, QPK, o);
-        }
-        if (!valid) {
-          // Rows past the context hold arbitrary bits; P is 0 there, but the
-          // tensor core still multiplies them, so they become zeros.
-          const uint32_t vrow = smem_u32(sm.v[st]) + tid * 128;
-#pragma unroll
-          for (int cc = 0; cc < 8; ++cc) {
-            st_shared_v4(vrow + cc * 16, 0, 0, 0, 0);
-            st_shared_v4(vrow + kHalf + cc * 16, 0, 0, 0, 0);
-          }
-        }
-        // P^T[h][token], K-major SW128: tokens 0-63 in the first 2 KiB half.
-        const uint32_t p_base = smem_u32(sm.p[sb]) + (tid >> 6) * kQHalf + (tid & 7) * 2;
-        const int chunk = (tid & 63) >> 3;
-#pragma unroll
-        for (int h = 0; h < QPK; ++h) {
-          const float mu = (m_ref[h] == -INFINITY) ? 0.f : m_ref[h];
-          const float p = valid ? fast_exp2(sv[h] - mu) : 0.f;
-          l_t[h] += p;
-          const __nv_bfloat16 pb = __float2bfloat16_rn(p);
-          const uint32_t addr = p_base + h * 128 + ((chunk ^ (h & 7)) << 4);
-          asm volatile("st.shared.b16 [%0], %1;" ::"r"(addr), "h"(*reinterpret_cast<const uint16_t*>(&pb))
-                       : "memory");
-        }
-        fence_proxy_async_smem();
-        tc_fence_before();
-        mbar_arrive(&sm.p_full[sb]);
-      }
+      if (lane == 0) sm.warp_ok[rb][warp] = ok;
+      named_barrier_sync(1, kSoftmaxThreads);
+      all_ok = sm.warp_ok[rb][0] && sm.warp_ok[rb][1] && sm.warp_ok[rb][2] && sm.warp_ok[rb][3];
       if (!all_ok) break;
+      bool any_resc = false;
+      float alpha[QPK];
+#pragma unroll
+      for (int h = 0; h < QPK; ++h) {
+        const float mt = fmaxf(fmaxf(sm.red[rb][0][h], sm.red[rb][1][h]), fmaxf(sm.red[rb][2][h], sm.red[rb][3][h]));
+        alpha[h] = 1.f;
+        if (mt > m_ref[h] + kRescaleThreshold) {
+          alpha[h] = fast_exp2(m_ref[h] - mt);  // 0 when m_ref = -inf
+          m_ref[h] = mt;
+          l_t[h] *= alpha[h];
+          any_resc = true;
+        }
+      }
+      if (any_resc && !first) {
+        // O^T lane t is dim t; PV(j-1) must be complete before O changes.
+        bool okr = __all_sync(0xffffffffu, mbar_wait(&sm.pv_done[(j - 1) & 1], ((j - 1) >> 1) & 1));
+        if (lane == 0) sm.resc_ok[warp] = okr;
+        named_barrier_sync(1, kSoftmaxThreads);
+        all_ok = sm.resc_ok[0] && sm.resc_ok[1] && sm.resc_ok[2] && sm.resc_ok[3];
+        if (!all_ok) break;
+        float o[8];
+        tc_fence_after();
+        tmem_ld_cols(o_tmem, QPK, o);
+#pragma unroll
+        for (int h = 0; h < QPK; ++h) o[h] *= alpha[h];
+        tmem_st_cols(o_tmem, QPK, o);
+      }
+      if (!valid) {
+        // Rows past the context hold arbitrary bits; P is 0 there, but the
+        // tensor core still multiplies them, so they become zeros.
+        const uint32_t vrow = smem_u32(sm.v[st]) + tid * 128;
+#pragma unroll
+        for (int cc = 0; cc < 8; ++cc) {
+          st_shared_v4(vrow + cc * 16, 0, 0, 0, 0);
+          st_shared_v4(vrow + kHalf + cc * 16, 0, 0, 0, 0);
+        }
+      }
+      // P^T[h][token], K-major SW128: tokens 0-63 in the first 2 KiB half.
+      const uint32_t p_base = smem_u32(sm.p[sb]) + (tid >> 6) * kQHalf + (tid & 7) * 2;
+      const int chunk = (tid & 63) >> 3;
+#pragma unroll
+      for (int h = 0; h < QPK; ++h) {
+        const float mu = (m_ref[h] == -INFINITY) ? 0.f : m_ref[h];
+        const float p = valid ? fast_exp2(sv[h] - mu) : 0.f;
+        l_t[h] += p;
+        const __nv_bfloat16 pb = __float2bfloat16_rn(p);
+        const uint32_t addr = p_base + h * 128 + ((chunk ^ (h & 7)) << 4);
+        asm volatile("st.shared.b16 [%0], %1;" ::"r"(addr), "h"(*reinterpret_cast<const uint16_t*>(&pb))
+                     : "memory");
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      mbar_arrive(&sm.p_full[sb]);
+      if (!(ti.flags & kLastTile)) continue;
       // Hand the segment's (m, l) to the epilogue warps and go on streaming;
-      // the info slot is free once the epilogue released segment seg-2.
+      // the info slot is free once the epilogue released segment seg-kOBufs.
+      const int seg = ti.seg;
       if (seg >= kOBufs && !__all_sync(0xffffffffu, mbar_wait(&sm.o_empty[ob], ((seg / kOBufs) - 1) & 1))) {
         all_ok = false;
         break;
@@ -792,12 +874,12 @@ __global__ void __launch_bounds__(kThreads, 1) paged_decode_kernel(const __grid_
         if (tid == 0) info.m[h] = m_ref[h];
       }
       if (tid == 0) {
-        info.b = s.b;
-        info.g = s.g;
-        info.n = s.n;
-        info.ntiles = s.ntiles;
-        info.pair_t0 = s.pair_t0;
-        info.slot = (s.start == lo) ? 0 : 1;
+        info.b = ti.b;
+        info.g = ti.g;
+        info.n = ti.n;
+        info.ntiles = ti.ntiles;
+        info.pair_t0 = ti.pair_t0;
+        info.slot = ti.slot;
       }
       mbar_arrive(&sm.seg_ready[ob]);
     }
@@ -1007,6 +1089,7 @@ extern "C" int nvk_paged_decode(void* out, const void* query, const void* key_ca
     a.block_size = block_size;
     a.log2_bs = __builtin_ctz(static_cast<unsigned>(block_size));
     a.sub_rows = sub_rows;
+    a.chunk_tiles = block_size >= 64 ? kChunkTiles : kSlotIds * block_size / kTile;
     a.num_heads = num_heads;
     a.num_kv_heads = num_kv_heads;
     a.qpk = qpk;
