@@ -133,6 +133,21 @@ __host__ __device__ constexpr int ceil_div(int a, int b) { return (a + b - 1) / 
 // its writes are visible; without such a launch it returns at once).
 // pdl_launch_dependents() lets the successor be scheduled early.
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+// L2 prefetch of the 128-byte lines holding bytes [p, p + n): line k is
+// requested by thread `tid` of part `part` when k % (parts * nthreads) ==
+// part * nthreads + tid. A prefetch moves no data into registers and L2 is
+// the point of coherence, so it may run before pdl_wait() on memory the
+// predecessor still writes: later loads see the predecessor's stores. Every
+// line requested holds a byte of the buffer, so it lies in mapped memory.
+__device__ __forceinline__ void prefetch_l2_range(const void* p, int64_t n, int part, int parts, int tid,
+                                                  int nthreads) {
+  if (p == nullptr || n <= 0) return;
+  const uintptr_t first = reinterpret_cast<uintptr_t>(p) & ~uintptr_t(127);
+  const int64_t lines = static_cast<int64_t>((reinterpret_cast<uintptr_t>(p) + n - first + 127) >> 7);
+  for (int64_t k = static_cast<int64_t>(part) * nthreads + tid; k < lines; k += static_cast<int64_t>(parts) * nthreads)
+    asm volatile("prefetch.global.L2 [%0];" ::"l"(first + (static_cast<uintptr_t>(k) << 7)));
+}
 __device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
 }  // namespace nvk

@@ -74,6 +74,7 @@ constexpr int kTicketStride = 32;          // ints: one 128-byte line per ticket
 
 struct DecodeArgs {
   __nv_bfloat16* out;
+  const void* query;  // only warmed in L2 here; read through the tensor map
   const int32_t* block_tables;
   const int32_t* context_lens;
   float* ws_o;    // [C][2][QPK][kD] partial numerators
@@ -132,6 +133,7 @@ struct Smem {
   uint64_t fin;
   uint32_t tmem_base;
   int total_tiles;
+  int b_lo, b_hi;  // sequences holding this CTA's first and last tile
   // softmax -> epilogue hand-off, one per O buffer
   struct SegInfo {
     int b, g, n, ntiles, pair_t0, slot;
@@ -149,18 +151,6 @@ struct Smem {
 };
 
 __device__ __forceinline__ int seq_tiles(int len) { return (len + kTile - 1) / kTile; }
-
-// Sequence whose pairs hold linear tile t: the largest b with
-// kvh * tiles_before[b] <= t (this skips sequences without tiles).
-__device__ __forceinline__ int find_seq(const Smem& sm, int batch, int kvh, int t) {
-  int lo = 0, hi = batch - 1;
-  while (lo < hi) {
-    const int mid = (lo + hi + 1) >> 1;
-    if (kvh * sm.tiles_before[mid] <= t) lo = mid;
-    else hi = mid - 1;
-  }
-  return lo;
-}
 
 // The T tiles of a launch split into C contiguous ranges: CTA c gets
 // q = T / C tiles, plus one more if c < r = T % C. Range starts and owners are
@@ -200,17 +190,19 @@ struct Segment {
   int b, g, len, i0, n, ntiles, pair_t0, start;
 };
 
-__device__ __forceinline__ Segment next_segment(const Smem& sm, const DecodeArgs& a, int t, int hi) {
+// The segment of sequence b (which must hold tile t) that starts at tile t
+// and ends at its pair's end or at hi.
+__device__ __forceinline__ Segment make_segment(const Smem& sm, const DecodeArgs& a, int b, int t, int hi) {
   Segment s;
-  s.b = find_seq(sm, a.batch, a.num_kv_heads, t);
-  s.n = sm.tiles_before[s.b + 1] - sm.tiles_before[s.b];
-  const int off = t - a.num_kv_heads * sm.tiles_before[s.b];
+  s.b = b;
+  s.n = sm.tiles_before[b + 1] - sm.tiles_before[b];
+  const int off = t - a.num_kv_heads * sm.tiles_before[b];
   s.g = off / s.n;
   s.i0 = off - s.g * s.n;
   s.ntiles = min(hi - t, s.n - s.i0);
   s.pair_t0 = t - s.i0;
   s.start = t;
-  s.len = (s.n - 1) * kTile + sm.last_rows[s.b];  // a segment exists only when s.n >= 1
+  s.len = (s.n - 1) * kTile + sm.last_rows[b];  // a segment exists only when s.n >= 1
   return s;
 }
 
@@ -219,55 +211,82 @@ __device__ __forceinline__ Segment next_segment(const Smem& sm, const DecodeArgs
 // then the whole pairs. Both pieces of every split pair are thus finished
 // early in every CTA, and their merge overlaps the streaming of whole pairs
 // instead of trailing the kernel. Every role follows the same order.
+// The sequences holding tiles lo and hi-1 come from the schedule scan, and
+// whole pairs follow one another, so no step searches.
 struct SegIter {
-  // Up to three sub-ranges, kept in named registers (no dynamically indexed
-  // local array: after an acquire at GPU scope local memory may miss L1).
-  int lo0, hi0, lo1, hi1, lo2, hi2, nr, ri, t, npartial;
+  int lo, hi;
+  int f_b, l_b, s1;  // sequences holding tiles lo and hi-1; start of the last segment
+  int cb, cg, ct;    // whole-pair cursor: pair (cb, cg) starts at tile ct ...
+  int m1;            // ... and whole pairs end at tile m1
+  int phase, npartial;
+  bool f_emit, l_emit;
 
-  __device__ __forceinline__ void init(const Smem& sm, const DecodeArgs& a, int lo, int hi) {
-    nr = 0;
-    ri = 0;
+  __device__ __forceinline__ void init(const Smem& sm, const DecodeArgs& a, int lo_, int hi_) {
+    lo = lo_;
+    hi = hi_;
+    phase = 0;
     npartial = 0;
-    lo0 = hi0 = lo1 = hi1 = lo2 = hi2 = 0;
-    t = lo;
+    f_emit = l_emit = false;
+    ct = m1 = hi;
+    f_b = l_b = s1 = cb = cg = 0;
     if (lo >= hi) return;
-    const Segment f = next_segment(sm, a, lo, hi);
+    f_b = sm.b_lo;
+    const Segment f = make_segment(sm, a, f_b, lo, hi);
     const int e0 = lo + f.ntiles;
     if (e0 >= hi) {  // a single segment
-      lo0 = lo;
-      hi0 = hi;
-      nr = 1;
+      f_emit = true;
       npartial = (f.ntiles != f.n) ? 1 : 0;
       return;
     }
-    const Segment l = next_segment(sm, a, hi - 1, hi);
-    const int s1 = max(e0, l.pair_t0);  // start of the last segment
-    const bool f_part = f.ntiles != f.n;
-    const bool l_part = (hi - s1) != l.n;
-    const int m0 = f_part ? e0 : lo, m1 = l_part ? s1 : hi;
-    if (f_part) push(lo, e0), ++npartial;
-    if (l_part) push(s1, hi), ++npartial;
-    if (m0 < m1) push(m0, m1);
-    t = lo0;
+    l_b = sm.b_hi;
+    const Segment l = make_segment(sm, a, l_b, hi - 1, hi);
+    s1 = max(e0, l.pair_t0);  // start of the last segment
+    f_emit = f.ntiles != f.n;
+    l_emit = (hi - s1) != l.n;
+    npartial = int(f_emit) + int(l_emit);
+    ct = f_emit ? e0 : lo;
+    m1 = l_emit ? s1 : hi;
+    cb = f_b;
+    cg = f.g;
+    if (f_emit && ct < m1) advance(sm, a.num_kv_heads);
   }
 
-  __device__ __forceinline__ void push(int x, int y) {
-    if (nr == 0) lo0 = x, hi0 = y;
-    else if (nr == 1) lo1 = x, hi1 = y;
-    else lo2 = x, hi2 = y;
-    ++nr;
+  // Next pair in linear order (one exists: the cursor is below m1).
+  __device__ __forceinline__ void advance(const Smem& sm, int kvh) {
+    if (++cg == kvh) {
+      cg = 0;
+      do {
+        ++cb;
+      } while (sm.tiles_before[cb + 1] == sm.tiles_before[cb]);  // sequences without tiles own no pair
+    }
   }
-  __device__ __forceinline__ int cur_hi() const { return ri == 0 ? hi0 : (ri == 1 ? hi1 : hi2); }
-  __device__ __forceinline__ int cur_lo() const { return ri == 0 ? lo0 : (ri == 1 ? lo1 : lo2); }
 
   __device__ __forceinline__ bool next(const Smem& sm, const DecodeArgs& a, Segment& s) {
-    while (ri < nr && t >= cur_hi()) {
-      ++ri;
-      if (ri < nr) t = cur_lo();
+    if (phase == 0) {
+      phase = 1;
+      if (f_emit) {
+        s = make_segment(sm, a, f_b, lo, hi);
+        return true;
+      }
     }
-    if (ri >= nr) return false;
-    s = next_segment(sm, a, t, cur_hi());
-    t += s.ntiles;
+    if (phase == 1) {
+      phase = 2;
+      if (l_emit) {
+        s = make_segment(sm, a, l_b, s1, hi);
+        return true;
+      }
+    }
+    if (ct >= m1) return false;
+    s.b = cb;
+    s.g = cg;
+    s.n = sm.tiles_before[cb + 1] - sm.tiles_before[cb];
+    s.len = (s.n - 1) * kTile + sm.last_rows[cb];
+    s.i0 = 0;
+    s.ntiles = s.n;
+    s.pair_t0 = ct;
+    s.start = ct;
+    ct += s.n;
+    if (ct < m1) advance(sm, a.num_kv_heads);
     return true;
   }
 };
@@ -501,15 +520,27 @@ __global__ void __launch_bounds__(kThreads, 1) paged_decode_kernel(const __grid_
     tmem_relinquish();
   }
   pdl_launch_dependents();
-  pdl_wait();  // nothing above reads global memory
+  // While the predecessor drains: warm L2 with the context lengths (every
+  // CTA scans them), and, spread over the grid, the block tables and queries.
+  if (warp == 0) prefetch_l2_range(a.context_lens, int64_t(a.batch) * 4, 0, 1, lane, 32);
+  else {
+    const int64_t bt_bytes = (int64_t(a.batch - 1) * a.bt_stride + a.max_blocks) * 4;
+    prefetch_l2_range(a.block_tables, bt_bytes, c, ctas, tid - 32, kThreads - 32);
+    prefetch_l2_range(a.query, int64_t(a.batch) * a.num_heads * kD * 2, c, ctas, tid - 32, kThreads - 32);
+  }
+  pdl_wait();  // nothing above loads global memory
   // ---- per-sequence tile prefix: every CTA derives the same schedule ----
+  // All lengths are loaded at once (one round trip), then warp 0 scans them
+  // in place.
+  for (int b = tid; b < a.batch; b += kThreads) sm.tiles_before[b] = a.context_lens[b];
+  __syncthreads();
   if (warp == 0) {
     int carry = 0;
     for (int base = 0; base < a.batch; base += 32) {
       const int b = base + lane;
       int n = 0;
       if (b < a.batch) {
-        int len = a.context_lens[b];
+        int len = sm.tiles_before[b];
         if (len > a.max_blocks * a.block_size) {
           if (c == 0) atomicOr(a.err, kErrContextTooLong);
           len = a.max_blocks * a.block_size;
@@ -530,6 +561,26 @@ __global__ void __launch_bounds__(kThreads, 1) paged_decode_kernel(const __grid_
     if (lane == 0) {
       sm.tiles_before[a.batch] = carry;
       sm.total_tiles = carry * kvh;
+    }
+    // Sequences holding this CTA's first and last tile: the largest b with
+    // kvh * tiles_before[b] <= t is the count of such b, less one.
+    __syncwarp();
+    const int total = carry * kvh;
+    if (total > 0) {
+      const Sched sc0 = make_sched(total, ctas);
+      const int t_lo = range_lo(c, sc0), t_hi = range_lo(c + 1, sc0) - 1;
+      int n_lo = 0, n_hi = 0;
+      for (int b = lane; b < a.batch; b += 32) {
+        const int v = kvh * sm.tiles_before[b];
+        n_lo += (v <= t_lo) ? 1 : 0;
+        n_hi += (v <= t_hi) ? 1 : 0;
+      }
+      n_lo = __reduce_add_sync(0xffffffffu, n_lo);
+      n_hi = __reduce_add_sync(0xffffffffu, n_hi);
+      if (lane == 0) {
+        sm.b_lo = max(n_lo - 1, 0);
+        sm.b_hi = max(n_hi - 1, 0);
+      }
     }
   }
   tc_fence_before();
@@ -1076,6 +1127,7 @@ extern "C" int nvk_paged_decode(void* out, const void* query, const void* key_ca
     if ((rc = kv_tensor_map(&qm, qb, nb, num_heads, 1, 0, qpk)) != NVK_OK) return rc;
     DecodeArgs a;
     a.out = static_cast<__nv_bfloat16*>(out) + static_cast<size_t>(b0) * num_heads * kD;
+    a.query = qb;
     a.block_tables = block_tables + static_cast<int64_t>(b0) * block_table_stride;
     a.context_lens = context_lens + b0;
     a.err = reinterpret_cast<int*>(ws);
