@@ -26,6 +26,11 @@
  *                         src/nanovllm_ascend/layers/npu_prefill_attention.py:82-96
  *   nvk_dense_prefill  <- the same op, dense mode (contiguous k/v, cumulative
  *                         actual_seq_lengths_kv), npu_prefill_attention.py:97-112
+ *   nvk_paged_decode_gather, nvk_peer_*
+ *                      <- no reference counterpart (the reference runs on one
+ *                         device, src/nanovllm_ascend/model_runner.py:31): KV-head
+ *                         sharded decode whose output all-gather across GPUs
+ *                         happens inside the attention kernel
  */
 #ifndef NVK_PAGED_KV_H_
 #define NVK_PAGED_KV_H_
@@ -57,7 +62,8 @@ enum {
 /* Message for the most recent non-zero return on the calling thread. */
 NVK_API const char* nvk_last_error(void);
 
-/* ABI version, bumped on any signature change (2: persistent decode, num_ctas). */
+/* ABI version, bumped on any signature change (2: persistent decode, num_ctas;
+   3: KV-head-sharded decode with in-kernel gather, peer buffers). */
 NVK_API int nvk_abi_version(void);
 
 /*
@@ -164,6 +170,54 @@ NVK_API int nvk_dense_prefill(void* out, const void* query, const void* key, con
                       const int32_t* cu_seqlens_q, const int32_t* cu_seqlens_kv, int batch, int total_q,
                       int total_kv, int max_q_len, int num_heads, int num_kv_heads, int head_dim, float scale,
                       int* error_word, nvk_stream_t stream);
+
+/*
+ * ---- KV-head-sharded decode, outputs gathered across GPUs in the kernel ----
+ * One process per GPU. Rank r of `world` holds a slice of the KV heads and the
+ * query heads of their GQA groups; every rank needs all heads' outputs.
+ *
+ * Peer buffers: nvk_peer_alloc returns zero-filled device memory of its own
+ * allocation, which nvk_peer_export describes in an NVK_PEER_HANDLE_BYTES
+ * handle (CUDA IPC); another process on the same node maps it with
+ * nvk_peer_import and unmaps it with nvk_peer_close. The exchange of handles
+ * between processes is the caller's (e.g. an all-gather over a process group).
+ */
+#define NVK_MAX_PEERS 8
+#define NVK_PEER_HANDLE_BYTES 64
+#define NVK_PEER_SIGNAL_BYTES 256 /* per rank: one uint32 flag per source rank and an epoch counter */
+
+NVK_API int nvk_peer_alloc(size_t bytes, void** ptr);
+NVK_API int nvk_peer_free(void* ptr);
+NVK_API int nvk_peer_export(const void* ptr, void* handle);
+NVK_API int nvk_peer_import(const void* handle, void** ptr);
+NVK_API int nvk_peer_close(void* ptr);
+
+/*
+ * nvk_paged_decode over this rank's heads, with the all-gather of the outputs
+ * done by the kernel's own stores. query: this rank's bf16 [batch, num_heads,
+ * head_dim] (num_heads query heads over the num_kv_heads KV heads of this
+ * rank's pool). The result for (b, h) is written to EVERY rank's gathered
+ * output out_peers[p], bf16 [batch, out_heads, head_dim], at head
+ * head_offset + h (plain stores over NVLink; out_peers[rank] is this rank's
+ * own buffer). signal_peers[p] is rank p's signal area of
+ * NVK_PEER_SIGNAL_BYTES (zeroed before first use, used by nothing else).
+ *
+ * When the call has completed on this rank's stream, out_peers[rank] holds the
+ * rows of every rank for this call: the kernel's last CTA posts an epoch flag
+ * to every rank and waits for all of theirs (bounded: after 1 s it sets bit 16
+ * of the workspace error word and returns). Every rank must make the same
+ * sequence of calls with the same batch. A rank can run one call ahead of a
+ * slower peer, so consecutive calls must write different output buffers
+ * (alternating two is enough when the consumer of a call's output runs on this
+ * stream before the next call). world in [1, NVK_MAX_PEERS].
+ */
+NVK_API int nvk_paged_decode_gather(const void* query, const void* key_cache, const void* value_cache,
+                                    int num_blocks, int block_size, const int32_t* block_tables,
+                                    int block_table_stride, int max_blocks_per_seq, const int32_t* context_lens,
+                                    int batch, int num_heads, int num_kv_heads, int head_dim, float scale,
+                                    int num_ctas, void* workspace, size_t workspace_bytes, void* const* out_peers,
+                                    void* const* signal_peers, int world, int rank, int out_heads, int head_offset,
+                                    nvk_stream_t stream);
 
 #ifdef __cplusplus
 }

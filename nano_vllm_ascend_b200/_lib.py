@@ -55,7 +55,21 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _i32, _i32, _i32, _i32, _i32, _i32, _i32,
          _f32, _c_void_p, _c_void_p],
     ),
+    "nvk_peer_alloc": (_i32, [_size_t, ctypes.POINTER(_c_void_p)]),
+    "nvk_peer_free": (_i32, [_c_void_p]),
+    "nvk_peer_export": (_i32, [_c_void_p, _c_void_p]),
+    "nvk_peer_import": (_i32, [_c_void_p, ctypes.POINTER(_c_void_p)]),
+    "nvk_peer_close": (_i32, [_c_void_p]),
+    "nvk_paged_decode_gather": (
+        _i32,
+        [_c_void_p, _c_void_p, _c_void_p, _i32, _i32, _c_void_p, _i32, _i32, _c_void_p, _i32, _i32, _i32, _i32, _f32,
+         _i32, _c_void_p, _size_t, _c_void_p, _c_void_p, _i32, _i32, _i32, _i32, _c_void_p],
+    ),
 }
+
+MAX_PEERS = 8
+PEER_HANDLE_BYTES = 64
+PEER_SIGNAL_BYTES = 256
 
 _LIB: ctypes.CDLL | None = None
 

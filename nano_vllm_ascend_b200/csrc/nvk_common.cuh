@@ -18,7 +18,8 @@ enum DeviceError : int {
   kErrWaitTimeout = 1,   // an mbarrier wait gave up after kWaitLimitNs
   kErrBadBlockId = 2,    // a block-table entry was outside [0, num_blocks)
   kErrBadSlot = 4,       // a slot_mapping entry was outside [0, num_slots)
-  kErrContextTooLong = 8 // context_lens[b] exceeds the block-table width
+  kErrContextTooLong = 8, // context_lens[b] exceeds the block-table width
+  kErrPeerTimeout = 16    // an in-kernel gather did not see every rank's flag in time
 };
 
 constexpr uint64_t kWaitLimitNs = 1000000000ull;  // 1 s
@@ -133,6 +134,17 @@ __host__ __device__ constexpr int ceil_div(int a, int b) { return (a + b - 1) / 
 // its writes are visible; without such a launch it returns at once).
 // pdl_launch_dependents() lets the successor be scheduled early.
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+// System-scope release store / acquire load of a 32-bit flag (may live in
+// another GPU's memory mapped into this process).
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
 
 // L2 prefetch of the 128-byte lines holding bytes [p, p + n): line k is
 // requested by thread `tid` of part `part` when k % (parts * nthreads) ==

@@ -89,6 +89,15 @@ struct DecodeArgs {
   int log2_bs;
   int sub_rows;
   int chunk_tiles;  // tiles per chunk: every chunk's block ids fit in kSlotIds
+  // Output rows: (b, local query head h) goes to head head_offset + h of a
+  // [batch, out_heads, 128] array -- `out`, or with world > 0 every rank's
+  // gathered output peer_out[r] (see gather_signal).
+  int out_heads, head_offset;
+  int world, rank;
+  __nv_bfloat16* peer_out[NVK_MAX_PEERS];
+  uint32_t* peer_sig[NVK_MAX_PEERS];
+  uint32_t* my_sig;
+  int* done;  // CTAs finished this call (gather mode), back at zero after it
   int num_heads;
   int num_kv_heads;
   int qpk;
@@ -291,6 +300,50 @@ struct SegIter {
   }
 };
 
+// Stores output element d of (sequence b, local query head qh).
+__device__ __forceinline__ void store_out(const DecodeArgs& a, int b, int qh, int d, float v) {
+  const int64_t off = (static_cast<int64_t>(b) * a.out_heads + a.head_offset + qh) * kD + d;
+  const __nv_bfloat16 x = __float2bfloat16_rn(v);
+  if (a.world == 0) {
+    a.out[off] = x;
+    return;
+  }
+#pragma unroll
+  for (int r = 0; r < NVK_MAX_PEERS; ++r)
+    if (r < a.world) a.peer_out[r][off] = x;  // a peer's buffer: a store over NVLink
+}
+
+constexpr int kEpochSlot = NVK_MAX_PEERS;  // signal word holding this rank's call count
+
+// Completion of the in-kernel gather (thread 0 of every CTA, after the CTA's
+// last output store): each CTA fences its stores at system scope and takes a
+// ticket; the last CTA posts this call's epoch to every rank's signal area and
+// waits until every rank has posted the same epoch to ours. Then every rank's
+// rows of this call are in our buffer when the kernel completes. The wait is
+// bounded (kWaitLimitNs -> kErrPeerTimeout).
+__device__ __forceinline__ void gather_signal(const DecodeArgs& a, int ctas) {
+  __threadfence_system();
+  int old;
+  asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], 1;" : "=r"(old) : "l"(a.done) : "memory");
+  if (old != ctas - 1) return;
+  __threadfence_system();
+  *a.done = 0;  // for the next call, which the kernel boundary orders after this one
+  const uint32_t epoch = a.my_sig[kEpochSlot] + 1;
+  a.my_sig[kEpochSlot] = epoch;
+#pragma unroll
+  for (int r = 0; r < NVK_MAX_PEERS; ++r)
+    if (r < a.world) st_release_sys(a.peer_sig[r] + a.rank, epoch);
+  const uint64_t t0 = globaltimer_ns();
+  for (int r = 0; r < a.world; ++r) {
+    while (static_cast<int>(ld_acquire_sys(a.my_sig + r) - epoch) < 0) {
+      if (globaltimer_ns() - t0 > kWaitLimitNs) {
+        atomicOr(a.err, kErrPeerTimeout);
+        return;
+      }
+    }
+  }
+}
+
 __device__ __forceinline__ void flag_error(const DecodeArgs& a, Smem& sm, int code) {
   atomicOr(a.err, code);
   sm.abort = 1;
@@ -400,7 +453,6 @@ __device__ __forceinline__ void publish_and_merge(Smem& sm, const DecodeArgs& a,
 #pragma unroll
   for (int k = 0; k < 2; ++k) {
     if (!sm.last[k] || slow[k]) continue;
-    __nv_bfloat16* out = a.out + (static_cast<int64_t>(sm.pend_b[k]) * a.num_heads + sm.pend_g[k] * QPK) * kD;
 #pragma unroll
     for (int h = 0; h < QPK; ++h) {
       float M = -INFINITY;
@@ -416,7 +468,7 @@ __device__ __forceinline__ void publish_and_merge(Smem& sm, const DecodeArgs& a,
           den = fmaf(w, mlv[k][u][h].y, den);
         }
       }
-      out[h * kD + d] = __float2bfloat16_rn(den > 0.f ? num / den : 0.f);
+      store_out(a, sm.pend_b[k], sm.pend_g[k] * QPK + h, d, den > 0.f ? num / den : 0.f);
     }
     if (e == 0) a.ws_cnt[static_cast<int64_t>(sm.pend_pair[k]) * kTicketStride] = 0;
   }
@@ -463,9 +515,8 @@ __device__ __forceinline__ void publish_and_merge(Smem& sm, const DecodeArgs& a,
       }
       named_barrier_sync(2, kEpilogueThreads);  // staging is rewritten by the next group
     }
-    __nv_bfloat16* out = a.out + (static_cast<int64_t>(sm.pend_b[k]) * a.num_heads + sm.pend_g[k] * QPK) * kD;
 #pragma unroll
-    for (int h = 0; h < QPK; ++h) out[h * kD + d] = __float2bfloat16_rn(den[h] > 0.f ? num[h] / den[h] : 0.f);
+    for (int h = 0; h < QPK; ++h) store_out(a, sm.pend_b[k], sm.pend_g[k] * QPK + h, d, den[h] > 0.f ? num[h] / den[h] : 0.f);
     if (e == 0) a.ws_cnt[static_cast<int64_t>(sm.pend_pair[k]) * kTicketStride] = 0;
   }
 }
@@ -970,10 +1021,8 @@ __global__ void __launch_bounds__(kThreads, 1) paged_decode_kernel(const __grid_
         tc_fence_before();
         mbar_arrive(&sm.o_empty[ob]);
         if (s.ntiles == s.n) {  // the whole pair lies in this CTA
-          __nv_bfloat16* out = a.out + (static_cast<int64_t>(s.b) * a.num_heads + s.g * QPK) * kD;
 #pragma unroll
-          for (int h = 0; h < QPK; ++h)
-            out[h * kD + d] = __float2bfloat16_rn(l_sum[h] > 0.f ? o[h] / l_sum[h] : 0.f);
+          for (int h = 0; h < QPK; ++h) store_out(a, s.b, s.g * QPK + h, d, l_sum[h] > 0.f ? o[h] / l_sum[h] : 0.f);
         } else {
           // A piece of a pair shared with other CTAs: stored now, published
           // with one ticket right after the partial segments.
@@ -1004,8 +1053,7 @@ __global__ void __launch_bounds__(kThreads, 1) paged_decode_kernel(const __grid_
     // Sequences without context own no tile: their outputs are zeros.
     for (int b = c; b < a.batch; b += ctas) {
       if (sm.tiles_before[b + 1] == sm.tiles_before[b]) {
-        __nv_bfloat16* out = a.out + static_cast<int64_t>(b) * a.num_heads * kD;
-        for (int h = 0; h < a.num_heads; ++h) out[h * kD + e] = __float2bfloat16_rn(0.f);
+        for (int h = 0; h < a.num_heads; ++h) store_out(a, b, h, e, 0.f);
       }
     }
   }
@@ -1017,6 +1065,7 @@ __global__ void __launch_bounds__(kThreads, 1) paged_decode_kernel(const __grid_
     __syncwarp();
     tmem_dealloc(tmem, kTmemCols);
   }
+  if (a.world > 0 && tid == 0) gather_signal(a, ctas);
 }
 
 static_assert(sizeof(Smem) + 1024 <= 232448, "decode shared memory exceeds the 227 KB per-CTA limit");
@@ -1069,12 +1118,20 @@ extern "C" int nvk_paged_decode_workspace_size(int batch, int num_heads, int num
   return NVK_OK;
 }
 
-extern "C" int nvk_paged_decode(void* out, const void* query, const void* key_cache, const void* value_cache,
-                                int num_blocks, int block_size, const int32_t* block_tables, int block_table_stride,
-                                int max_blocks_per_seq, const int32_t* context_lens, int batch, int num_heads,
-                                int num_kv_heads, int head_dim, float scale, int num_ctas, void* workspace,
-                                size_t workspace_bytes, nvk_stream_t stream) {
-  using namespace nvk;
+namespace nvk {
+namespace {
+
+// Where a gathering decode call stores its rows (see nvk_paged_decode_gather).
+struct GatherTargets {
+  void* const* out_peers;
+  void* const* signal_peers;
+  int world, rank, out_heads, head_offset;
+};
+
+int decode_impl(void* out, const void* query, const void* key_cache, const void* value_cache, int num_blocks,
+                int block_size, const int32_t* block_tables, int block_table_stride, int max_blocks_per_seq,
+                const int32_t* context_lens, int batch, int num_heads, int num_kv_heads, int head_dim, float scale,
+                int num_ctas, void* workspace, size_t workspace_bytes, const GatherTargets* gt, nvk_stream_t stream) {
   if (batch < 0 || num_blocks <= 0 || num_heads <= 0 || num_kv_heads <= 0 || num_ctas < 0)
     return fail(NVK_ERR_INVALID_ARGUMENT, "paged_decode: bad sizes (batch=%d blocks=%d heads=%d kv_heads=%d ctas=%d)",
                 batch, num_blocks, num_heads, num_kv_heads, num_ctas);
@@ -1092,9 +1149,9 @@ extern "C" int nvk_paged_decode(void* out, const void* query, const void* key_ca
   if (max_blocks_per_seq <= 0 || block_table_stride < max_blocks_per_seq)
     return fail(NVK_ERR_INVALID_ARGUMENT, "paged_decode: block table width %d / stride %d invalid",
                 max_blocks_per_seq, block_table_stride);
-  if (!out || !query || !key_cache || !value_cache || !block_tables || !context_lens)
+  if ((!gt && !out) || !query || !key_cache || !value_cache || !block_tables || !context_lens)
     return fail(NVK_ERR_INVALID_ARGUMENT, "paged_decode: null pointer");
-  if (!aligned16(out) || !aligned16(query))
+  if ((!gt && !aligned16(out)) || !aligned16(query))
     return fail(NVK_ERR_INVALID_ARGUMENT, "paged_decode: q/out must be 16-byte aligned");
   int ctas = 0;
   int rc = resolve_ctas(num_ctas, &ctas);
@@ -1126,7 +1183,20 @@ extern "C" int nvk_paged_decode(void* out, const void* query, const void* key_ca
     // q as [nb, heads, 128]: box {64 dims, QPK heads, 1 sequence}
     if ((rc = kv_tensor_map(&qm, qb, nb, num_heads, 1, 0, qpk)) != NVK_OK) return rc;
     DecodeArgs a;
-    a.out = static_cast<__nv_bfloat16*>(out) + static_cast<size_t>(b0) * num_heads * kD;
+    const int out_heads = gt ? gt->out_heads : num_heads;
+    const size_t out_skip = static_cast<size_t>(b0) * out_heads * kD;
+    a.out = gt ? nullptr : static_cast<__nv_bfloat16*>(out) + out_skip;
+    a.out_heads = out_heads;
+    a.head_offset = gt ? gt->head_offset : 0;
+    a.world = gt ? gt->world : 0;
+    a.rank = gt ? gt->rank : 0;
+    for (int r = 0; r < NVK_MAX_PEERS; ++r) {
+      const bool on = gt && r < gt->world;
+      a.peer_out[r] = on ? static_cast<__nv_bfloat16*>(gt->out_peers[r]) + out_skip : nullptr;
+      a.peer_sig[r] = on ? static_cast<uint32_t*>(gt->signal_peers[r]) : nullptr;
+    }
+    a.my_sig = gt ? static_cast<uint32_t*>(gt->signal_peers[gt->rank]) : nullptr;
+    a.done = reinterpret_cast<int*>(ws + 64);
     a.query = qb;
     a.block_tables = block_tables + static_cast<int64_t>(b0) * block_table_stride;
     a.context_lens = context_lens + b0;
@@ -1157,6 +1227,45 @@ extern "C" int nvk_paged_decode(void* out, const void* query, const void* key_ca
     if (rc != NVK_OK) return rc;
   }
   return NVK_OK;
+}
+
+}  // namespace
+}  // namespace nvk
+
+extern "C" int nvk_paged_decode(void* out, const void* query, const void* key_cache, const void* value_cache,
+                                int num_blocks, int block_size, const int32_t* block_tables, int block_table_stride,
+                                int max_blocks_per_seq, const int32_t* context_lens, int batch, int num_heads,
+                                int num_kv_heads, int head_dim, float scale, int num_ctas, void* workspace,
+                                size_t workspace_bytes, nvk_stream_t stream) {
+  return nvk::decode_impl(out, query, key_cache, value_cache, num_blocks, block_size, block_tables,
+                          block_table_stride, max_blocks_per_seq, context_lens, batch, num_heads, num_kv_heads,
+                          head_dim, scale, num_ctas, workspace, workspace_bytes, nullptr, stream);
+}
+
+extern "C" int nvk_paged_decode_gather(const void* query, const void* key_cache, const void* value_cache,
+                                       int num_blocks, int block_size, const int32_t* block_tables,
+                                       int block_table_stride, int max_blocks_per_seq, const int32_t* context_lens,
+                                       int batch, int num_heads, int num_kv_heads, int head_dim, float scale,
+                                       int num_ctas, void* workspace, size_t workspace_bytes,
+                                       void* const* out_peers, void* const* signal_peers, int world, int rank,
+                                       int out_heads, int head_offset, nvk_stream_t stream) {
+  using namespace nvk;
+  if (world < 1 || world > NVK_MAX_PEERS || rank < 0 || rank >= world)
+    return fail(NVK_ERR_INVALID_ARGUMENT, "paged_decode_gather: rank %d / world %d invalid (world 1..%d)", rank,
+                world, NVK_MAX_PEERS);
+  if (head_offset < 0 || num_heads <= 0 || out_heads < head_offset + num_heads)
+    return fail(NVK_ERR_INVALID_ARGUMENT, "paged_decode_gather: heads [%d, %d) outside the %d output heads",
+                head_offset, head_offset + num_heads, out_heads);
+  if (!out_peers || !signal_peers) return fail(NVK_ERR_INVALID_ARGUMENT, "paged_decode_gather: null peer arrays");
+  for (int r = 0; r < world; ++r) {
+    if (!out_peers[r] || !aligned16(out_peers[r]) || !signal_peers[r] ||
+        (reinterpret_cast<uintptr_t>(signal_peers[r]) & 3u) != 0)
+      return fail(NVK_ERR_INVALID_ARGUMENT, "paged_decode_gather: rank %d buffers null or misaligned", r);
+  }
+  const GatherTargets gt{out_peers, signal_peers, world, rank, out_heads, head_offset};
+  return decode_impl(nullptr, query, key_cache, value_cache, num_blocks, block_size, block_tables,
+                     block_table_stride, max_blocks_per_seq, context_lens, batch, num_heads, num_kv_heads, head_dim,
+                     scale, num_ctas, workspace, workspace_bytes, &gt, stream);
 }
 
 // ---------------------------------------------------------------------------
