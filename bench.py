@@ -17,6 +17,13 @@ Workloads (seeded synthetic inputs with the configs' shapes; no model weights):
       its own pool (sequence-sharded replicas, no collective): weak scaling.
   decode_c4: 256 sequences, context ~ U[2048, 6144], split evenly across
       ranks by sequence (strong scaling).
+  decode_c5: Qwen3-8B KV shapes (36 layers, 32 query / 8 KV heads), 128
+      sequences at context 8192, KV-head sharded over N in {2, 4, 8} GPUs
+      (the pool does not fit one GPU). Per layer: append of this rank's KV
+      heads, then decode attention over them whose output rows go straight
+      into every rank's gathered [128, 32, 128] output (in-kernel all-gather
+      over NVLink, --gather kernel) or, as the baseline, decode followed by an
+      NCCL all_gather_into_tensor and a permuting copy (--gather nccl).
 
 Printed (rank 0, one JSON line): value = KV bytes read by decode attention
 per step, summed over ranks, / max-over-ranks step time (GB/s); tok/s; the
@@ -68,6 +75,9 @@ WORKLOADS = {
                           describe="config[1]: Qwen3-0.6B decode step, 32 seqs, ctx~U[256,2304], CUDA graph bs 32"),
     "decode_c4": Workload("decode_c4", 28, 256, 16, 8, 2048, 6144, "strong",
                           describe="config[3]: Qwen3-0.6B decode step, 256 seqs, ctx~U[2048,6144], sequence-sharded"),
+    "decode_c5": Workload("decode_c5", 36, 128, 32, 8, 8192, 8192, "strong",
+                          describe="config[4]: Qwen3-8B KV cache, 128 seqs at ctx 8192, KV-head sharded, "
+                                   "outputs all-gathered"),
     # prefill: ctx_lo = cached prefix tokens, ctx_hi = new tokens per request
     "prefill_c3": Workload("prefill_c3", 28, 32, 16, 8, 768, 256, "weak",
                            describe="config[2]: Qwen3-0.6B prefix-cache prefill, 32 requests x (768 cached + 256 new)"),
@@ -567,6 +577,181 @@ def run_ours(args, world, rank, local):
     return 0
 
 
+# ------------------------------------------------------------ config 5 ----
+def run_c5_ours(args, world, rank, local):
+    """KV-head-sharded decode step (config 5) with the outputs all-gathered."""
+    from nano_vllm_ascend_b200 import BlockManager, PagedKVCache, ops
+    from nano_vllm_ascend_b200.peer_gather import PeerGather
+    from nano_vllm_ascend_b200.sharding import gather_head_shards, kv_head_shard
+
+    wl = WORKLOADS["decode_c5"]
+    device = torch.device("cuda", local)
+    kv_r, q_r = kv_head_shard(wl.heads, wl.kv_heads, world, rank)
+    kvh, hl, hoff = len(kv_r), len(q_r), q_r.start
+    b, layers = wl.batch, wl.layers
+    ctx = [wl.ctx_lo] * b
+    need = sum((n + 1 + BLOCK - 1) // BLOCK for n in ctx)
+    num_blocks = need + 64
+    pool_bytes = 2 * layers * num_blocks * BLOCK * kvh * HEAD_DIM * 2
+    free, _ = torch.cuda.mem_get_info(device)
+    if pool_bytes > wl.util * free:
+        raise SystemExit(f"decode_c5: {pool_bytes / 1e9:.1f} GB of KV per GPU at N={world} exceeds "
+                         f"{wl.util:.0%} of free HBM ({free / 1e9:.1f} GB); run it on 2, 4 or 8 GPUs")
+    bm = BlockManager(num_blocks, BLOCK, device)
+    bm.free_block_ids = torch.randperm(num_blocks, generator=torch.Generator().manual_seed(42)).tolist()
+    slots = list(range(b))
+    bm.prepare_prefill_metadata(slots, ctx, [0] * b, [[] for _ in slots])
+    md = bm.prepare_decode_metadata(slots, ctx, q_len=1)
+    kv = PagedKVCache(layers, num_blocks, BLOCK, kvh, HEAD_DIM, torch.bfloat16, device)
+    gen = torch.Generator(device=device).manual_seed(5 + rank)
+    for cache in (kv.key_cache, kv.value_cache):  # layer 0 random, the others copies (same bytes to stream)
+        cache[0].normal_(generator=gen)
+        for layer in range(1, layers):
+            cache[layer].copy_(cache[0])
+    g = torch.Generator(device=device).manual_seed(11 + rank)
+    q = torch.randn(layers, b, hl, HEAD_DIM, generator=g, device=device).to(torch.bfloat16)
+    k_new = torch.randn(layers, b, kvh, HEAD_DIM, generator=g, device=device).to(torch.bfloat16)
+    v_new = torch.randn(layers, b, kvh, HEAD_DIM, generator=g, device=device).to(torch.bfloat16)
+    tables = md.block_tables.to(device)
+    ctx_d = md.context_lens.to(device=device, dtype=torch.int32)
+    slot_map = md.slot_mapping.to(device)
+    scale = HEAD_DIM ** -0.5
+    ws = torch.zeros(ops.decode_workspace_bytes(b, hl, kvh, HEAD_DIM), dtype=torch.uint8, device=device)
+    in_kernel = args.gather == "kernel"
+    pg = PeerGather(b, wl.heads, HEAD_DIM, slots=layers, device=device) if in_kernel else None
+    local_out = torch.empty(layers, b, hl, HEAD_DIM, dtype=torch.bfloat16, device=device)
+    gathered = torch.empty(layers, b, wl.heads, HEAD_DIM, dtype=torch.bfloat16, device=device)
+
+    def attend(layer, gather=True):
+        kc, vc = kv.get_physical_cache(layer)
+        if in_kernel:
+            return pg.decode(q[layer], kc, vc, tables, ctx_d, scale, ws, head_offset=hoff, slot=layer)
+        ops.paged_decode(local_out[layer], q[layer], kc, vc, tables, ctx_d, scale, ws)
+        if gather and world > 1:
+            return gather_head_shards(local_out[layer], out=gathered[layer])
+        return local_out[layer]
+
+    def step():
+        out = None
+        for layer in range(layers):
+            kv.write(layer, k_new[layer], v_new[layer], slot_map)
+            out = attend(layer)
+        return out
+
+    stream = torch.cuda.Stream(device)
+    with torch.cuda.stream(stream):
+        step()  # eager warm-up (NCCL communicator, workspace); every rank makes the same calls
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            last_out = step()
+    torch.cuda.synchronize()
+
+    with torch.cuda.stream(stream), ClockSampler(local) as clocks:
+        # decode kernel alone (roofline; with --gather kernel the kernel includes
+        # its gather), cycling layers: every rank runs the same launches
+        for i in range(layers):
+            attend(i, gather=False)
+        barrier_sync(world)
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        n_launch = layers * (1 if args.quick else 4)
+        ev0.record(stream)
+        for i in range(n_launch):
+            attend(i % layers, gather=False)
+        ev1.record(stream)
+        ev1.synchronize()
+        t_dec = ev0.elapsed_time(ev1) / 1e3 / n_launch
+        if ops.decode_error_word(ws) != 0:
+            raise RuntimeError(f"decode error word {ops.decode_error_word(ws)}")
+        for _ in range(args.warmup):
+            graph.replay()
+        barrier_sync(world)
+        ev0.record(stream)
+        for _ in range(args.steps):
+            graph.replay()
+        ev1.record(stream)
+        barrier_sync(world)
+        t_step = ev0.elapsed_time(ev1) / 1e3 / args.steps
+
+        # end to end: pinned host inputs -> device, replay, last layer's gathered output -> host
+        h_q, h_k, h_v = (t.cpu().pin_memory() for t in (q, k_new, v_new))
+        h_tables, h_slots, h_ctx = (t.cpu().pin_memory() for t in (tables, slot_map, ctx_d))
+        h_out = torch.empty(last_out.shape, dtype=last_out.dtype).pin_memory()
+
+        def e2e_step():
+            q.copy_(h_q, non_blocking=True)
+            k_new.copy_(h_k, non_blocking=True)
+            v_new.copy_(h_v, non_blocking=True)
+            tables.copy_(h_tables, non_blocking=True)
+            slot_map.copy_(h_slots, non_blocking=True)
+            ctx_d.copy_(h_ctx, non_blocking=True)
+            graph.replay()
+            h_out.copy_(last_out, non_blocking=True)
+
+        for _ in range(args.warmup):
+            e2e_step()
+        barrier_sync(world)
+        ev0.record(stream)
+        for _ in range(args.steps):
+            e2e_step()
+        ev1.record(stream)
+        barrier_sync(world)
+        t_e2e = ev0.elapsed_time(ev1) / 1e3 / args.steps
+    clk = clocks.summary()
+    if ops.decode_error_word(ws) != 0:
+        raise RuntimeError(f"decode error word {ops.decode_error_word(ws)}")
+
+    bytes_layer = kv_bytes_per_layer([n + 1 for n in ctx], kvh)
+    t_step_max = max_over_ranks(t_step, world)
+    t_e2e_max = max_over_ranks(t_e2e, world)
+    t_dec_max = max_over_ranks(t_dec, world)
+    bytes_all = sum_over_ranks(float(bytes_layer * layers), world)
+    peak, peak_kind = peaks()
+    dec_bytes = bytes_layer + b * hl * HEAD_DIM * 2 * 2 + tables.numel() * 4 + b * 4
+    nvlink_bytes = b * hl * HEAD_DIM * 2 * (world - 1)
+    h2d = sum(t.numel() * t.element_size() for t in (h_q, h_k, h_v, h_tables, h_slots, h_ctx))
+    d2h = h_out.numel() * h_out.element_size()
+    if rank == 0:
+        line = {
+            "metric": "paged decode-attn KV GB/s", "value": bytes_all / t_step_max / 1e9, "unit": "GB/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": t_step_max * 1e3,
+            "higher_is_better": True, "scaling": wl.scaling, "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic: seeded N(0,1) q/K/V (pool layer 0 random, copied to the other layers), "
+                    "seeded block tables",
+            "config": {"workload": wl.describe, "layers": layers, "global_batch": b, "seq_len": wl.ctx_lo + 1,
+                       "heads": [wl.heads, wl.kv_heads, HEAD_DIM], "heads_per_gpu": [hl, kvh],
+                       "block_size": BLOCK, "pool_blocks": num_blocks,
+                       "parallelism": f"KV-head sharded x{world}",
+                       "gather": "in-kernel peer stores over NVLink + epoch flags" if in_kernel
+                       else "NCCL all_gather_into_tensor + permute",
+                       "cache": "inputs larger than L2: every step reads %.1f GB of KV per GPU"
+                                % (bytes_layer * layers / 1e9)},
+            "tok_per_s": b / t_step_max,
+            "hbm_frac_of_step": (bytes_all / t_step_max / 1e9) / (peak * world),
+            "roofline": {"kernel": "paged_decode_kernel (gather)" if in_kernel else "paged_decode_kernel",
+                         "bound": "hbm", "achieved": dec_bytes / t_dec_max / 1e9, "peak": peak,
+                         "peak_kind": peak_kind, "unit": "GB/s", "frac": dec_bytes / t_dec_max / 1e9 / peak,
+                         "traffic": None, "algorithmic_bytes_per_launch": dec_bytes,
+                         "nvlink_bytes_per_launch": nvlink_bytes if in_kernel else 0,
+                         "us_per_launch": t_dec_max * 1e6},
+            "e2e": {"value": bytes_all / t_e2e_max / 1e9, "unit": "GB/s", "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h, "ms_per_step": t_e2e_max * 1e3},
+            "clocks": clk,
+            "gpu_launches": args.steps * layers * 2,
+            "cpu_baseline": None,
+        }
+        print(json.dumps(line), flush=True)
+    del graph
+    if pg is not None:
+        pg.close()
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
 # ---------------------------------------------------------------- prefill ----
 def prefill_flops(q_lens: list[int], kv_lens: list[int], heads: int) -> float:
     """4 * D * (visible (query, key) pairs), bottom-right causal."""
@@ -784,6 +969,8 @@ def main():
     ap.add_argument("--pool-blocks", type=int, default=0,
                     help="cap the KV pool at this many blocks (small-footprint profiling runs)")
     ap.add_argument("--quick", action="store_true", help="short roofline loops (profiling runs)")
+    ap.add_argument("--gather", choices=["kernel", "nccl"], default="kernel",
+                    help="decode_c5: all-gather of the head shards inside the attention kernel or by NCCL")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
@@ -809,6 +996,8 @@ def main():
         return run_reference(args, world, rank)
     if prefill:
         return run_prefill_ours(args, world, rank, local)
+    if args.workload == "decode_c5":
+        return run_c5_ours(args, world, rank, local)
     return run_ours(args, world, rank, local)
 
 
