@@ -5,9 +5,11 @@
                     [--impl ours|reference]
 
 A "step" is one decode step of the configured batch through every layer:
-per layer, the KV append of this step's token (nvk_kv_append) and paged GQA
-decode attention over the whole context (nvk_paged_decode), replayed as ONE
-CUDA graph captured by DecodeGraphRunner at the batch size.
+per layer, the KV append of this step's token and paged GQA decode attention
+over the whole context, replayed as ONE CUDA graph captured by
+DecodeGraphRunner at the batch size. The runner defers each layer's
+PagedKVCache.write so that the decode kernel performs the append itself
+(nvk_paged_decode_append): one launch per layer.
 
 Workloads (seeded synthetic inputs with the configs' shapes; no model weights):
   decode_c2 (default, N=1 headline): 28 layers, 32 sequences, context ~
@@ -552,6 +554,7 @@ def run_ours(args, world, rank, local):
                 "parallelism": f"sequence-sharded x{world}, independent pools, no collective",
                 "cache": "inputs larger than L2: every step reads %.2f GB of KV" % (bytes_step / 1e9),
                 "decode_grid": "persistent, one CTA per SM",
+                "append": "fused into the decode kernel" if runner.fuse_appends else "separate kernel",
             },
             "tok_per_s": seqs_all / t_step_max,
             "hbm_frac_of_step": (bytes_all / t_step_max / 1e9) / (peak * world),
@@ -564,7 +567,7 @@ def run_ours(args, world, rank, local):
             "e2e": {"value": bytes_all / t_e2e_max / 1e9, "unit": "GB/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "ms_per_step": t_e2e_max * 1e3},
             "clocks": clk,
-            "gpu_launches": args.steps * wl.layers * 2,
+            "gpu_launches": args.steps * wl.layers * (1 if runner.fuse_appends else 2),
             "cpu_baseline": cpu,
         }
         print(json.dumps(line), flush=True)
@@ -622,20 +625,22 @@ def run_c5_ours(args, world, rank, local):
     local_out = torch.empty(layers, b, hl, HEAD_DIM, dtype=torch.bfloat16, device=device)
     gathered = torch.empty(layers, b, wl.heads, HEAD_DIM, dtype=torch.bfloat16, device=device)
 
-    def attend(layer, gather=True):
+    def attend(layer, gather=True, append=False):
         kc, vc = kv.get_physical_cache(layer)
+        new = dict(new_key=k_new[layer], new_value=v_new[layer], slot_mapping=slot_map) if append else {}
         if in_kernel:
-            return pg.decode(q[layer], kc, vc, tables, ctx_d, scale, ws, head_offset=hoff, slot=layer)
-        ops.paged_decode(local_out[layer], q[layer], kc, vc, tables, ctx_d, scale, ws)
+            return pg.decode(q[layer], kc, vc, tables, ctx_d, scale, ws, head_offset=hoff, slot=layer, **new)
+        ops.paged_decode(local_out[layer], q[layer], kc, vc, tables, ctx_d, scale, ws, **new)
         if gather and world > 1:
             return gather_head_shards(local_out[layer], out=gathered[layer])
         return local_out[layer]
 
     def step():
+        # per layer: this step's append fused into the attention kernel, then
+        # (baseline) the NCCL gather
         out = None
         for layer in range(layers):
-            kv.write(layer, k_new[layer], v_new[layer], slot_map)
-            out = attend(layer)
+            out = attend(layer, append=True)
         return out
 
     stream = torch.cuda.Stream(device)
@@ -724,6 +729,7 @@ def run_c5_ours(args, world, rank, local):
                        "parallelism": f"KV-head sharded x{world}",
                        "gather": "in-kernel peer stores over NVLink + epoch flags" if in_kernel
                        else "NCCL all_gather_into_tensor + permute",
+                       "append": "fused into the decode kernel",
                        "cache": "inputs larger than L2: every step reads %.1f GB of KV per GPU"
                                 % (bytes_layer * layers / 1e9)},
             "tok_per_s": b / t_step_max,
@@ -737,7 +743,7 @@ def run_c5_ours(args, world, rank, local):
             "e2e": {"value": bytes_all / t_e2e_max / 1e9, "unit": "GB/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "ms_per_step": t_e2e_max * 1e3},
             "clocks": clk,
-            "gpu_launches": args.steps * layers * 2,
+            "gpu_launches": args.steps * layers,
             "cpu_baseline": None,
         }
         print(json.dumps(line), flush=True)

@@ -26,6 +26,9 @@
  *                         src/nanovllm_ascend/layers/npu_prefill_attention.py:82-96
  *   nvk_dense_prefill  <- the same op, dense mode (contiguous k/v, cumulative
  *                         actual_seq_lengths_kv), npu_prefill_attention.py:97-112
+ *   nvk_paged_decode_append
+ *                      <- PagedKVCache.write + _npu_paged_attention of one decode layer
+ *                         (qwen3.py:91-117), fused
  *   nvk_paged_decode_gather, nvk_peer_*
  *                      <- no reference counterpart (the reference runs on one
  *                         device, src/nanovllm_ascend/model_runner.py:31): KV-head
@@ -63,7 +66,7 @@ enum {
 NVK_API const char* nvk_last_error(void);
 
 /* ABI version, bumped on any signature change (2: persistent decode, num_ctas;
-   3: KV-head-sharded decode with in-kernel gather, peer buffers). */
+   3: KV-head-sharded decode with in-kernel gather, peer buffers, fused append). */
 NVK_API int nvk_abi_version(void);
 
 /*
@@ -117,6 +120,27 @@ NVK_API int nvk_paged_decode(void* out, const void* query, const void* key_cache
                      int block_size, const int32_t* block_tables, int block_table_stride, int max_blocks_per_seq,
                      const int32_t* context_lens, int batch, int num_heads, int num_kv_heads, int head_dim,
                      float scale, int num_ctas, void* workspace, size_t workspace_bytes, nvk_stream_t stream);
+
+/*
+ * nvk_paged_decode with this step's KV append fused in: for every sequence b
+ * the token row key[b] / value[b] (bf16 [batch, num_kv_heads, head_dim],
+ * heads and dims contiguous, key_token_stride / value_token_stride ELEMENTS
+ * between tokens, 16-byte aligned) is written to pool slot slot_mapping[b]
+ * (int64, device) and then attended over, exactly as nvk_kv_append followed
+ * by nvk_paged_decode. Replaces the write + attention pair of one layer
+ * (Qwen3Attention.forward, src/nanovllm_ascend/models/qwen3.py:91-117) in
+ * decode. slot_mapping[b] must be sequence b's last context position
+ * (block_tables[b][(context_lens[b]-1) / block_size] * block_size +
+ * (context_lens[b]-1) % block_size), as the reference's decode metadata makes
+ * it; a row whose slot is not is skipped and bit 4 of the error word is set.
+ */
+NVK_API int nvk_paged_decode_append(void* out, const void* query, void* key_cache, void* value_cache,
+                                    int num_blocks, int block_size, const int32_t* block_tables,
+                                    int block_table_stride, int max_blocks_per_seq, const int32_t* context_lens,
+                                    int batch, int num_heads, int num_kv_heads, int head_dim, float scale,
+                                    int num_ctas, void* workspace, size_t workspace_bytes, const void* key,
+                                    const void* value, int64_t key_token_stride, int64_t value_token_stride,
+                                    const int64_t* slot_mapping, nvk_stream_t stream);
 
 /*
  * nvk_paged_decode without a caller workspace. No counterpart in the
@@ -210,14 +234,18 @@ NVK_API int nvk_peer_close(void* ptr);
  * slower peer, so consecutive calls must write different output buffers
  * (alternating two is enough when the consumer of a call's output runs on this
  * stream before the next call). world in [1, NVK_MAX_PEERS].
+ * key, value, key_token_stride, value_token_stride, slot_mapping: an
+ * optional fused append of this rank's KV heads, as in
+ * nvk_paged_decode_append (slot_mapping NULL: none).
  */
-NVK_API int nvk_paged_decode_gather(const void* query, const void* key_cache, const void* value_cache,
-                                    int num_blocks, int block_size, const int32_t* block_tables,
-                                    int block_table_stride, int max_blocks_per_seq, const int32_t* context_lens,
-                                    int batch, int num_heads, int num_kv_heads, int head_dim, float scale,
-                                    int num_ctas, void* workspace, size_t workspace_bytes, void* const* out_peers,
-                                    void* const* signal_peers, int world, int rank, int out_heads, int head_offset,
-                                    nvk_stream_t stream);
+NVK_API int nvk_paged_decode_gather(const void* query, void* key_cache, void* value_cache, int num_blocks,
+                                    int block_size, const int32_t* block_tables, int block_table_stride,
+                                    int max_blocks_per_seq, const int32_t* context_lens, int batch, int num_heads,
+                                    int num_kv_heads, int head_dim, float scale, int num_ctas, void* workspace,
+                                    size_t workspace_bytes, void* const* out_peers, void* const* signal_peers,
+                                    int world, int rank, int out_heads, int head_offset, const void* key,
+                                    const void* value, int64_t key_token_stride, int64_t value_token_stride,
+                                    const int64_t* slot_mapping, nvk_stream_t stream);
 
 #ifdef __cplusplus
 }

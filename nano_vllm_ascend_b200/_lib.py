@@ -63,7 +63,13 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "nvk_paged_decode_gather": (
         _i32,
         [_c_void_p, _c_void_p, _c_void_p, _i32, _i32, _c_void_p, _i32, _i32, _c_void_p, _i32, _i32, _i32, _i32, _f32,
-         _i32, _c_void_p, _size_t, _c_void_p, _c_void_p, _i32, _i32, _i32, _i32, _c_void_p],
+         _i32, _c_void_p, _size_t, _c_void_p, _c_void_p, _i32, _i32, _i32, _i32, _c_void_p, _c_void_p, _i64, _i64,
+         _c_void_p, _c_void_p],
+    ),
+    "nvk_paged_decode_append": (
+        _i32,
+        [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _i32, _i32, _c_void_p, _i32, _i32, _c_void_p, _i32, _i32, _i32,
+         _i32, _f32, _i32, _c_void_p, _size_t, _c_void_p, _c_void_p, _i64, _i64, _c_void_p, _c_void_p],
     ),
 }
 

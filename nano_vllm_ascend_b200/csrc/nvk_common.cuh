@@ -135,6 +135,12 @@ __host__ __device__ constexpr int ceil_div(int a, int b) { return (a + b - 1) / 
 // pdl_launch_dependents() lets the successor be scheduled early.
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 
+// Orders this thread's earlier generic-proxy global stores before later
+// async-proxy (TMA) accesses to the same memory.
+__device__ __forceinline__ void fence_proxy_async_global() {
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+
 // System-scope release store / acquire load of a 32-bit flag (may live in
 // another GPU's memory mapped into this process).
 __device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {

@@ -98,6 +98,16 @@ struct DecodeArgs {
   uint32_t* peer_sig[NVK_MAX_PEERS];
   uint32_t* my_sig;
   int* done;  // CTAs finished this call (gather mode), back at zero after it
+  // Fused append (new_slots != nullptr): this step's token of sequence b,
+  // rows k_new/v_new + b * stride (16-byte words, heads and dims packed), is
+  // written to pool slot new_slots[b] before any of its tiles is read.
+  const uint4* k_new;
+  const uint4* v_new;
+  int64_t k_new_stride_w, v_new_stride_w;
+  const int64_t* new_slots;
+  uint4* kc_words;
+  uint4* vc_words;
+  int64_t num_slots;
   int num_heads;
   int num_kv_heads;
   int qpk;
@@ -703,6 +713,26 @@ __global__ void __launch_bounds__(kThreads, 1) paged_decode_kernel(const __grid_
           ck.slot = (s.start == lo) ? 0 : 1;
           ck.blk0 = blk0;
         }
+        if (a.new_slots != nullptr && i + nt == s.n) {
+          // Fused append: this chunk holds the pair's last tile, which only
+          // this CTA reads, so it writes the new token's row of head s.g
+          // first (K by lanes 0-15, V by lanes 16-31, 16 bytes each). The
+          // slot must be the sequence's last context position.
+          __syncwarp();  // ck.ids written by every lane
+          const int last = s.len - 1;
+          const int blk = ck.ids[(last >> a.log2_bs) - blk0];
+          const int64_t want = static_cast<int64_t>(blk) * a.block_size + (last & (a.block_size - 1));
+          const int64_t slot = a.new_slots[s.b];
+          if (slot == want && blk < a.num_blocks) {
+            const int w = s.g * (kD * 2 / 16) + (lane & 15);
+            const int64_t row = slot * kvh * (kD * 2 / 16) + w;
+            if (lane < 16) a.kc_words[row] = a.k_new[s.b * a.k_new_stride_w + w];
+            else a.vc_words[row] = a.v_new[s.b * a.v_new_stride_w + w];
+          } else if (lane == 0) {
+            atomicOr(a.err, kErrBadSlot);
+          }
+          fence_proxy_async_global();  // the producer's TMA copies of this tile come after the ring arrive
+        }
         mbar_arrive(&sm.ring_full[chunk % kRingSlots]);
       }
     }
@@ -1050,10 +1080,23 @@ __global__ void __launch_bounds__(kThreads, 1) paged_decode_kernel(const __grid_
     }
     if (!ok) flag_error(a, sm, kErrWaitTimeout);
 
-    // Sequences without context own no tile: their outputs are zeros.
+    // Sequences without context own no tile: their outputs are zeros (and
+    // a fused append still writes their row, as the reference's write would).
     for (int b = c; b < a.batch; b += ctas) {
       if (sm.tiles_before[b + 1] == sm.tiles_before[b]) {
         for (int h = 0; h < a.num_heads; ++h) store_out(a, b, h, e, 0.f);
+        if (a.new_slots != nullptr) {
+          const int64_t slot = a.new_slots[b];
+          const int words = kvh * (kD * 2 / 16);
+          if (slot >= 0 && slot < a.num_slots) {
+            for (int w = e; w < words; w += kEpilogueThreads) {
+              a.kc_words[slot * words + w] = a.k_new[b * a.k_new_stride_w + w];
+              a.vc_words[slot * words + w] = a.v_new[b * a.v_new_stride_w + w];
+            }
+          } else if (e == 0) {
+            atomicOr(a.err, kErrBadSlot);
+          }
+        }
       }
     }
   }
@@ -1121,6 +1164,14 @@ extern "C" int nvk_paged_decode_workspace_size(int batch, int num_heads, int num
 namespace nvk {
 namespace {
 
+// This step's token rows for a fused append (see nvk_paged_decode_append).
+struct AppendRows {
+  const void* key;
+  const void* value;
+  int64_t key_stride, value_stride;  // elements between consecutive tokens
+  const int64_t* slots;
+};
+
 // Where a gathering decode call stores its rows (see nvk_paged_decode_gather).
 struct GatherTargets {
   void* const* out_peers;
@@ -1131,7 +1182,8 @@ struct GatherTargets {
 int decode_impl(void* out, const void* query, const void* key_cache, const void* value_cache, int num_blocks,
                 int block_size, const int32_t* block_tables, int block_table_stride, int max_blocks_per_seq,
                 const int32_t* context_lens, int batch, int num_heads, int num_kv_heads, int head_dim, float scale,
-                int num_ctas, void* workspace, size_t workspace_bytes, const GatherTargets* gt, nvk_stream_t stream) {
+                int num_ctas, void* workspace, size_t workspace_bytes, const GatherTargets* gt, const AppendRows* ap,
+                nvk_stream_t stream) {
   if (batch < 0 || num_blocks <= 0 || num_heads <= 0 || num_kv_heads <= 0 || num_ctas < 0)
     return fail(NVK_ERR_INVALID_ARGUMENT, "paged_decode: bad sizes (batch=%d blocks=%d heads=%d kv_heads=%d ctas=%d)",
                 batch, num_blocks, num_heads, num_kv_heads, num_ctas);
@@ -1153,6 +1205,14 @@ int decode_impl(void* out, const void* query, const void* key_cache, const void*
     return fail(NVK_ERR_INVALID_ARGUMENT, "paged_decode: null pointer");
   if ((!gt && !aligned16(out)) || !aligned16(query))
     return fail(NVK_ERR_INVALID_ARGUMENT, "paged_decode: q/out must be 16-byte aligned");
+  if (ap) {
+    const int64_t row = static_cast<int64_t>(num_kv_heads) * kD;
+    if (!ap->key || !ap->value || !ap->slots || !aligned16(ap->key) || !aligned16(ap->value) ||
+        ap->key_stride < row || ap->value_stride < row || ap->key_stride % 8 != 0 || ap->value_stride % 8 != 0)
+      return fail(NVK_ERR_INVALID_ARGUMENT,
+                  "paged_decode_append: new rows null, misaligned or strides (%lld, %lld) below a row / not 16-byte",
+                  (long long)ap->key_stride, (long long)ap->value_stride);
+  }
   int ctas = 0;
   int rc = resolve_ctas(num_ctas, &ctas);
   if (rc != NVK_OK) return rc;
@@ -1197,6 +1257,14 @@ int decode_impl(void* out, const void* query, const void* key_cache, const void*
     }
     a.my_sig = gt ? static_cast<uint32_t*>(gt->signal_peers[gt->rank]) : nullptr;
     a.done = reinterpret_cast<int*>(ws + 64);
+    a.new_slots = ap ? ap->slots + b0 : nullptr;
+    a.k_new = ap ? static_cast<const uint4*>(ap->key) + b0 * (ap->key_stride / 8) : nullptr;
+    a.v_new = ap ? static_cast<const uint4*>(ap->value) + b0 * (ap->value_stride / 8) : nullptr;
+    a.k_new_stride_w = ap ? ap->key_stride / 8 : 0;
+    a.v_new_stride_w = ap ? ap->value_stride / 8 : 0;
+    a.kc_words = static_cast<uint4*>(const_cast<void*>(key_cache));
+    a.vc_words = static_cast<uint4*>(const_cast<void*>(value_cache));
+    a.num_slots = rows;
     a.query = qb;
     a.block_tables = block_tables + static_cast<int64_t>(b0) * block_table_stride;
     a.context_lens = context_lens + b0;
@@ -1239,16 +1307,31 @@ extern "C" int nvk_paged_decode(void* out, const void* query, const void* key_ca
                                 size_t workspace_bytes, nvk_stream_t stream) {
   return nvk::decode_impl(out, query, key_cache, value_cache, num_blocks, block_size, block_tables,
                           block_table_stride, max_blocks_per_seq, context_lens, batch, num_heads, num_kv_heads,
-                          head_dim, scale, num_ctas, workspace, workspace_bytes, nullptr, stream);
+                          head_dim, scale, num_ctas, workspace, workspace_bytes, nullptr, nullptr, stream);
 }
 
-extern "C" int nvk_paged_decode_gather(const void* query, const void* key_cache, const void* value_cache,
+extern "C" int nvk_paged_decode_append(void* out, const void* query, void* key_cache, void* value_cache,
+                                       int num_blocks, int block_size, const int32_t* block_tables,
+                                       int block_table_stride, int max_blocks_per_seq, const int32_t* context_lens,
+                                       int batch, int num_heads, int num_kv_heads, int head_dim, float scale,
+                                       int num_ctas, void* workspace, size_t workspace_bytes, const void* key,
+                                       const void* value, int64_t key_token_stride, int64_t value_token_stride,
+                                       const int64_t* slot_mapping, nvk_stream_t stream) {
+  const nvk::AppendRows ap{key, value, key_token_stride, value_token_stride, slot_mapping};
+  return nvk::decode_impl(out, query, key_cache, value_cache, num_blocks, block_size, block_tables,
+                          block_table_stride, max_blocks_per_seq, context_lens, batch, num_heads, num_kv_heads,
+                          head_dim, scale, num_ctas, workspace, workspace_bytes, nullptr, &ap, stream);
+}
+
+extern "C" int nvk_paged_decode_gather(const void* query, void* key_cache, void* value_cache,
                                        int num_blocks, int block_size, const int32_t* block_tables,
                                        int block_table_stride, int max_blocks_per_seq, const int32_t* context_lens,
                                        int batch, int num_heads, int num_kv_heads, int head_dim, float scale,
                                        int num_ctas, void* workspace, size_t workspace_bytes,
                                        void* const* out_peers, void* const* signal_peers, int world, int rank,
-                                       int out_heads, int head_offset, nvk_stream_t stream) {
+                                       int out_heads, int head_offset, const void* key, const void* value,
+                                       int64_t key_token_stride, int64_t value_token_stride,
+                                       const int64_t* slot_mapping, nvk_stream_t stream) {
   using namespace nvk;
   if (world < 1 || world > NVK_MAX_PEERS || rank < 0 || rank >= world)
     return fail(NVK_ERR_INVALID_ARGUMENT, "paged_decode_gather: rank %d / world %d invalid (world 1..%d)", rank,
@@ -1263,9 +1346,10 @@ extern "C" int nvk_paged_decode_gather(const void* query, const void* key_cache,
       return fail(NVK_ERR_INVALID_ARGUMENT, "paged_decode_gather: rank %d buffers null or misaligned", r);
   }
   const GatherTargets gt{out_peers, signal_peers, world, rank, out_heads, head_offset};
+  const AppendRows ap{key, value, key_token_stride, value_token_stride, slot_mapping};
   return decode_impl(nullptr, query, key_cache, value_cache, num_blocks, block_size, block_tables,
                      block_table_stride, max_blocks_per_seq, context_lens, batch, num_heads, num_kv_heads, head_dim,
-                     scale, num_ctas, workspace, workspace_bytes, &gt, stream);
+                     scale, num_ctas, workspace, workspace_bytes, &gt, slot_mapping ? &ap : nullptr, stream);
 }
 
 // ---------------------------------------------------------------------------

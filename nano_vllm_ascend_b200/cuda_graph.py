@@ -18,7 +18,7 @@ reference's per-task workspace, :229-242).
 from __future__ import annotations
 
 import math
-from contextlib import contextmanager
+from contextlib import contextmanager, nullcontext
 from dataclasses import dataclass, field
 from typing import Any, Iterator
 
@@ -121,9 +121,12 @@ class DecodeGraphRunner:
     """
 
     def __init__(self, model, kv_cache, batch_sizes: list[int], max_model_len: int | None = None,
-                 block_size: int | None = None, device: torch.device | str | None = None) -> None:
+                 block_size: int | None = None, device: torch.device | str | None = None,
+                 fuse_appends: bool = True) -> None:
         self.model = model
         self.kv_cache = kv_cache
+        # Decode appends fused into the attention kernels (PagedKVCache.deferred_appends).
+        self.fuse_appends = fuse_appends
         self.batch_sizes = set(batch_sizes)
         self.max_blocks_per_seq = None
         if max_model_len is not None and block_size is not None:
@@ -179,7 +182,9 @@ class DecodeGraphRunner:
         )
 
     def _run_model(self, entry: DecodeGraphEntry, static_md):
-        with capture_decode_graph_tasks(entry):
+        defer = getattr(self.kv_cache, "deferred_appends", None)
+        fused = defer() if (self.fuse_appends and defer is not None) else nullcontext()
+        with capture_decode_graph_tasks(entry), fused:
             return self.model(
                 input_ids_flat=entry.input_ids,
                 position_ids_flat=entry.position_ids,

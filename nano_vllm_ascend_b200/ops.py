@@ -97,11 +97,18 @@ def paged_decode(
     scale: float,
     workspace: torch.Tensor,
     num_ctas: int = 0,
+    new_key: torch.Tensor | None = None,
+    new_value: torch.Tensor | None = None,
+    slot_mapping: torch.Tensor | None = None,
 ) -> torch.Tensor:
     """Paged GQA decode attention into ``out`` ([B, H, D] bf16).
 
     ``workspace`` (uint8, zeroed once) must hold decode_workspace_bytes(B, H,
     KVH, D, num_ctas); calls sharing it must be ordered on one stream.
+    With ``new_key``/``new_value`` ([B, KVH, D] rows) and ``slot_mapping``
+    ([B] int64) the step's append is fused in: the rows are written to the
+    pool at their slots (each sequence's last context position) and attended
+    over, as kv_append followed by paged_decode.
     """
     dev = query.device
     for name, t in (("out", out), ("query", query), ("key_cache", key_cache), ("value_cache", value_cache),
@@ -121,13 +128,43 @@ def paged_decode(
         raise ValueError("paged_decode: block_tables must be int32 [batch, max_blocks] with unit column stride")
     if context_lens.dtype != torch.int32 or context_lens.numel() != batch or not context_lens.is_contiguous():
         raise ValueError("paged_decode: context_lens must be a contiguous int32 [batch] device tensor")
+    ws_bytes = workspace.numel() * workspace.element_size()
+    if slot_mapping is None:
+        _lib.call(
+            "nvk_paged_decode", _ptr(out), _ptr(query), _ptr(key_cache), _ptr(value_cache), num_blocks, block_size,
+            _ptr(block_tables), block_tables.stride(0), block_tables.shape[1], _ptr(context_lens), batch, num_heads,
+            kvh, head_dim, float(scale), int(num_ctas), _ptr(workspace), ws_bytes, _stream(dev),
+        )
+        return out
+    new_key, new_value, slot_mapping = check_new_rows(new_key, new_value, slot_mapping, batch, kvh, head_dim, dev)
     _lib.call(
-        "nvk_paged_decode", _ptr(out), _ptr(query), _ptr(key_cache), _ptr(value_cache), num_blocks, block_size,
-        _ptr(block_tables), block_tables.stride(0), block_tables.shape[1], _ptr(context_lens), batch, num_heads,
-        kvh, head_dim, float(scale), int(num_ctas), _ptr(workspace), workspace.numel() * workspace.element_size(),
-        _stream(dev),
+        "nvk_paged_decode_append", _ptr(out), _ptr(query), _ptr(key_cache), _ptr(value_cache), num_blocks,
+        block_size, _ptr(block_tables), block_tables.stride(0), block_tables.shape[1], _ptr(context_lens), batch,
+        num_heads, kvh, head_dim, float(scale), int(num_ctas), _ptr(workspace), ws_bytes, _ptr(new_key),
+        _ptr(new_value), new_key.stride(0), new_value.stride(0), _ptr(slot_mapping), _stream(dev),
     )
     return out
+
+
+def check_new_rows(new_key, new_value, slot_mapping, batch: int, kvh: int, head_dim: int, dev):
+    """Validates the one-token-per-sequence rows of a fused append; returns them usable by the kernel."""
+    if new_key is None or new_value is None:
+        raise ValueError("paged_decode: a fused append needs new_key, new_value and slot_mapping")
+    for name, t in (("new_key", new_key), ("new_value", new_value), ("slot_mapping", slot_mapping)):
+        _require_cuda(name, t, dev)
+    if new_key.dtype != _BF16 or new_value.dtype != _BF16:
+        raise ValueError("paged_decode: new_key/new_value must be bfloat16")
+    _require_rows("new_key", new_key)
+    _require_rows("new_value", new_value)
+    if new_key.shape != (batch, kvh, head_dim) or new_value.shape != new_key.shape:
+        raise ValueError(f"kv shape mismatch: got {tuple(new_key.shape)} / {tuple(new_value.shape)}")
+    if slot_mapping.dtype != torch.int64 or slot_mapping.numel() != batch:
+        raise ValueError("paged_decode: slot_mapping must be int64 with one entry per sequence")
+    if (new_key.stride(0) * 2) % 16 or new_key.data_ptr() % 16:
+        new_key = new_key.contiguous()
+    if (new_value.stride(0) * 2) % 16 or new_value.data_ptr() % 16:
+        new_value = new_value.contiguous()
+    return new_key, new_value, slot_mapping.contiguous()
 
 
 def decode_error_word(workspace: torch.Tensor) -> int:

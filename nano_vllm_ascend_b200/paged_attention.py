@@ -5,7 +5,8 @@ src/nanovllm_ascend/layers/npu_paged_attention.py:14-100).
 ``forward(q, key_cache, value_cache, block_tables, context_lens)`` returns a
 new [tokens, num_heads, head_dim] tensor like the reference. ``context_lens``
 may be the reference's CPU int32 tensor (it is copied to the device) or a
-device tensor (the CUDA-graph path). Inside a decode-graph capture the
+device tensor (the CUDA-graph path). Inside PagedKVCache.deferred_appends()
+(the CUDA-graph decode runner) the layer's append is fused into the kernel. Inside a decode-graph capture the
 workspace comes from the capturing graph entry, mirroring the per-task
 workspace of src/nanovllm_ascend/npu/acl_graph.py:229-242.
 """
@@ -17,6 +18,7 @@ from torch import nn
 
 from . import ops
 from .cuda_graph import PagedAttentionGraphTask, current_decode_graph_entry, record_paged_attention_task
+from .paged_kv_cache import take_deferred
 
 _NUM_SMS: dict[int, int] = {}
 _WORKSPACES: dict[int, torch.Tensor] = {}
@@ -79,8 +81,16 @@ class PagedAttention(nn.Module):
                 workspace = shared_workspace(device, self.workspace_bytes(total_tokens))
             ctx = context_lens if context_lens.is_cuda else context_lens.to(device=device, dtype=torch.int32)
             tables = block_tables if block_tables.is_cuda else block_tables.to(device)
+            # This layer's append, when PagedKVCache.deferred_appends() held it
+            # back, is done by the decode kernel itself.
+            pending = take_deferred(key_cache)
+            if pending is not None and pending[0].shape[0] != total_tokens:
+                ops.kv_append(key_cache, value_cache, *pending)  # not one row per sequence: plain append first
+                pending = None
+            new_key, new_value, slots = pending if pending is not None else (None, None, None)
             ops.paged_decode(output, q.contiguous(), key_cache, value_cache, tables.to(torch.int32),
-                             ctx.to(torch.int32), self.scale, workspace, self.num_ctas)
+                             ctx.to(torch.int32), self.scale, workspace, self.num_ctas, new_key=new_key,
+                             new_value=new_value, slot_mapping=slots)
         if entry is not None:
             record_paged_attention_task(PagedAttentionGraphTask(
                 query=q, key_cache=key_cache, value_cache=value_cache, num_kv_heads=self.num_key_value_heads,

@@ -24,7 +24,7 @@ import torch
 import torch.distributed as dist
 
 from . import _lib
-from .ops import _BF16, _ptr, _require_cuda, _stream
+from .ops import _BF16, _ptr, _require_cuda, _stream, check_new_rows
 
 
 class _DeviceBytes:
@@ -100,8 +100,12 @@ class PeerGather:
     # ------------------------------------------------------------ decode ---
     def decode(self, query: torch.Tensor, key_cache: torch.Tensor, value_cache: torch.Tensor,
                block_tables: torch.Tensor, context_lens: torch.Tensor, scale: float, workspace: torch.Tensor,
-               head_offset: int, slot: int | None = None, num_ctas: int = 0) -> torch.Tensor:
-        """Decode over this rank's heads; returns the gathered [batch, out_heads, D] output of the slot used."""
+               head_offset: int, slot: int | None = None, num_ctas: int = 0, new_key: torch.Tensor | None = None,
+               new_value: torch.Tensor | None = None, slot_mapping: torch.Tensor | None = None) -> torch.Tensor:
+        """Decode over this rank's heads; returns the gathered [batch, out_heads, D] output of the slot used.
+
+        With ``new_key``/``new_value``/``slot_mapping`` the step's append of
+        this rank's KV heads is fused in (see ops.paged_decode)."""
         dev = query.device
         for name, t in (("query", query), ("key_cache", key_cache), ("value_cache", value_cache),
                         ("block_tables", block_tables), ("context_lens", context_lens), ("workspace", workspace)):
@@ -119,6 +123,9 @@ class PeerGather:
             raise ValueError("paged_decode_gather: block_tables must be int32 [batch, max_blocks]")
         if context_lens.dtype != torch.int32 or context_lens.numel() != batch or not context_lens.is_contiguous():
             raise ValueError("paged_decode_gather: context_lens must be a contiguous int32 [batch] device tensor")
+        if slot_mapping is not None:
+            new_key, new_value, slot_mapping = check_new_rows(new_key, new_value, slot_mapping, batch, kvh, head_dim,
+                                                              dev)
         if slot is None:
             slot = self.next_slot()
         outs, sigs = self._slot_ptrs(slot)
@@ -127,7 +134,8 @@ class PeerGather:
             _ptr(block_tables), block_tables.stride(0), block_tables.shape[1], _ptr(context_lens), batch, num_heads,
             kvh, head_dim, float(scale), int(num_ctas), _ptr(workspace),
             workspace.numel() * workspace.element_size(), outs, sigs, self.world, self.rank, self.out_heads,
-            int(head_offset), _stream(dev),
+            int(head_offset), _ptr(new_key), _ptr(new_value), 0 if new_key is None else new_key.stride(0),
+            0 if new_value is None else new_value.stride(0), _ptr(slot_mapping), _stream(dev),
         )
         return self.output(slot)
 
