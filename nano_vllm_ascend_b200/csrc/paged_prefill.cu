@@ -12,10 +12,12 @@
 //   warp 4 (producer): TMA loads of the Q tile once, then 128-key K and V
 //     tiles (one pool block each, 128-byte swizzle = the canonical UMMA
 //     operand layout) into a 2-stage ring.
-//   warp 5 (MMA): allocates 256 TMEM columns (S: 0-127, O: 128-255) and one
-//     lane issues S = Q K^T (8 x M128 N128 K16, both K-major) and
-//     O += P V (8 x M128 N128 K16, P K-major from smem, V MN-major), with
-//     tcgen05.commit signalling the mbarriers.
+//   warp 5 (MMA): allocates 512 TMEM columns (S double buffered: 0-127 and
+//     128-255, O: 256-383) and one lane issues S = Q K^T (8 x M128 N128 K16,
+//     both K-major) one key tile ahead of O += P V (8 x M128 N128 K16, P
+//     K-major from smem, V MN-major), so the tensor core computes S(j+1)
+//     while the softmax warps work on tile j; tcgen05.commit signals the
+//     mbarriers.
 //   warps 0-3 (softmax): thread r owns query row r = TMEM lane r: loads its
 //     S row (tcgen05.ld), masks, base-2 online softmax with lazy rescaling
 //     of O in TMEM (only when the running max grows by more than 2^8), writes
@@ -39,7 +41,7 @@ constexpr int kSoftmaxThreads = 128;
 constexpr int kProducerWarp = 4;
 constexpr int kMmaWarp = 5;
 constexpr int kThreads = 6 * 32;
-constexpr uint32_t kTmemCols = 256;
+constexpr uint32_t kTmemCols = 512;  // S0, S1, O (128 each) rounded up to a power of two
 constexpr float kRescaleThreshold = 8.0f;
 
 struct PrefillArgs {
@@ -66,7 +68,8 @@ struct PrefillSmem {
   uint64_t full_k[kStages];
   uint64_t full_v[kStages];
   uint64_t kv_empty[kStages];
-  uint64_t s_full;
+  uint64_t s_full[2];
+  uint64_t s_free[2];
   uint64_t p_full;
   uint64_t o_done;
   uint64_t fin;
@@ -120,7 +123,10 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
       mbar_init(&sm.full_v[s], 1);
       mbar_init(&sm.kv_empty[s], 1);
     }
-    mbar_init(&sm.s_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&sm.s_full[i], 1);
+      mbar_init(&sm.s_free[i], kSoftmaxThreads);
+    }
     mbar_init(&sm.p_full, kSoftmaxThreads);
     mbar_init(&sm.o_done, 1);
     mbar_init(&sm.fin, 1);
@@ -135,8 +141,8 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = sm.tmem_base;
-  const uint32_t tmem_s = tmem;
-  const uint32_t tmem_o = tmem + kRows;
+  const uint32_t tmem_s = tmem;            // S(j) in columns (j & 1) * 128
+  const uint32_t tmem_o = tmem + 2 * kRows;
 
   if (warp == kProducerWarp) {
     // -------------------------------------------------------- producer ----
@@ -189,22 +195,30 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
       const uint32_t q_addr = smem_u32(sm.q), p_addr = smem_u32(sm.p);
       bool ok = mbar_wait(&sm.bar_q, 0);
       if (!ok) flag_error(a, sm, kErrWaitTimeout);
-      for (int j = 0; ok && j < n_kv; ++j) {
+      // S(j) = Q K(j)^T into S buffer j & 1, once K(j) has landed and the
+      // softmax has read S(j-2) out of that buffer.
+      auto issue_s = [&](int j) -> bool {
         const int s = j & 1;
-        const uint32_t ph = (j >> 1) & 1;
-        if (!mbar_wait(&sm.full_k[s], ph)) { ok = false; break; }
+        if (!mbar_wait(&sm.full_k[s], (j >> 1) & 1)) return false;
+        if (j >= 2 && !mbar_wait(&sm.s_free[s], ((j >> 1) - 1) & 1)) return false;
         tc_fence_after();
         const uint32_t k_addr = smem_u32(sm.k[s]);
 #pragma unroll
         for (int kk = 0; kk < kD / 16; ++kk) {
           const uint32_t off = (kk >> 2) * kHalfBytes + (kk & 3) * 32;
-          umma_f16_ss(tmem_s, smem_desc_sw128(q_addr + off, 16, 1024), smem_desc_sw128(k_addr + off, 16, 1024),
-                      idesc_qk, kk > 0);
+          umma_f16_ss(tmem_s + s * kRows, smem_desc_sw128(q_addr + off, 16, 1024),
+                      smem_desc_sw128(k_addr + off, 16, 1024), idesc_qk, kk > 0);
         }
-        umma_commit(&sm.s_full);
+        umma_commit(&sm.s_full[s]);
+        return true;
+      };
+      if (ok) ok = issue_s(0);
+      for (int j = 0; ok && j < n_kv; ++j) {
+        const int s = j & 1;
+        if (j + 1 < n_kv && !issue_s(j + 1)) { ok = false; break; }
         if (!mbar_wait(&sm.p_full, j & 1)) { ok = false; break; }
         tc_fence_after();
-        if (!mbar_wait(&sm.full_v[s], ph)) { ok = false; break; }
+        if (!mbar_wait(&sm.full_v[s], (j >> 1) & 1)) { ok = false; break; }
         const uint32_t v_addr = smem_u32(sm.v[s]);
 #pragma unroll
         for (int kk = 0; kk < kRows / 16; ++kk) {
@@ -212,7 +226,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
           const uint64_t vb = smem_desc_sw128(v_addr + kk * 16 * 128, kHalfBytes, 1024);
           umma_f16_ss(tmem_o, pa, vb, idesc_pv, (j > 0 || kk > 0) ? 1u : 0u);
         }
-        umma_commit(&sm.kv_empty[s]);
+        umma_commit(&sm.kv_empty[s]);  // K(j) was read by S(j), which P(j) already depended on
         umma_commit(&sm.o_done);
       }
       if (!ok) flag_error(a, sm, kErrWaitTimeout);
@@ -231,25 +245,29 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
     bool ok = true;
     for (int j = 0; j < n_kv; ++j) {
       // warp-uniform outcome: the tcgen05.ld/st below need a converged warp
-      if (!__all_sync(0xffffffffu, mbar_wait(&sm.s_full, j & 1))) { ok = false; break; }
+      const int sb = j & 1;
+      if (!__all_sync(0xffffffffu, mbar_wait(&sm.s_full[sb], (j >> 1) & 1))) { ok = false; break; }
       tc_fence_after();
       uint32_t sr[4][32];
 #pragma unroll
-      for (int c = 0; c < 4; ++c) tmem_ld32(tmem_s + t_lane + c * 32, sr[c]);
+      for (int c = 0; c < 4; ++c) tmem_ld32(tmem_s + sb * kRows + t_lane + c * 32, sr[c]);
       tmem_ld_wait();
+      tc_fence_before();
+      mbar_arrive(&sm.s_free[sb]);  // S buffer sb may take S(j+2)
       const int kbase = j * kRows;
       const bool need_mask = kbase + kRows - 1 > lim;
-      float mt = -INFINITY;
+      // The max is taken over raw scores (scale > 0), the scale folded into
+      // the exponent's FMA below.
+      float mraw = -INFINITY;
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
 #pragma unroll
         for (int e = 0; e < 32; ++e) {
-          float x = __uint_as_float(sr[c][e]) * a.scale_log2;
-          if (need_mask && kbase + c * 32 + e > lim) x = -INFINITY;
-          sr[c][e] = __float_as_uint(x);
-          mt = fmaxf(mt, x);
+          if (need_mask && kbase + c * 32 + e > lim) sr[c][e] = __float_as_uint(-INFINITY);
+          mraw = fmaxf(mraw, __uint_as_float(sr[c][e]));
         }
       }
+      const float mt = mraw * a.scale_log2;
       const float m_new = fmaxf(m, mt);
       const bool resc = m_new > m + kRescaleThreshold;
       const float alpha = resc ? fast_exp2(m - m_new) : 1.f;
@@ -273,7 +291,8 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
         l *= alpha;
         m = m_new;
       }
-      const float mu = (m == -INFINITY) ? 0.f : m;
+      const float neg_mu = (m == -INFINITY) ? 0.f : -m;
+      const float sc = a.scale_log2;
       float sum = 0.f;
 #pragma unroll
       for (int c8 = 0; c8 < 16; ++c8) {  // 16 chunks of 8 keys
@@ -281,8 +300,8 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
         uint32_t w[4];
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
-          const float p0 = fast_exp2(__uint_as_float(sr[c][e0 + 2 * e]) - mu);
-          const float p1 = fast_exp2(__uint_as_float(sr[c][e0 + 2 * e + 1]) - mu);
+          const float p0 = fast_exp2(fmaf(__uint_as_float(sr[c][e0 + 2 * e]), sc, neg_mu));
+          const float p1 = fast_exp2(fmaf(__uint_as_float(sr[c][e0 + 2 * e + 1]), sc, neg_mu));
           sum += p0 + p1;
           w[e] = pack_bf16x2(p0, p1);
         }
