@@ -11,7 +11,9 @@
 // One CTA = 128 query rows of one sequence x one query head.
 //   warp 4 (producer): TMA loads of the Q tile once, then 128-key K and V
 //     tiles (one pool block each, 128-byte swizzle = the canonical UMMA
-//     operand layout) into a 2-stage ring.
+//     operand layout): K into a 3-stage ring freed as soon as S has read it,
+//     V into a 2-stage ring freed by PV; K runs two tiles ahead of V, and
+//     the block ids come 32 at a time (one parallel load per warp).
 //   warp 5 (MMA): allocates 512 TMEM columns (S double buffered: 0-127 and
 //     128-255, O: 256-383) and one lane issues S = Q K^T (8 x M128 N128 K16,
 //     both K-major) one key tile ahead of O += P V (8 x M128 N128 K16, P
@@ -36,7 +38,8 @@ constexpr int kD = 128;
 constexpr int kRows = 128;              // query rows per CTA, keys per KV tile
 constexpr int kHalfBytes = kRows * 128; // one 64-dim half of a 128-row tile
 constexpr int kTileBytes = 2 * kHalfBytes;
-constexpr int kStages = 2;
+constexpr int kKStages = 3;
+constexpr int kVStages = 2;
 constexpr int kSoftmaxThreads = 128;
 constexpr int kProducerWarp = 4;
 constexpr int kMmaWarp = 5;
@@ -61,13 +64,12 @@ struct PrefillArgs {
 
 struct PrefillSmem {
   alignas(1024) uint8_t q[kTileBytes];
-  alignas(1024) uint8_t k[kStages][kTileBytes];
-  alignas(1024) uint8_t v[kStages][kTileBytes];
+  alignas(1024) uint8_t k[kKStages][kTileBytes];
+  alignas(1024) uint8_t v[kVStages][kTileBytes];
   alignas(1024) uint8_t p[kTileBytes];
   uint64_t bar_q;
-  uint64_t full_k[kStages];
-  uint64_t full_v[kStages];
-  uint64_t kv_empty[kStages];
+  uint64_t full_k[kKStages], k_empty[kKStages];
+  uint64_t full_v[kVStages], v_empty[kVStages];
   uint64_t s_full[2];
   uint64_t s_free[2];
   uint64_t p_full;
@@ -76,6 +78,8 @@ struct PrefillSmem {
   uint32_t tmem_base;
   volatile int abort;
 };
+
+static_assert(sizeof(PrefillSmem) + 1024 <= 232448, "prefill shared memory exceeds the 227 KB per-CTA limit");
 
 __device__ __forceinline__ void flag_error(const PrefillArgs& a, PrefillSmem& sm, int code) {
   if (a.err) atomicOr(a.err, code);
@@ -118,10 +122,13 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
 
   if (tid == 0) {
     mbar_init(&sm.bar_q, 1);
-    for (int s = 0; s < kStages; ++s) {
+    for (int s = 0; s < kKStages; ++s) {
       mbar_init(&sm.full_k[s], 1);
+      mbar_init(&sm.k_empty[s], 1);
+    }
+    for (int s = 0; s < kVStages; ++s) {
       mbar_init(&sm.full_v[s], 1);
-      mbar_init(&sm.kv_empty[s], 1);
+      mbar_init(&sm.v_empty[s], 1);
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&sm.s_full[i], 1);
@@ -146,6 +153,8 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
 
   if (warp == kProducerWarp) {
     // -------------------------------------------------------- producer ----
+    // The whole warp walks the tiles (block ids come 32 at a time, one per
+    // lane); lane 0 waits for ring slots and issues the copies.
     if (lane == 0) {
       tma_prefetch_desc(&qmap);
       tma_prefetch_desc(&kmap);
@@ -153,39 +162,72 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
       mbar_arrive_expect_tx(&sm.bar_q, kTileBytes);
       tma_load_3d(sm.q, &qmap, &sm.bar_q, 0, h, q0 + qt * kRows);
       tma_load_3d(sm.q + kHalfBytes, &qmap, &sm.bar_q, 64, h, q0 + qt * kRows);
-      const int32_t* bt = a.block_tables + static_cast<int64_t>(b) * a.bt_stride;
-      int issued = 0;
-      for (int j = 0; j < n_kv && !sm.abort; ++j) {
-        const int s = j & 1;
-        if (j >= kStages && !mbar_wait(&sm.kv_empty[s], ((j >> 1) - 1) & 1)) {
-          flag_error(a, sm, kErrWaitTimeout);
-          break;
-        }
-        int row;
-        if (a.paged) {
-          int blk = bt[j];
+    }
+    const int32_t* bt = a.block_tables + static_cast<int64_t>(b) * a.bt_stride;
+    // First pool row of tile j; `chunk` holds this lane's id of the current
+    // 32-tile chunk and is refreshed when j crosses a multiple of 32 (each
+    // caller passes its own register and consecutive j).
+    auto row_of = [&](int j, int& chunk) -> int {
+      if ((j & 31) == 0) {
+        const int jj = j + lane;
+        int blk = 0;
+        if (a.paged && jj < n_kv) {
+          blk = bt[jj];
           if (blk < 0 || blk >= a.num_blocks) {
             if (a.err) atomicOr(a.err, kErrBadBlockId);
             blk = a.num_blocks;  // fully outside the tensor map: zero fill
           }
-          row = blk * kRows;
-        } else {
-          row = kv_row0 + j * kRows;
         }
-        mbar_arrive_expect_tx(&sm.full_k[s], kTileBytes);
-        tma_load_3d(sm.k[s], &kmap, &sm.full_k[s], 0, g, row);
-        tma_load_3d(sm.k[s] + kHalfBytes, &kmap, &sm.full_k[s], 64, g, row);
-        mbar_arrive_expect_tx(&sm.full_v[s], kTileBytes);
-        tma_load_3d(sm.v[s], &vmap, &sm.full_v[s], 0, g, row);
-        tma_load_3d(sm.v[s] + kHalfBytes, &vmap, &sm.full_v[s], 64, g, row);
-        ++issued;
+        chunk = blk;
       }
+      const int blk = __shfl_sync(0xffffffffu, chunk, j & 31);
+      return a.paged ? blk * kRows : kv_row0 + j * kRows;
+    };
+    int k_chunk = 0, v_chunk = 0, k_issued = 0, v_issued = 0;
+    bool ok = true;
+    auto load_k = [&](int j) {
+      const int row = row_of(j, k_chunk);
+      const int st = j % kKStages;
+      if (lane == 0) {
+        if (j >= kKStages && !mbar_wait(&sm.k_empty[st], ((j / kKStages) - 1) & 1)) {
+          ok = false;
+        } else {
+          mbar_arrive_expect_tx(&sm.full_k[st], kTileBytes);
+          tma_load_3d(sm.k[st], &kmap, &sm.full_k[st], 0, g, row);
+          tma_load_3d(sm.k[st] + kHalfBytes, &kmap, &sm.full_k[st], 64, g, row);
+        }
+      }
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      k_issued += ok ? 1 : 0;
+    };
+    auto load_v = [&](int j) {
+      const int row = row_of(j, v_chunk);
+      const int st = j % kVStages;
+      if (lane == 0) {
+        if (j >= kVStages && !mbar_wait(&sm.v_empty[st], ((j / kVStages) - 1) & 1)) {
+          ok = false;
+        } else {
+          mbar_arrive_expect_tx(&sm.full_v[st], kTileBytes);
+          tma_load_3d(sm.v[st], &vmap, &sm.full_v[st], 0, g, row);
+          tma_load_3d(sm.v[st] + kHalfBytes, &vmap, &sm.full_v[st], 64, g, row);
+        }
+      }
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      v_issued += ok ? 1 : 0;
+    };
+    for (int j = 0; ok && j < 2 && j < n_kv; ++j) load_k(j);
+    for (int t = 0; ok && t < n_kv && !sm.abort; ++t) {
+      if (t + 2 < n_kv) load_k(t + 2);
+      if (ok) load_v(t);
+    }
+    if (lane == 0) {
+      if (!ok) flag_error(a, sm, kErrWaitTimeout);
       // Drain every copy this CTA issued before it may exit.
       (void)mbar_wait(&sm.bar_q, 0);
-      for (int j = max(0, issued - kStages); j < issued; ++j) {
-        (void)mbar_wait(&sm.full_k[j & 1], (j >> 1) & 1);
-        (void)mbar_wait(&sm.full_v[j & 1], (j >> 1) & 1);
-      }
+      for (int j = max(0, k_issued - kKStages); j < k_issued; ++j)
+        (void)mbar_wait(&sm.full_k[j % kKStages], (j / kKStages) & 1);
+      for (int j = max(0, v_issued - kVStages); j < v_issued; ++j)
+        (void)mbar_wait(&sm.full_v[j % kVStages], (j / kVStages) & 1);
     }
   } else if (warp == kMmaWarp) {
     // ------------------------------------------------------------- MMA ----
@@ -198,11 +240,11 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
       // S(j) = Q K(j)^T into S buffer j & 1, once K(j) has landed and the
       // softmax has read S(j-2) out of that buffer.
       auto issue_s = [&](int j) -> bool {
-        const int s = j & 1;
-        if (!mbar_wait(&sm.full_k[s], (j >> 1) & 1)) return false;
+        const int s = j & 1, ks = j % kKStages;
+        if (!mbar_wait(&sm.full_k[ks], (j / kKStages) & 1)) return false;
         if (j >= 2 && !mbar_wait(&sm.s_free[s], ((j >> 1) - 1) & 1)) return false;
         tc_fence_after();
-        const uint32_t k_addr = smem_u32(sm.k[s]);
+        const uint32_t k_addr = smem_u32(sm.k[ks]);
 #pragma unroll
         for (int kk = 0; kk < kD / 16; ++kk) {
           const uint32_t off = (kk >> 2) * kHalfBytes + (kk & 3) * 32;
@@ -210,6 +252,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
                       smem_desc_sw128(k_addr + off, 16, 1024), idesc_qk, kk > 0);
         }
         umma_commit(&sm.s_full[s]);
+        umma_commit(&sm.k_empty[ks]);  // K(j) slot free once S(j) has read it
         return true;
       };
       if (ok) ok = issue_s(0);
@@ -226,7 +269,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
           const uint64_t vb = smem_desc_sw128(v_addr + kk * 16 * 128, kHalfBytes, 1024);
           umma_f16_ss(tmem_o, pa, vb, idesc_pv, (j > 0 || kk > 0) ? 1u : 0u);
         }
-        umma_commit(&sm.kv_empty[s]);  // K(j) was read by S(j), which P(j) already depended on
+        umma_commit(&sm.v_empty[s]);
         umma_commit(&sm.o_done);
       }
       if (!ok) flag_error(a, sm, kErrWaitTimeout);
