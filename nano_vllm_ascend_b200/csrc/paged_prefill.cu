@@ -12,19 +12,19 @@
 //   warp 4 (producer): TMA loads of the Q tile once, then 128-key K and V
 //     tiles (one pool block each, 128-byte swizzle = the canonical UMMA
 //     operand layout): K into a 3-stage ring freed as soon as S has read it,
-//     V into a 2-stage ring freed by PV; K runs two tiles ahead of V, and
+//     V into a 3-stage ring freed by PV; K runs two tiles ahead of V, and
 //     the block ids come 32 at a time (one parallel load per warp).
-//   warp 5 (MMA): allocates 512 TMEM columns (S double buffered: 0-127 and
-//     128-255, O: 256-383) and one lane issues S = Q K^T (8 x M128 N128 K16,
-//     both K-major) one key tile ahead of O += P V (8 x M128 N128 K16, P
-//     K-major from smem, V MN-major), so the tensor core computes S(j+1)
-//     while the softmax warps work on tile j; tcgen05.commit signals the
-//     mbarriers.
+//   warp 5 (MMA): allocates 512 TMEM columns (S/P triple buffered: 0-127,
+//     128-255, 256-383; O: 384-511) and one lane issues S = Q K^T (8 x M128 N128 K16,
+//     both K-major) one key tile ahead of O += P V (8 x M128 N128 K16, P read
+//     from TMEM where the softmax wrote it over S(j), V MN-major from smem),
+//     so the tensor core computes S(j+1) while the softmax warps work on
+//     tile j; tcgen05.commit signals the mbarriers.
 //   warps 0-3 (softmax): thread r owns query row r = TMEM lane r: loads its
 //     S row (tcgen05.ld), masks, base-2 online softmax with lazy rescaling
 //     of O in TMEM (only when the running max grows by more than 2^8), writes
-//     P as bf16 into smem in the K-major SW128 layout, and at the end
-//     normalises its O row and stores it.
+//     P as bf16 pairs into the first 64 columns of its S buffer (tcgen05.st),
+//     and at the end normalises its O row and stores it.
 // Every mbarrier wait is bounded; on a timeout the CTA records the error,
 // drains its in-flight copies and MMAs, frees TMEM and exits.
 #include "host_common.h"
@@ -39,12 +39,13 @@ constexpr int kRows = 128;              // query rows per CTA, keys per KV tile
 constexpr int kHalfBytes = kRows * 128; // one 64-dim half of a 128-row tile
 constexpr int kTileBytes = 2 * kHalfBytes;
 constexpr int kKStages = 3;
-constexpr int kVStages = 2;
+constexpr int kVStages = 3;
 constexpr int kSoftmaxThreads = 128;
 constexpr int kProducerWarp = 4;
 constexpr int kMmaWarp = 5;
 constexpr int kThreads = 6 * 32;
-constexpr uint32_t kTmemCols = 512;  // S0, S1, O (128 each) rounded up to a power of two
+constexpr int kSBufs = 3;            // S/P buffers in TMEM
+constexpr uint32_t kTmemCols = 512;  // S0, S1, S2, O: 128 columns each
 constexpr float kRescaleThreshold = 8.0f;
 
 struct PrefillArgs {
@@ -66,14 +67,12 @@ struct PrefillSmem {
   alignas(1024) uint8_t q[kTileBytes];
   alignas(1024) uint8_t k[kKStages][kTileBytes];
   alignas(1024) uint8_t v[kVStages][kTileBytes];
-  alignas(1024) uint8_t p[kTileBytes];
   uint64_t bar_q;
   uint64_t full_k[kKStages], k_empty[kKStages];
   uint64_t full_v[kVStages], v_empty[kVStages];
-  uint64_t s_full[2];
-  uint64_t s_free[2];
-  uint64_t p_full;
-  uint64_t o_done;
+  uint64_t s_full[kSBufs];
+  uint64_t p_full[kSBufs];   // P(j) written into S buffer j % 3
+  uint64_t pv_done[kSBufs];  // PV(j) complete (S buffer j % 3 free again)
   uint64_t fin;
   uint32_t tmem_base;
   volatile int abort;
@@ -130,12 +129,11 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
       mbar_init(&sm.full_v[s], 1);
       mbar_init(&sm.v_empty[s], 1);
     }
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < kSBufs; ++i) {
       mbar_init(&sm.s_full[i], 1);
-      mbar_init(&sm.s_free[i], kSoftmaxThreads);
+      mbar_init(&sm.p_full[i], kSoftmaxThreads);
+      mbar_init(&sm.pv_done[i], 1);
     }
-    mbar_init(&sm.p_full, kSoftmaxThreads);
-    mbar_init(&sm.o_done, 1);
     mbar_init(&sm.fin, 1);
     sm.abort = 0;
     fence_mbar_init();
@@ -148,8 +146,8 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = sm.tmem_base;
-  const uint32_t tmem_s = tmem;            // S(j) in columns (j & 1) * 128
-  const uint32_t tmem_o = tmem + 2 * kRows;
+  const uint32_t tmem_s = tmem;            // S(j), then P(j), in columns (j % 3) * 128
+  const uint32_t tmem_o = tmem + kSBufs * kRows;
 
   if (warp == kProducerWarp) {
     // -------------------------------------------------------- producer ----
@@ -234,15 +232,15 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
     if (lane == 0) {
       constexpr uint32_t idesc_qk = umma_idesc_bf16(kRows, kRows, false);
       constexpr uint32_t idesc_pv = umma_idesc_bf16(kRows, kD, true);
-      const uint32_t q_addr = smem_u32(sm.q), p_addr = smem_u32(sm.p);
+      const uint32_t q_addr = smem_u32(sm.q);
       bool ok = mbar_wait(&sm.bar_q, 0);
       if (!ok) flag_error(a, sm, kErrWaitTimeout);
-      // S(j) = Q K(j)^T into S buffer j & 1, once K(j) has landed and the
-      // softmax has read S(j-2) out of that buffer.
+      // S(j) = Q K(j)^T into S buffer j % 3, once K(j) has landed and PV(j-3)
+      // has read P(j-3) out of that buffer.
       auto issue_s = [&](int j) -> bool {
-        const int s = j & 1, ks = j % kKStages;
+        const int s = j % kSBufs, ks = j % kKStages;
         if (!mbar_wait(&sm.full_k[ks], (j / kKStages) & 1)) return false;
-        if (j >= 2 && !mbar_wait(&sm.s_free[s], ((j >> 1) - 1) & 1)) return false;
+        if (j >= kSBufs && !mbar_wait(&sm.pv_done[s], ((j / kSBufs) - 1) & 1)) return false;
         tc_fence_after();
         const uint32_t k_addr = smem_u32(sm.k[ks]);
 #pragma unroll
@@ -257,20 +255,20 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
       };
       if (ok) ok = issue_s(0);
       for (int j = 0; ok && j < n_kv; ++j) {
-        const int s = j & 1;
+        const int s = j % kSBufs;
         if (j + 1 < n_kv && !issue_s(j + 1)) { ok = false; break; }
-        if (!mbar_wait(&sm.p_full, j & 1)) { ok = false; break; }
+        if (!mbar_wait(&sm.p_full[s], (j / kSBufs) & 1)) { ok = false; break; }
+        const int vs = j % kVStages;
+        if (!mbar_wait(&sm.full_v[vs], (j / kVStages) & 1)) { ok = false; break; }
         tc_fence_after();
-        if (!mbar_wait(&sm.full_v[s], (j >> 1) & 1)) { ok = false; break; }
-        const uint32_t v_addr = smem_u32(sm.v[s]);
+        const uint32_t v_addr = smem_u32(sm.v[vs]);
 #pragma unroll
         for (int kk = 0; kk < kRows / 16; ++kk) {
-          const uint64_t pa = smem_desc_sw128(p_addr + (kk >> 2) * kHalfBytes + (kk & 3) * 32, 16, 1024);
           const uint64_t vb = smem_desc_sw128(v_addr + kk * 16 * 128, kHalfBytes, 1024);
-          umma_f16_ss(tmem_o, pa, vb, idesc_pv, (j > 0 || kk > 0) ? 1u : 0u);
+          umma_f16_ts(tmem_o, tmem_s + s * kRows + kk * 8, vb, idesc_pv, (j > 0 || kk > 0) ? 1u : 0u);
         }
-        umma_commit(&sm.v_empty[s]);
-        umma_commit(&sm.o_done);
+        umma_commit(&sm.v_empty[vs]);
+        umma_commit(&sm.pv_done[s]);
       }
       if (!ok) flag_error(a, sm, kErrWaitTimeout);
       // All MMAs of this CTA complete before TMEM is released.
@@ -282,21 +280,17 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
     const int r = tid;
     const int lim = (i < lq) ? (lk - lq + i) : (lk - 1);
     const uint32_t t_lane = static_cast<uint32_t>(warp * 32) << 16;
-    const uint32_t p_row = smem_u32(sm.p) + r * 128;
-    const int sw = r & 7;
     float m = -INFINITY, l = 0.f;
     bool ok = true;
     for (int j = 0; j < n_kv; ++j) {
       // warp-uniform outcome: the tcgen05.ld/st below need a converged warp
-      const int sb = j & 1;
-      if (!__all_sync(0xffffffffu, mbar_wait(&sm.s_full[sb], (j >> 1) & 1))) { ok = false; break; }
+      const int sb = j % kSBufs;
+      if (!__all_sync(0xffffffffu, mbar_wait(&sm.s_full[sb], (j / kSBufs) & 1))) { ok = false; break; }
       tc_fence_after();
       uint32_t sr[4][32];
 #pragma unroll
       for (int c = 0; c < 4; ++c) tmem_ld32(tmem_s + sb * kRows + t_lane + c * 32, sr[c]);
       tmem_ld_wait();
-      tc_fence_before();
-      mbar_arrive(&sm.s_free[sb]);  // S buffer sb may take S(j+2)
       const int kbase = j * kRows;
       const bool need_mask = kbase + kRows - 1 > lim;
       // The max is taken over raw scores (scale > 0), the scale folded into
@@ -314,21 +308,21 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
       const float m_new = fmaxf(m, mt);
       const bool resc = m_new > m + kRescaleThreshold;
       const float alpha = resc ? fast_exp2(m - m_new) : 1.f;
-      if (j > 0) {
-        if (!__all_sync(0xffffffffu, mbar_wait(&sm.o_done, (j - 1) & 1))) { ok = false; break; }
+      // O rows change only when one of this warp's rows rescales; then
+      // PV(j-1) must be complete first.
+      if (j > 0 && __any_sync(0xffffffffu, resc)) {
+        if (!__all_sync(0xffffffffu, mbar_wait(&sm.pv_done[(j - 1) % kSBufs], ((j - 1) / kSBufs) & 1))) { ok = false; break; }
         tc_fence_after();
-        if (__any_sync(0xffffffffu, resc)) {
 #pragma unroll 1
-          for (int c = 0; c < 4; ++c) {
-            uint32_t o[32];
-            tmem_ld32(tmem_o + t_lane + c * 32, o);
-            tmem_ld_wait();
+        for (int c = 0; c < 4; ++c) {
+          uint32_t o[32];
+          tmem_ld32(tmem_o + t_lane + c * 32, o);
+          tmem_ld_wait();
 #pragma unroll
-            for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
-            tmem_st32(tmem_o + t_lane + c * 32, o);
-          }
-          tmem_st_wait();
+          for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
+          tmem_st32(tmem_o + t_lane + c * 32, o);
         }
+        tmem_st_wait();
       }
       if (resc) {
         l *= alpha;
@@ -337,26 +331,26 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
       const float neg_mu = (m == -INFINITY) ? 0.f : -m;
       const float sc = a.scale_log2;
       float sum = 0.f;
+      // P over the first 64 columns of the S buffer (S is in registers now):
+      // column k holds keys 2k and 2k+1 of this row as a bf16 pair.
 #pragma unroll
-      for (int c8 = 0; c8 < 16; ++c8) {  // 16 chunks of 8 keys
-        const int c = c8 >> 2, e0 = (c8 & 3) * 8;
-        uint32_t w[4];
+      for (int c = 0; c < 4; ++c) {  // 32 keys -> 16 columns at a time
+        uint32_t w[16];
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const float p0 = fast_exp2(fmaf(__uint_as_float(sr[c][e0 + 2 * e]), sc, neg_mu));
-          const float p1 = fast_exp2(fmaf(__uint_as_float(sr[c][e0 + 2 * e + 1]), sc, neg_mu));
+        for (int e = 0; e < 16; ++e) {
+          const float p0 = fast_exp2(fmaf(__uint_as_float(sr[c][2 * e]), sc, neg_mu));
+          const float p1 = fast_exp2(fmaf(__uint_as_float(sr[c][2 * e + 1]), sc, neg_mu));
           sum += p0 + p1;
           w[e] = pack_bf16x2(p0, p1);
         }
-        const int half = c8 >> 3, chunk = c8 & 7;
-        st_shared_v4(p_row + half * kHalfBytes + ((chunk ^ sw) << 4), w[0], w[1], w[2], w[3]);
+        tmem_st16(tmem_s + sb * kRows + c * 16 + t_lane, w);
       }
       l += sum;
-      fence_proxy_async_smem();
+      tmem_st_wait();
       tc_fence_before();
-      mbar_arrive(&sm.p_full);
+      mbar_arrive(&sm.p_full[sb]);
     }
-    if (ok && !__all_sync(0xffffffffu, mbar_wait(&sm.o_done, (n_kv - 1) & 1))) ok = false;
+    if (ok && !__all_sync(0xffffffffu, mbar_wait(&sm.pv_done[(n_kv - 1) % kSBufs], ((n_kv - 1) / kSBufs) & 1))) ok = false;
     if (!ok) {
       flag_error(a, sm, kErrWaitTimeout);
     } else {
