@@ -338,18 +338,29 @@ def time_append(kv, bm, device, rows: int, launches: int) -> float:
     g = torch.Generator(device=device).manual_seed(3)
     k = torch.randn(rows, kv.num_kv_heads, HEAD_DIM, generator=g, device=device).to(torch.bfloat16)
     v = torch.randn(rows, kv.num_kv_heads, HEAD_DIM, generator=g, device=device).to(torch.bfloat16)
-    stream = torch.cuda.current_stream(device)
-    for i in range(3):
-        ops.kv_append(kv.key_cache[i % kv.num_layers], kv.value_cache[i % kv.num_layers], k, v, slots)
-    torch.cuda.synchronize()
-    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    start.record(stream)
-    for i in range(launches):
-        layer = i % kv.num_layers
-        ops.kv_append(kv.key_cache[layer], kv.value_cache[layer], k, v, slots)
-    end.record(stream)
-    end.synchronize()
-    return start.elapsed_time(end) / 1e3 / launches
+    # One CUDA graph of `launches` appends (cycling layers): a Python call per
+    # append costs more host time than the kernel takes on the device.
+    stream = torch.cuda.Stream(device)
+    with torch.cuda.stream(stream):
+        for i in range(3):
+            ops.kv_append(kv.key_cache[i % kv.num_layers], kv.value_cache[i % kv.num_layers], k, v, slots)
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            for i in range(launches):
+                layer = i % kv.num_layers
+                ops.kv_append(kv.key_cache[layer], kv.value_cache[layer], k, v, slots)
+        for _ in range(2):
+            graph.replay()
+        torch.cuda.synchronize()
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record(stream)
+        for _ in range(3):
+            graph.replay()
+        end.record(stream)
+        end.synchronize()
+    del graph
+    return start.elapsed_time(end) / 1e3 / (3 * launches)
 
 
 class CpuBaseline:

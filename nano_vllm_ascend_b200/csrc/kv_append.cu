@@ -18,6 +18,7 @@ namespace nvk {
 namespace {
 
 constexpr int kAppendThreads = 256;
+constexpr int64_t kBulkMinTokens = 1024;  // below this the register path's one round trip is shorter
 constexpr int kAppendUnroll = 4;
 
 __device__ __forceinline__ uint4 ldg_stream(const uint4* p) {
@@ -69,6 +70,107 @@ __global__ void __launch_bounds__(kAppendThreads) kv_append_kernel(
   }
 }
 
+// ---------------------------------------------------------------------------
+// Large appends (prefill-sized): whole rows move by TMA bulk copies, global ->
+// shared -> global, so reads and writes stream concurrently without a
+// register round trip. Each of kBulkWarps warps per CTA owns an interleaved
+// set of rows and a ring of kBulkStages (K row, V row) stages; its lane 0
+// keeps up to kBulkStages - kBulkLag rows loading while the stores of the
+// last kBulkLag rows drain, reusing a stage once its store has read it
+// (cp.async.bulk.wait_group.read). Slots come 32 at a time, one per lane.
+constexpr int kBulkWarps = 4;
+constexpr int kBulkStages = 12;
+constexpr int kBulkLag = 4;  // stores in flight per warp before a stage is reused
+constexpr int kBulkMaxRowBytes = 2048;
+
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+__device__ __forceinline__ void bulk_store(void* dst, const void* src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(dst), "r"(smem_u32(src)), "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void bulk_wait_read() {
+  asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
+struct BulkSmem {
+  alignas(128) uint8_t k[kBulkWarps][kBulkStages][kBulkMaxRowBytes];
+  alignas(128) uint8_t v[kBulkWarps][kBulkStages][kBulkMaxRowBytes];
+  uint64_t full[kBulkWarps][kBulkStages];
+};
+
+__global__ void __launch_bounds__(kBulkWarps * 32, 1) kv_append_bulk_kernel(
+    const uint8_t* __restrict__ key, const uint8_t* __restrict__ value, int64_t key_stride_b, int64_t value_stride_b,
+    uint8_t* __restrict__ key_cache, uint8_t* __restrict__ value_cache, const int64_t* __restrict__ slots,
+    int64_t num_tokens, int64_t num_slots, int row_bytes, int* __restrict__ error_word) {
+  extern __shared__ uint8_t smem_raw[];
+  BulkSmem& sm = *reinterpret_cast<BulkSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) {
+    for (int s = 0; s < kBulkStages; ++s) mbar_init(&sm.full[warp][s], 1);
+    fence_mbar_init();
+  }
+  __syncwarp();
+  pdl_launch_dependents();
+  pdl_wait();
+  const int64_t nw = static_cast<int64_t>(gridDim.x) * kBulkWarps;
+  const int64_t w0 = static_cast<int64_t>(blockIdx.x) * kBulkWarps + warp;
+  const int64_t n = w0 < num_tokens ? (num_tokens - w0 + nw - 1) / nw : 0;  // rows of this warp: w0 + i * nw
+  const uint32_t rb = static_cast<uint32_t>(row_bytes);
+  int64_t loaded = 0;  // rows whose load lane 0 has issued (in order)
+  auto issue_load = [&](int64_t i) {
+    ++loaded;
+    const int s = static_cast<int>(i % kBulkStages);
+    const int64_t t = w0 + i * nw;
+    mbar_arrive_expect_tx(&sm.full[warp][s], 2 * rb);
+    bulk_load(sm.k[warp][s], key + t * key_stride_b, rb, &sm.full[warp][s]);
+    bulk_load(sm.v[warp][s], value + t * value_stride_b, rb, &sm.full[warp][s]);
+  };
+  bool ok = true;
+  int64_t slot_chunk = 0;
+  if (lane == 0)
+    for (int64_t i = 0; i < n && i < kBulkStages; ++i) issue_load(i);
+  for (int64_t i = 0; i < n; ++i) {
+    if ((i & 31) == 0) {  // this lane's slot of the next 32 rows
+      const int64_t ii = i + lane;
+      slot_chunk = ii < n ? slots[w0 + ii * nw] : -1;
+    }
+    const int64_t slot = __shfl_sync(0xffffffffu, slot_chunk, static_cast<int>(i & 31));
+    if (lane == 0) {
+      const int s = static_cast<int>(i % kBulkStages);
+      if (ok && !mbar_wait(&sm.full[warp][s], static_cast<uint32_t>((i / kBulkStages) & 1))) ok = false;
+      if (ok && slot >= 0 && slot < num_slots) {
+        bulk_store(key_cache + slot * rb, sm.k[warp][s], rb);
+        bulk_store(value_cache + slot * rb, sm.v[warp][s], rb);
+      } else if (ok && error_word != nullptr) {
+        atomicOr(error_word, kErrBadSlot);
+      }
+      bulk_commit();  // one group per row, empty for a skipped row
+      // The stage of row i - kBulkLag + 1 is free once at most kBulkLag - 1
+      // newer store groups still read shared memory; refill it.
+      const int64_t nxt = i - kBulkLag + 1 + kBulkStages;
+      if (ok && i >= kBulkLag - 1 && nxt < n) {
+        bulk_wait_read<kBulkLag - 1>();
+        issue_load(nxt);
+      }
+    }
+  }
+  if (lane == 0) {
+    if (!ok && error_word != nullptr) atomicOr(error_word, kErrWaitTimeout);
+    // Drain: every load issued lands and every store completes before exit.
+    for (int64_t i = loaded > kBulkStages ? loaded - kBulkStages : 0; i < loaded; ++i)
+      (void)mbar_wait(&sm.full[warp][i % kBulkStages], static_cast<uint32_t>((i / kBulkStages) & 1));
+    bulk_wait_all();
+  }
+}
+
 }  // namespace
 }  // namespace nvk
 
@@ -97,6 +199,20 @@ extern "C" int nvk_kv_append(const void* key, const void* value, int64_t key_tok
   int sms = 148;
   int dev = 0;
   if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  if (num_tokens >= kBulkMinTokens && row_bytes <= kBulkMaxRowBytes) {
+    const size_t smem = sizeof(BulkSmem) + 128;
+    int rc = ensure_dynamic_smem(reinterpret_cast<const void*>(&kv_append_bulk_kernel), smem);
+    if (rc != NVK_OK) return rc;
+    const int64_t warps_needed = (num_tokens + 7) / 8;  // at least ~8 rows per warp
+    const int64_t want = (warps_needed + kBulkWarps - 1) / kBulkWarps;
+    const int grid = static_cast<int>(want < sms ? want : sms);
+    const cudaError_t e = launch_pdl(kv_append_bulk_kernel, dim3(grid), dim3(kBulkWarps * 32), smem,
+                                     reinterpret_cast<cudaStream_t>(stream), static_cast<const uint8_t*>(key),
+                                     static_cast<const uint8_t*>(value), key_token_stride * 2, value_token_stride * 2,
+                                     static_cast<uint8_t*>(key_cache), static_cast<uint8_t*>(value_cache),
+                                     slot_mapping, num_tokens, num_slots, static_cast<int>(row_bytes), error_word);
+    return check_cuda(e, "kv_append (bulk) launch");
+  }
   const int64_t want = (total + int64_t(kAppendThreads) * kAppendUnroll - 1) / (int64_t(kAppendThreads) * kAppendUnroll);
   const int blocks = static_cast<int>(want < int64_t(sms) * 8 ? (want > 0 ? want : 1) : int64_t(sms) * 8);
   const cudaError_t e = launch_pdl(kv_append_kernel, dim3(blocks), dim3(kAppendThreads), 0,

@@ -79,6 +79,31 @@ def test_append_out_of_range_slot_is_skipped_and_flagged(cuda_device):
     assert bool((flat[5] == 1).all()) and int((flat != 0).sum()) == 8 * 128
 
 
+@pytest.mark.parametrize("tokens,kvh", [(1024, 8), (5000, 8), (3000, 4), (2048, 1)])
+def test_append_bulk_path_vs_oracle_with_bad_slots(cuda_device, tokens, kvh):
+    # >= 1024 rows take the TMA bulk-copy kernel; a few slots are out of range
+    nb, bs, d = (tokens + 127) // 128 + 8, 128, 128
+    gen = torch.Generator(device=cuda_device).manual_seed(tokens + kvh)
+    k = torch.randn(tokens, kvh, d, generator=gen, device=cuda_device).to(torch.bfloat16)
+    v = torch.randn(tokens, kvh, d, generator=gen, device=cuda_device).to(torch.bfloat16)
+    slots = torch.randperm(nb * bs, device=cuda_device)[:tokens]
+    bad = torch.tensor([3, tokens // 2, tokens - 1], device=cuda_device)
+    slots[bad] = torch.tensor([-5, nb * bs, nb * bs + 99], device=cuda_device)
+    kc = torch.zeros(nb, bs, kvh, d, dtype=torch.bfloat16, device=cuda_device)
+    vc = torch.zeros_like(kc)
+    err = torch.zeros(1, dtype=torch.int32, device=cuda_device)
+    ops.kv_append(kc, vc, k, v, slots, error_word=err)
+    torch.cuda.synchronize()
+    assert int(err.item()) == 4
+    keep = torch.ones(tokens, dtype=torch.bool, device=cuda_device)
+    keep[bad] = False
+    kc_ref = np.zeros((nb, bs, kvh, d), dtype=np.uint16)
+    vc_ref = np.zeros_like(kc_ref)
+    orc.kv_append(kc_ref, vc_ref, bits(k[keep]), bits(v[keep]), slots[keep].cpu().numpy())
+    assert np.array_equal(bits(kc), kc_ref)
+    assert np.array_equal(bits(vc), vc_ref)
+
+
 # ----------------------------------------------------------------- decode ---
 def run_decode(cuda_device, ctx, h=16, kvh=8, bs=128, nb=None, seed=0, num_ctas=0, width=None, q_scale=1.0):
     need = sum((n + bs - 1) // bs for n in ctx)
