@@ -13,8 +13,11 @@
 //    contiguous range [c*T/C, (c+1)*T/C) of the T tiles, so loads stream
 //    without per-CTA fill/drain and the load balance is within one tile.
 //    A range holds whole pairs ("segments") plus at most a partial pair at
-//    each end; a pair split across CTAs is merged by the CTA that finishes
-//    its piece last (atomic ticket), from two partial slots per CTA.
+//    each end; a pair split across CTAs is merged by the CTA that completes
+//    it: a CTA that finds every other piece already published (acquire load
+//    of the pair's ticket) fetches them while its own piece is computed and
+//    merges in registers; otherwise it publishes its piece (two partial
+//    slots per CTA, acq_rel ticket) and the last publisher merges.
 //  * warp 4 (producer): per segment a TMA load of the group's QPK query rows
 //    into a zero-padded 16-row operand; per tile, TMA loads of the K and V
 //    tile (box {64 dims, 1 head, <=32 tokens}, 128-byte swizzle, only the
@@ -160,10 +163,8 @@ struct Smem {
     float l_part[4][8];
   } seg_info[kOBufs];
   uint64_t seg_ready[kOBufs];
-  int last[2];
-  int pend_pair[2], pend_t0[2], pend_n[2], pend_b[2], pend_g[2];  // partial pieces, published at the end
-  int pieces[kMaxMergePieces];
-  int npieces;
+  int pre_last[2];  // per partial segment: every other piece of its pair was already published
+  int last[2];      // per partial segment: this CTA's publish was the pair's last
   float2 mml[kMaxMergePieces * 8];          // (m, l) of the pieces being merged
   int epi_ok[4];
   volatile int abort;
@@ -402,93 +403,53 @@ __device__ __forceinline__ void tmem_st_cols(uint32_t taddr, int qpk, const floa
   tmem_st_wait();
 }
 
-constexpr int kFastPieces = 4;  // pieces per pair merged with one round of loads
+constexpr int kFastPieces = 4;  // other pieces of a pair fetched in one round of loads
 
-// Publishes this CTA's partial pieces (one acq_rel ticket each, both in
-// flight together) and merges every pair whose last piece this CTA holds.
-// A merge with up to kFastPieces pieces issues every (m, l) and value load
-// of both pairs at once: two global round trips in all. Called by the 128
-// epilogue threads right after the partial segments.
+__device__ __forceinline__ int ld_acquire_gpu(const int* p) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Merges pair (b, g), split over the CTAs c_first .. c_first + pieces - 1,
+// from the published partials of every piece (this CTA's included) and
+// resets its ticket. Called by the 128 epilogue threads of the CTA whose
+// publish was the pair's last (thread e owns dim d).
 template <int QPK>
-__device__ __forceinline__ void publish_and_merge(Smem& sm, const DecodeArgs& a, int c, const Sched& sc, int e,
-                                                  int d, bool all_ok) {
-  if (!all_ok) {
-    if (e == 0) flag_error(a, sm, kErrWaitTimeout);
-    return;
-  }
-  if (e < 2) {
-    int last = 0;
-    if (sm.pend_n[e] > 0) {
-      const int c_first = cta_of(sm.pend_t0[e], sc);
-      const int c_last = cta_of(sm.pend_t0[e] + sm.pend_n[e] - 1, sc);
-      const int pieces = c_last - c_first + 1;  // ranges holding tiles are contiguous
-      int old;
-      // release this CTA's stores, acquire the other pieces'
-      asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], 1;" : "=r"(old) : "l"(a.ws_cnt + static_cast<int64_t>(sm.pend_pair[e]) * kTicketStride) : "memory");
-      last = (old == pieces - 1);
-    }
-    sm.last[e] = last;
-  }
-  named_barrier_sync(2, kEpilogueThreads);
-
-  // Fast path: pieces are the contiguous CTAs c_first .. c_last of the pair.
-  int cf[2], np[2];
-  bool slow[2];
-#pragma unroll
-  for (int k = 0; k < 2; ++k) {
-    cf[k] = 0;
-    np[k] = 0;
-    if (sm.last[k]) {
-      const int pair_t0 = sm.pend_t0[k];
-      cf[k] = cta_of(pair_t0, sc);
-      np[k] = cta_of(pair_t0 + sm.pend_n[k] - 1, sc) - cf[k] + 1;
-    }
-    slow[k] = np[k] > kFastPieces;
-  }
-  float2 mlv[2][kFastPieces][QPK];
-  float ov[2][kFastPieces][QPK];
-#pragma unroll
-  for (int k = 0; k < 2; ++k) {
+__device__ __forceinline__ void merge_published(Smem& sm, const DecodeArgs& a, const Sched& sc, int e, int d, int b,
+                                                int g, int pair_t0, int c_first, int pieces, int* ticket) {
+  if (pieces <= kFastPieces) {
+    float2 ml[kFastPieces][QPK];
+    float ov[kFastPieces][QPK];
 #pragma unroll
     for (int u = 0; u < kFastPieces; ++u) {
 #pragma unroll
       for (int h = 0; h < QPK; ++h) {
-        const bool use = !slow[k] && u < np[k];
-        const int64_t pp = use ? part_index(cf[k] + u, sm.pend_t0[k], sc, QPK) + h : 0;
-        mlv[k][u][h] = use ? __ldcg(&a.ws_ml[pp]) : make_float2(-INFINITY, 0.f);
-        ov[k][u][h] = use ? __ldcg(&a.ws_o[pp * kD + d]) : 0.f;
+        const bool use = u < pieces;
+        const int64_t pp = use ? part_index(c_first + u, pair_t0, sc, QPK) + h : 0;
+        ml[u][h] = use ? __ldcg(&a.ws_ml[pp]) : make_float2(-INFINITY, 0.f);
+        ov[u][h] = use ? __ldcg(&a.ws_o[pp * kD + d]) : 0.f;
       }
     }
-  }
-#pragma unroll
-  for (int k = 0; k < 2; ++k) {
-    if (!sm.last[k] || slow[k]) continue;
 #pragma unroll
     for (int h = 0; h < QPK; ++h) {
       float M = -INFINITY;
 #pragma unroll
-      for (int u = 0; u < kFastPieces; ++u) M = fmaxf(M, mlv[k][u][h].x);
+      for (int u = 0; u < kFastPieces; ++u) M = fmaxf(M, ml[u][h].x);
       float num = 0.f, den = 0.f;
       if (M != -INFINITY) {
 #pragma unroll
         for (int u = 0; u < kFastPieces; ++u) {
-          if (mlv[k][u][h].x == -INFINITY) continue;
-          const float w = fast_exp2(mlv[k][u][h].x - M);
-          num = fmaf(w, ov[k][u][h], num);
-          den = fmaf(w, mlv[k][u][h].y, den);
+          if (ml[u][h].x == -INFINITY) continue;
+          const float w = fast_exp2(ml[u][h].x - M);
+          num = fmaf(w, ov[u][h], num);
+          den = fmaf(w, ml[u][h].y, den);
         }
       }
-      store_out(a, sm.pend_b[k], sm.pend_g[k] * QPK + h, d, den > 0.f ? num / den : 0.f);
+      store_out(a, b, g * QPK + h, d, den > 0.f ? num / den : 0.f);
     }
-    if (e == 0) a.ws_cnt[static_cast<int64_t>(sm.pend_pair[k]) * kTicketStride] = 0;
-  }
-
-  // Slow path (a pair split over more than kFastPieces CTAs): staged passes.
-  for (int k = 0; k < 2; ++k) {
-    if (!sm.last[k] || !slow[k]) continue;
-    const int pair_t0 = sm.pend_t0[k], pn = sm.pend_n[k];
-    const int c_first = cta_of(pair_t0, sc);
-    const int c_last = cta_of(pair_t0 + pn - 1, sc);
+  } else {
+    // Many pieces (a long pair over many CTAs): staged passes through smem.
     float num[QPK], den[QPK], M[QPK];
 #pragma unroll
     for (int h = 0; h < QPK; ++h) {
@@ -496,16 +457,10 @@ __device__ __forceinline__ void publish_and_merge(Smem& sm, const DecodeArgs& a,
       den[h] = 0.f;
       M[h] = -INFINITY;
     }
-    for (int c0 = c_first; c0 <= c_last; c0 += kMaxMergePieces) {
-      if (e == 0) {
-        int n = 0;
-        for (int cc = c0; cc <= min(c_last, c0 + kMaxMergePieces - 1); ++cc) sm.pieces[n++] = cc;
-        sm.npieces = n;
-      }
-      named_barrier_sync(2, kEpilogueThreads);
-      const int n = sm.npieces;
+    for (int c0 = c_first; c0 < c_first + pieces; c0 += kMaxMergePieces) {
+      const int n = min(kMaxMergePieces, c_first + pieces - c0);
       for (int r = e; r < n * QPK; r += kEpilogueThreads)
-        sm.mml[r] = __ldcg(&a.ws_ml[part_index(sm.pieces[r / QPK], pair_t0, sc, QPK) + (r % QPK)]);
+        sm.mml[r] = __ldcg(&a.ws_ml[part_index(c0 + r / QPK, pair_t0, sc, QPK) + (r % QPK)]);
       named_barrier_sync(2, kEpilogueThreads);
 #pragma unroll
       for (int h = 0; h < QPK; ++h) {
@@ -519,16 +474,16 @@ __device__ __forceinline__ void publish_and_merge(Smem& sm, const DecodeArgs& a,
           const float2 ml = sm.mml[p * QPK + h];
           if (ml.x == -INFINITY) continue;
           const float w = fast_exp2(ml.x - mg);
-          num[h] = fmaf(w, __ldcg(&a.ws_o[(part_index(sm.pieces[p], pair_t0, sc, QPK) + h) * kD + d]), num[h]);
+          num[h] = fmaf(w, __ldcg(&a.ws_o[(part_index(c0 + p, pair_t0, sc, QPK) + h) * kD + d]), num[h]);
           den[h] = fmaf(w, ml.y, den[h]);
         }
       }
       named_barrier_sync(2, kEpilogueThreads);  // staging is rewritten by the next group
     }
 #pragma unroll
-    for (int h = 0; h < QPK; ++h) store_out(a, sm.pend_b[k], sm.pend_g[k] * QPK + h, d, den[h] > 0.f ? num[h] / den[h] : 0.f);
-    if (e == 0) a.ws_cnt[static_cast<int64_t>(sm.pend_pair[k]) * kTicketStride] = 0;
+    for (int h = 0; h < QPK; ++h) store_out(a, b, g * QPK + h, d, den[h] > 0.f ? num[h] / den[h] : 0.f);
   }
+  if (e == 0) *ticket = 0;  // every piece has arrived: ready for the next call
 }
 
 template <int QPK>
@@ -569,7 +524,6 @@ __global__ void __launch_bounds__(kThreads, 1) paged_decode_kernel(const __grid_
     }
     mbar_init(&sm.fin, 2);  // one commit from each MMA-issuing thread
     sm.abort = 0;
-    sm.pend_n[0] = sm.pend_n[1] = 0;
     fence_mbar_init();
   }
   // Zero the padded Q and P operands once (rows >= QPK are never written).
@@ -755,6 +709,9 @@ __global__ void __launch_bounds__(kThreads, 1) paged_decode_kernel(const __grid_
     if (lane == 0) {
       tma_prefetch_desc(&kmap);
       tma_prefetch_desc(&vmap);
+      // K/V are read exactly once per launch: keep them from evicting the
+      // workspace partials, block tables and queries other CTAs still need.
+      const uint64_t stream_policy = l2_policy_evict_first();
       int j = 0;
       bool ok = true;
       for (int chunk = 0; ok; ++chunk) {
@@ -795,10 +752,10 @@ __global__ void __launch_bounds__(kThreads, 1) paged_decode_kernel(const __grid_
             const int blk = ck.ids[(tok >> a.log2_bs) - blk0];
             const int row = blk * a.block_size + (tok & (a.block_size - 1));
             const int off = u * a.sub_rows * 128;
-            tma_load_3d(sm.k[st] + off, &kmap, &sm.full_k[st], 0, g, row);
-            tma_load_3d(sm.k[st] + kHalf + off, &kmap, &sm.full_k[st], 64, g, row);
-            tma_load_3d(sm.v[st] + off, &vmap, &sm.full_v[st], 0, g, row);
-            tma_load_3d(sm.v[st] + kHalf + off, &vmap, &sm.full_v[st], 64, g, row);
+            tma_load_3d_hint(sm.k[st] + off, &kmap, &sm.full_k[st], 0, g, row, stream_policy);
+            tma_load_3d_hint(sm.k[st] + kHalf + off, &kmap, &sm.full_k[st], 64, g, row, stream_policy);
+            tma_load_3d_hint(sm.v[st] + off, &vmap, &sm.full_v[st], 0, g, row, stream_policy);
+            tma_load_3d_hint(sm.v[st] + kHalf + off, &vmap, &sm.full_v[st], 64, g, row, stream_policy);
           }
         }
         mbar_arrive(&sm.ring_empty[rs]);  // the chunk's ids are no longer read
@@ -1030,10 +987,43 @@ __global__ void __launch_bounds__(kThreads, 1) paged_decode_kernel(const __grid_
     SegIter it;
     it.init(sm, a, lo, hi);
     Segment s;
-    // Never leaves the walk early: every epilogue warp must reach the publish
-    // barrier after the partial segments, even after a failed wait.
+    // Never leaves the walk early and takes every named barrier of a partial
+    // segment, even after a failed wait: the epilogue warps stay in step.
+    int npart = 0;
     for (; it.next(sm, a, s); ++seg) {
       const int ob = seg % kOBufs;
+      const bool part = s.ntiles != s.n;
+      const int pi = npart & 1;
+      // A piece of a pair shared with other CTAs. If every other piece is
+      // already published, this CTA merges the pair: the others' partials are
+      // fetched now, while its own piece is still being computed, and it
+      // publishes nothing. Otherwise it publishes its piece after computing it.
+      int c_first = 0, pieces = 1;
+      int* ticket = nullptr;
+      bool pre_last = false;
+      float2 pml[kFastPieces][QPK];
+      float po[kFastPieces][QPK];
+      if (part) {
+        c_first = cta_of(s.pair_t0, sc);
+        pieces = cta_of(s.pair_t0 + s.n - 1, sc) - c_first + 1;  // CTAs holding tiles are contiguous
+        ticket = a.ws_cnt + static_cast<int64_t>(s.b * kvh + s.g) * kTicketStride;
+        if (e == 0) sm.pre_last[pi] = (pieces - 1 <= kFastPieces) && ld_acquire_gpu(ticket) == pieces - 1;
+        named_barrier_sync(2, kEpilogueThreads);  // one decision for all epilogue threads
+        pre_last = sm.pre_last[pi] != 0;
+        if (pre_last) {
+#pragma unroll
+          for (int u = 0; u < kFastPieces; ++u) {
+            const int cc = c_first + (u < c - c_first ? u : u + 1);  // every piece but this CTA's
+#pragma unroll
+            for (int h = 0; h < QPK; ++h) {
+              const bool use = u < pieces - 1;
+              const int64_t pp = use ? part_index(cc, s.pair_t0, sc, QPK) + h : 0;
+              pml[u][h] = use ? __ldcg(&a.ws_ml[pp]) : make_float2(-INFINITY, 0.f);
+              po[u][h] = use ? __ldcg(&a.ws_o[pp * kD + d]) : 0.f;
+            }
+          }
+        }
+      }
       if (ok) ok = mbar_wait(&sm.seg_ready[ob], (seg / kOBufs) & 1) && mbar_wait(&sm.o_full[ob], (seg / kOBufs) & 1);
       ok = __all_sync(0xffffffffu, ok);
       if (ok) {
@@ -1047,36 +1037,65 @@ __global__ void __launch_bounds__(kThreads, 1) paged_decode_kernel(const __grid_
           l_sum[h] = info.l_part[0][h] + info.l_part[1][h] + info.l_part[2][h] + info.l_part[3][h];
           m_seg[h] = info.m[h];
         }
-        const int slot = info.slot;
         tc_fence_before();
         mbar_arrive(&sm.o_empty[ob]);
-        if (s.ntiles == s.n) {  // the whole pair lies in this CTA
+        if (!part) {  // the whole pair lies in this CTA
 #pragma unroll
           for (int h = 0; h < QPK; ++h) store_out(a, s.b, s.g * QPK + h, d, l_sum[h] > 0.f ? o[h] / l_sum[h] : 0.f);
-        } else {
-          // A piece of a pair shared with other CTAs: stored now, published
-          // with one ticket right after the partial segments.
-          const int64_t part = part_index(c, s.pair_t0, sc, QPK);
+        } else if (pre_last) {  // merge this piece (registers) with the fetched ones
 #pragma unroll
           for (int h = 0; h < QPK; ++h) {
-            a.ws_o[(part + h) * kD + d] = o[h];
-            if (e == 0) a.ws_ml[part + h] = make_float2(m_seg[h], l_sum[h]);
+            float M = m_seg[h];
+#pragma unroll
+            for (int u = 0; u < kFastPieces; ++u) M = fmaxf(M, pml[u][h].x);
+            float num = 0.f, den = 0.f;
+            if (M != -INFINITY) {
+              if (m_seg[h] != -INFINITY) {
+                const float w = fast_exp2(m_seg[h] - M);
+                num = w * o[h];
+                den = w * l_sum[h];
+              }
+#pragma unroll
+              for (int u = 0; u < kFastPieces; ++u) {
+                if (pml[u][h].x == -INFINITY) continue;
+                const float w = fast_exp2(pml[u][h].x - M);
+                num = fmaf(w, po[u][h], num);
+                den = fmaf(w, pml[u][h].y, den);
+              }
+            }
+            store_out(a, s.b, s.g * QPK + h, d, den > 0.f ? num / den : 0.f);
           }
-          if (e == 0) {
-            sm.pend_pair[slot] = s.b * kvh + s.g;
-            sm.pend_t0[slot] = s.pair_t0;
-            sm.pend_n[slot] = s.n;
-            sm.pend_b[slot] = s.b;
-            sm.pend_g[slot] = s.g;
+          if (e == 0) *ticket = 0;  // every other piece arrived and none will touch it again this call
+        } else {  // this CTA's piece, for whichever CTA merges the pair
+          const int64_t slot_part = part_index(c, s.pair_t0, sc, QPK);
+#pragma unroll
+          for (int h = 0; h < QPK; ++h) {
+            a.ws_o[(slot_part + h) * kD + d] = o[h];
+            if (e == 0) a.ws_ml[slot_part + h] = make_float2(m_seg[h], l_sum[h]);
           }
         }
       }
-      if (seg + 1 == it.npartial) {
+      if (part && !pre_last) {
+        // Publish: one acq_rel ticket releases the piece (every epilogue
+        // thread's stores, ordered by the barrier) and acquires the others'.
         if (lane == 0) sm.epi_ok[ew] = ok;
-        named_barrier_sync(2, kEpilogueThreads);  // every partial store of this CTA is issued
-        const bool all_ok = sm.epi_ok[0] && sm.epi_ok[1] && sm.epi_ok[2] && sm.epi_ok[3];
-        publish_and_merge<QPK>(sm, a, c, sc, e, d, all_ok);
+        named_barrier_sync(2, kEpilogueThreads);
+        if (e == 0) {
+          const bool all_ok = sm.epi_ok[0] && sm.epi_ok[1] && sm.epi_ok[2] && sm.epi_ok[3];
+          int last = 0;
+          if (all_ok) {
+            int old;
+            asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], 1;" : "=r"(old) : "l"(ticket) : "memory");
+            last = (old == pieces - 1);
+          } else {
+            flag_error(a, sm, kErrWaitTimeout);
+          }
+          sm.last[pi] = last;
+        }
+        named_barrier_sync(2, kEpilogueThreads);
+        if (sm.last[pi]) merge_published<QPK>(sm, a, sc, e, d, s.b, s.g, s.pair_t0, c_first, pieces, ticket);
       }
+      if (part) ++npart;
     }
     if (!ok) flag_error(a, sm, kErrWaitTimeout);
 

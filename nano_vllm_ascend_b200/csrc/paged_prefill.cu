@@ -277,7 +277,6 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
     }
   } else {
     // --------------------------------------------------------- softmax ----
-    const int r = tid;
     const int lim = (i < lq) ? (lk - lq + i) : (lk - 1);
     const uint32_t t_lane = static_cast<uint32_t>(warp * 32) << 16;
     float m = -INFINITY, l = 0.f;
