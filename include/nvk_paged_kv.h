@@ -29,6 +29,9 @@
  *   nvk_paged_decode_append
  *                      <- PagedKVCache.write + _npu_paged_attention of one decode layer
  *                         (qwen3.py:91-117), fused
+ *   nvk_decode_metadata
+ *                      <- BlockManager.prepare_decode_metadata's table / length / slot
+ *                         building, src/nanovllm_ascend/npu/block_manager.py:207-250,304-328
  *   nvk_paged_decode_gather, nvk_peer_*
  *                      <- no reference counterpart (the reference runs on one
  *                         device, src/nanovllm_ascend/model_runner.py:31): KV-head
@@ -66,7 +69,8 @@ enum {
 NVK_API const char* nvk_last_error(void);
 
 /* ABI version, bumped on any signature change (2: persistent decode, num_ctas;
-   3: KV-head-sharded decode with in-kernel gather, peer buffers, fused append). */
+   3: KV-head-sharded decode with in-kernel gather, peer buffers, fused append,
+   device-side decode metadata). */
 NVK_API int nvk_abi_version(void);
 
 /*
@@ -194,6 +198,30 @@ NVK_API int nvk_dense_prefill(void* out, const void* query, const void* key, con
                       const int32_t* cu_seqlens_q, const int32_t* cu_seqlens_kv, int batch, int total_q,
                       int total_kv, int max_q_len, int num_heads, int num_kv_heads, int head_dim, float scale,
                       int* error_word, nvk_stream_t stream);
+
+/*
+ * Decode-step metadata on the device (replaces the host loops of
+ * BlockManager.prepare_decode_metadata, src/nanovllm_ascend/npu/block_manager.py:304-328,
+ * with get_block_tables_tensor :207-224, get_context_lens_tensor :226-231 and
+ * get_slot_mapping :233-250). table_mirror: int32 [mirror_rows, mirror_stride]
+ * device copy of the per-sequence block tables (row = sequence slot), kept
+ * by this call: sequence b first gets its new entries
+ * table_mirror[seq_slots[b]][update_idx[u]] = update_block[u] for u in
+ * [update_offsets[b], update_offsets[b+1]), then
+ *   block_tables[b][j] = j < ceil(end_b / block_size) ? table[j] : 0  (j < block_table_width)
+ *   context_lens[b]    = end_b = start_positions[b] + q_len
+ *   slot_mapping[b * q_len + t] = table[p / block_size] * block_size + p % block_size,
+ *                        p = start_positions[b] + t
+ * bit-exact with the host path. All arrays are device memory. A sequence
+ * whose table would not fit (or a bad slot) gets a zero row, length 0, slots
+ * -1, and bit 8 in error_word (may be NULL).
+ */
+NVK_API int nvk_decode_metadata(int32_t* table_mirror, int mirror_stride, int mirror_rows, const int32_t* seq_slots,
+                                const int64_t* start_positions, int batch, int q_len, int block_size,
+                                const int32_t* update_offsets, const int32_t* update_idx,
+                                const int32_t* update_block, int32_t* block_tables, int block_table_stride,
+                                int block_table_width, int32_t* context_lens, int64_t* slot_mapping, int* error_word,
+                                nvk_stream_t stream);
 
 /*
  * ---- KV-head-sharded decode, outputs gathered across GPUs in the kernel ----

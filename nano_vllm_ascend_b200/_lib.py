@@ -55,6 +55,11 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _i32, _i32, _i32, _i32, _i32, _i32, _i32,
          _f32, _c_void_p, _c_void_p],
     ),
+    "nvk_decode_metadata": (
+        _i32,
+        [_c_void_p, _i32, _i32, _c_void_p, _c_void_p, _i32, _i32, _i32, _c_void_p, _c_void_p, _c_void_p, _c_void_p,
+         _i32, _i32, _c_void_p, _c_void_p, _c_void_p, _c_void_p],
+    ),
     "nvk_peer_alloc": (_i32, [_size_t, ctypes.POINTER(_c_void_p)]),
     "nvk_peer_free": (_i32, [_c_void_p]),
     "nvk_peer_export": (_i32, [_c_void_p, _c_void_p]),

@@ -1,0 +1,71 @@
+"""Device-built decode metadata (nvk_decode_metadata via DeviceBlockTables)
+is bit-identical to BlockManager.prepare_decode_metadata over a seeded script
+of prefills with prefix hits, decode steps crossing block boundaries (q_len 1
+and 3), frees and slot reuse, with two managers driven by the same
+operations."""
+
+import random
+
+import numpy as np
+import pytest
+import torch
+
+from nano_vllm_ascend_b200 import BlockManager
+from nano_vllm_ascend_b200.device_metadata import DeviceBlockTables
+
+pytestmark = pytest.mark.gpu
+
+
+def test_device_decode_metadata_bit_exact_over_a_seeded_script(cuda_device):
+    rnd = random.Random(7)
+    bs, nb = 16, 4000
+    host_bm, dev_bm = BlockManager(nb, bs, "cpu"), BlockManager(nb, bs, cuda_device)
+    perm = list(range(nb))
+    rnd.shuffle(perm)
+    host_bm.free_block_ids = perm
+    dev_bm.free_block_ids = perm
+    dt = DeviceBlockTables(dev_bm, max_slots=64, max_blocks_per_seq=256, device=cuda_device)
+    pos: dict[int, int] = {}
+    for step in range(300):
+        op = rnd.random()
+        free_slots = [s for s in range(64) if s not in pos]
+        if (op < 0.15 or not pos) and free_slots:  # prefill a new sequence (sometimes over a prefix)
+            slot = rnd.choice(free_slots)
+            n = rnd.randint(1, 300)
+            prefix = []
+            if pos and rnd.random() < 0.3:
+                donor = rnd.choice(list(pos))
+                prefix = host_bm.block_tables[donor][: rnd.randint(0, len(host_bm.block_tables[donor]))]
+                n = max(n, len(prefix) * bs + 1)
+            start = len(prefix) * bs
+            for bm in (host_bm, dev_bm):
+                bm.prepare_prefill_metadata([slot], [n - start], [start], [list(prefix)])
+            pos[slot] = n
+        elif op < 0.22 and len(pos) > 1:  # finish a sequence
+            slot = rnd.choice(list(pos))
+            for bm in (host_bm, dev_bm):
+                bm.free_slot(slot)
+            del pos[slot]
+        else:  # one decode step of a random subset
+            q_len = 3 if rnd.random() < 0.2 else 1
+            slots = rnd.sample(list(pos), rnd.randint(1, len(pos)))
+            starts = [pos[s] for s in slots]
+            want = host_bm.prepare_decode_metadata(slots, starts, q_len)
+            got = dt.prepare_decode_metadata(slots, starts, q_len)
+            torch.cuda.synchronize()
+            assert np.array_equal(got.block_tables.cpu().numpy(), want.block_tables.cpu().numpy()), step
+            assert np.array_equal(got.context_lens.cpu().numpy(), want.context_lens.numpy()), step
+            assert np.array_equal(got.slot_mapping.cpu().numpy(), want.slot_mapping.cpu().numpy()), step
+            for s in slots:
+                pos[s] += q_len
+    assert int(dt.error_word.item()) == 0
+
+
+def test_device_decode_metadata_padded_width(cuda_device):
+    bm = BlockManager(64, 16, cuda_device)
+    bm.prepare_prefill_metadata([0, 1], [40, 5], [0, 0], [[], []])
+    dt = DeviceBlockTables(bm, 4, 32, cuda_device)
+    md = dt.prepare_decode_metadata([0, 1], [40, 5], 1, width=32)
+    t = md.block_tables.cpu()
+    assert t.shape == (2, 32) and int(t[0, 3:].abs().sum()) == 0 and int(t[1, 1:].abs().sum()) == 0
+    assert t[0, :3].tolist() == bm.block_tables[0] and t[1, :1].tolist() == bm.block_tables[1]

@@ -28,8 +28,12 @@ D = 128
 SCALE = D ** -0.5
 
 
-def last_slots(tables: torch.Tensor, ctx: list[int], bs: int) -> torch.Tensor:
-    return torch.tensor([int(tables[b, (n - 1) // bs]) * bs + (n - 1) % bs if n > 0 else int(tables[b, 0]) * bs
+def last_slots(tables: torch.Tensor, ctx: list[int], bs: int, nb: int) -> torch.Tensor:
+    """Each sequence's last context position; a sequence without context gets a
+    row of its own in a block no sequence uses (distinct slots, as a decode step has)."""
+    used = {int(x) for b, n in enumerate(ctx) for x in tables[b, : (n + bs - 1) // bs]}
+    spare = iter(sorted(set(range(nb)) - used))
+    return torch.tensor([int(tables[b, (n - 1) // bs]) * bs + (n - 1) % bs if n > 0 else next(spare) * bs
                          for b, n in enumerate(ctx)], dtype=torch.int64)
 
 
@@ -37,7 +41,7 @@ def run_fused(dev, ctx, h=16, kvh=8, bs=128, num_ctas=0, seed=0, strided=False, 
     nb = sum((n + bs - 1) // bs for n in ctx) + 4
     kc, vc = random_pool(nb, bs, kvh, D, dev, seed)
     tables = seeded_tables(ctx, bs, nb, seed)
-    slots = last_slots(tables, ctx, bs)
+    slots = last_slots(tables, ctx, bs, nb)
     if bad is not None:
         slots[bad] = (slots[bad] + 1) % (nb * bs)  # not the sequence's last position
     g = torch.Generator(device=dev).manual_seed(seed + 7)
