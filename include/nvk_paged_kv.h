@@ -29,6 +29,9 @@
  *   nvk_paged_decode_append
  *                      <- PagedKVCache.write + _npu_paged_attention of one decode layer
  *                         (qwen3.py:91-117), fused
+ *   nvk_qk_norm_rope_append
+ *                      <- q_norm + k_norm + apply_rotary_pos_emb_tnd + PagedKVCache.write,
+ *                         src/nanovllm_ascend/models/qwen3.py:83-96, fused
  *   nvk_decode_metadata
  *                      <- BlockManager.prepare_decode_metadata's table / length / slot
  *                         building, src/nanovllm_ascend/npu/block_manager.py:207-250,304-328
@@ -198,6 +201,30 @@ NVK_API int nvk_dense_prefill(void* out, const void* query, const void* key, con
                       const int32_t* cu_seqlens_q, const int32_t* cu_seqlens_kv, int batch, int total_q,
                       int total_kv, int max_q_len, int num_heads, int num_kv_heads, int head_dim, float scale,
                       int* error_word, nvk_stream_t stream);
+
+/*
+ * Fused prologue of one attention layer (Qwen3Attention.forward,
+ * src/nanovllm_ascend/models/qwen3.py:83-96): per-head RMSNorm of q and k
+ * (q_norm / k_norm, npu_rms_norm over head_dim, layers/layernorm.py:12-17),
+ * rotary embedding in "half" mode (apply_rotary_pos_emb_tnd,
+ * layers/rotary_embedding.py:58-99; cos/sin rows of the fp32 tables
+ * [max_position, head_dim] cast to bf16), and PagedKVCache.write of the
+ * rotated k and of v at slot_mapping. query/key/value: bf16 rows of
+ * num_heads / num_kv_heads heads, query_stride etc. ELEMENTS between tokens
+ * (slices of a fused QKV output work); query_out: bf16 [num_tokens,
+ * num_heads, head_dim] contiguous (may alias query when its stride is
+ * num_heads * head_dim). Arithmetic in fp32, the norm's output rounded to
+ * bf16 before the rotation (as the separate ops do). A bad slot skips that
+ * token's k/v rows and sets bit 4 of error_word; a position outside the
+ * table is clamped and sets bit 8.
+ */
+NVK_API int nvk_qk_norm_rope_append(const void* query, const void* key, const void* value, int64_t query_stride,
+                                    int64_t key_stride, int64_t value_stride, const void* q_weight,
+                                    const void* k_weight, float eps, const float* cos_table, const float* sin_table,
+                                    int max_position, const int64_t* positions, void* query_out, void* key_cache,
+                                    void* value_cache, const int64_t* slot_mapping, int64_t num_tokens,
+                                    int64_t num_slots, int num_heads, int num_kv_heads, int head_dim,
+                                    int* error_word, nvk_stream_t stream);
 
 /*
  * Decode-step metadata on the device (replaces the host loops of

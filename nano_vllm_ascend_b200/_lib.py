@@ -55,6 +55,11 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _i32, _i32, _i32, _i32, _i32, _i32, _i32,
          _f32, _c_void_p, _c_void_p],
     ),
+    "nvk_qk_norm_rope_append": (
+        _i32,
+        [_c_void_p, _c_void_p, _c_void_p, _i64, _i64, _i64, _c_void_p, _c_void_p, _f32, _c_void_p, _c_void_p, _i32,
+         _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _i64, _i64, _i32, _i32, _i32, _c_void_p, _c_void_p],
+    ),
     "nvk_decode_metadata": (
         _i32,
         [_c_void_p, _i32, _i32, _c_void_p, _c_void_p, _i32, _i32, _i32, _c_void_p, _c_void_p, _c_void_p, _c_void_p,

@@ -78,6 +78,66 @@ def kv_append(
     )
 
 
+# ------------------------------------------------- norm + rope + append ---
+def qk_norm_rope_append(
+    query: torch.Tensor,
+    key: torch.Tensor,
+    value: torch.Tensor,
+    q_weight: torch.Tensor,
+    k_weight: torch.Tensor,
+    eps: float,
+    cos_table: torch.Tensor,
+    sin_table: torch.Tensor,
+    positions: torch.Tensor,
+    key_cache: torch.Tensor,
+    value_cache: torch.Tensor,
+    slot_mapping: torch.Tensor,
+    query_out: torch.Tensor | None = None,
+    error_word: torch.Tensor | None = None,
+) -> torch.Tensor:
+    """q_norm + k_norm + rotary embedding + KV append in one kernel
+    (Qwen3Attention.forward's prologue, qwen3.py:83-96). Returns the rotated
+    query [T, H, D] (``query_out``, new if None); the rotated key and the value
+    rows land in ONE layer of the pool at ``slot_mapping``."""
+    dev = query.device
+    for name, t in (("query", query), ("key", key), ("value", value), ("q_weight", q_weight),
+                    ("k_weight", k_weight), ("cos_table", cos_table), ("sin_table", sin_table),
+                    ("positions", positions), ("key_cache", key_cache), ("value_cache", value_cache),
+                    ("slot_mapping", slot_mapping)):
+        _require_cuda(name, t, dev)
+    for name, t in (("query", query), ("key", key), ("value", value)):
+        _require_rows(name, t)
+        if t.dtype != _BF16:
+            raise ValueError(f"qk_norm_rope_append: {name} must be bfloat16")
+    tokens, num_heads, head_dim = query.shape
+    num_blocks, block_size, kvh, d = key_cache.shape
+    if key.shape != (tokens, kvh, head_dim) or value.shape != key.shape or d != head_dim:
+        raise ValueError(f"kv shape mismatch: got {tuple(key.shape)} / {tuple(value.shape)}")
+    if q_weight.numel() != head_dim or k_weight.numel() != head_dim or q_weight.dtype != _BF16 \
+            or k_weight.dtype != _BF16:
+        raise ValueError("qk_norm_rope_append: q_weight/k_weight must be bfloat16 [head_dim]")
+    if cos_table.dtype != torch.float32 or sin_table.shape != cos_table.shape or cos_table.dim() != 2 \
+            or cos_table.shape[1] != head_dim or not (cos_table.is_contiguous() and sin_table.is_contiguous()):
+        raise ValueError("qk_norm_rope_append: cos/sin tables must be contiguous float32 [max_position, head_dim]")
+    if positions.dtype != torch.int64 or positions.numel() != tokens or slot_mapping.dtype != torch.int64 \
+            or slot_mapping.numel() != tokens:
+        raise ValueError("qk_norm_rope_append: positions and slot_mapping must be int64 [tokens]")
+    if not (key_cache.is_contiguous() and value_cache.is_contiguous()):
+        raise ValueError("qk_norm_rope_append: caches must be contiguous")
+    if query_out is None:
+        query_out = torch.empty(tokens, num_heads, head_dim, dtype=_BF16, device=dev)
+    elif query_out.shape != (tokens, num_heads, head_dim) or not query_out.is_contiguous() or query_out.dtype != _BF16:
+        raise ValueError("qk_norm_rope_append: query_out must be a contiguous bf16 [tokens, heads, head_dim]")
+    _lib.call(
+        "nvk_qk_norm_rope_append", _ptr(query), _ptr(key), _ptr(value), query.stride(0), key.stride(0),
+        value.stride(0), _ptr(q_weight.contiguous()), _ptr(k_weight.contiguous()), float(eps), _ptr(cos_table),
+        _ptr(sin_table), cos_table.shape[0], _ptr(positions.contiguous()), _ptr(query_out), _ptr(key_cache),
+        _ptr(value_cache), _ptr(slot_mapping.contiguous()), tokens, num_blocks * block_size, num_heads, kvh,
+        head_dim, _ptr(error_word), _stream(dev),
+    )
+    return query_out
+
+
 # ----------------------------------------------------------------- decode ---
 def decode_workspace_bytes(batch: int, num_heads: int, num_kv_heads: int, head_dim: int, num_ctas: int = 0) -> int:
     """Workspace bytes of paged_decode (num_ctas 0 = one CTA per SM of the current device)."""

@@ -80,6 +80,42 @@ def kv_append(key_cache: np.ndarray, value_cache: np.ndarray, key: np.ndarray, v
     vflat[slots] = value
 
 
+# ------------------------------------------------- norm + rope + append ----
+def qk_norm_rope_append(q: np.ndarray, k: np.ndarray, v: np.ndarray, q_weight: np.ndarray, k_weight: np.ndarray,
+                        eps: float, cos_table: np.ndarray, sin_table: np.ndarray, positions: np.ndarray,
+                        key_cache: np.ndarray, value_cache: np.ndarray, slots: np.ndarray) -> np.ndarray:
+    """Prologue of Qwen3Attention.forward (src/nanovllm_ascend/models/qwen3.py:83-96).
+
+    q [T, H, D], k/v [T, KVH, D] and the weights [D] are bf16 bits; the
+    fp32 cos/sin tables are RotaryEmbedding's (layers/rotary_embedding.py:20-40).
+    q_norm / k_norm (layers/layernorm.py:12-17): y = x / sqrt(mean(x^2) + eps) * w
+    in fp32, output bf16. apply_rotary_pos_emb_tnd (:58-99): cos/sin rows cast to
+    bf16, "half" rotation out = y * cos + rotate_half(y) * sin, rotate_half(y) =
+    (-y[D/2:], y[:D/2]), output bf16. k_out and v are then written at slots
+    (PagedKVCache.write, paged_kv_cache.py:44-69). Returns q_out bits.
+    """
+    def norm(x_bits, w_bits):
+        x = bf16_bits_to_f32(x_bits)
+        w = bf16_bits_to_f32(w_bits)
+        ms = np.mean(x * x, axis=-1, keepdims=True, dtype=np.float32)
+        y = (x * (np.float32(1.0) / np.sqrt(ms + np.float32(eps)))) * w
+        return bf16_bits_to_f32(f32_to_bf16_bits(y.astype(np.float32)))
+
+    pos = np.asarray(positions, dtype=np.int64)
+    cos = bf16_bits_to_f32(f32_to_bf16_bits(cos_table[pos].astype(np.float32)))[:, None, :]
+    sin = bf16_bits_to_f32(f32_to_bf16_bits(sin_table[pos].astype(np.float32)))[:, None, :]
+
+    def rope(y):
+        half = y.shape[-1] // 2
+        rot = np.concatenate([-y[..., half:], y[..., :half]], axis=-1)
+        return f32_to_bf16_bits((y * cos + rot * sin).astype(np.float32))
+
+    q_out = rope(norm(q, q_weight))
+    k_out = rope(norm(k, k_weight))
+    kv_append(key_cache, value_cache, k_out, v, np.asarray(slots, dtype=np.int64))
+    return q_out
+
+
 # ---------------------------------------------------------------- decode ----
 def as_f32(x: np.ndarray) -> np.ndarray:
     """uint16 arrays are bf16 bit patterns; anything else is cast to f32."""

@@ -142,3 +142,45 @@ def test_oracle_empty_and_fully_masked_rows_are_zero():
     kc = np.ones((1, 16, 1, 128), np.float32)
     out = orc.paged_decode(q, kc, kc, np.array([[0], [0]]), np.array([0, 3]), 0.1)
     assert np.all(out[0] == 0) and np.allclose(out[1], 1.0)
+
+
+def test_norm_rope_oracle_matches_torch_cpu_restatement():
+    """The numpy restatement of qwen3.py:83-96 against an independent torch-CPU
+    expression of the same ops (float32 norm, bf16 output, bf16 cos/sin)."""
+    import torch
+
+    g = torch.Generator().manual_seed(0)
+    t, h, kvh, d = 9, 4, 2, 128
+    q = (torch.randn(t, h, d, generator=g) * 2).to(torch.bfloat16)
+    k = (torch.randn(t, kvh, d, generator=g) * 2).to(torch.bfloat16)
+    v = torch.randn(t, kvh, d, generator=g).to(torch.bfloat16)
+    wq = (1 + 0.1 * torch.randn(d, generator=g)).to(torch.bfloat16)
+    wk = (1 + 0.1 * torch.randn(d, generator=g)).to(torch.bfloat16)
+    inv = 1.0 / (1e6 ** (torch.arange(0, d, 2, dtype=torch.float32) / d))
+    emb = torch.cat([torch.outer(torch.arange(64, dtype=torch.float32), inv)] * 2, dim=-1)
+    cos, sin = emb.cos(), emb.sin()
+    pos = torch.randint(0, 64, (t,), generator=g)
+    slots = torch.randperm(4 * 16, generator=g)[:t]
+
+    def norm(x, w):
+        xf = x.float()
+        y = xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + 1e-6) * w.float()
+        return y.to(torch.bfloat16).float()
+
+    def rope(y):
+        c = cos[pos].to(torch.bfloat16).float()[:, None]
+        s = sin[pos].to(torch.bfloat16).float()[:, None]
+        rot = torch.cat([-y[..., d // 2:], y[..., : d // 2]], dim=-1)
+        return (y * c + rot * s).to(torch.bfloat16)
+
+    q_t, k_t = rope(norm(q, wq)), rope(norm(k, wk))
+    bits = lambda x: x.contiguous().view(torch.int16).numpy().view(np.uint16)
+    kc = np.zeros((4, 16, kvh, d), dtype=np.uint16)
+    vc = np.zeros_like(kc)
+    q_o = orc.qk_norm_rope_append(bits(q), bits(k), bits(v), bits(wq), bits(wk), 1e-6, cos.numpy(), sin.numpy(),
+                                  pos.numpy(), kc, vc, slots.numpy())
+    kflat = kc.reshape(-1, kvh, d)
+    for got, want in ((q_o, bits(q_t)), (kflat[slots.numpy()], bits(k_t))):
+        diff = np.abs(got.astype(np.int32) - want.astype(np.int32))
+        assert (diff == 0).mean() > 0.99 and diff.max() <= 1
+    assert np.array_equal(vc.reshape(-1, kvh, d)[slots.numpy()], bits(v))
