@@ -35,17 +35,21 @@ namespace nvk {
 namespace {
 
 constexpr int kD = 128;
-constexpr int kRows = 128;              // query rows per CTA, keys per KV tile
-constexpr int kHalfBytes = kRows * 128; // one 64-dim half of a 128-row tile
-constexpr int kTileBytes = 2 * kHalfBytes;
-constexpr int kKStages = 3;
-constexpr int kVStages = 3;
+constexpr int kRows = 128;                   // query rows per CTA
+constexpr int kKeys = 64;                    // keys per K/V tile (half a 128-token pool block)
+constexpr int kQHalfBytes = kRows * 128;     // one 64-dim half of the Q tile
+constexpr int kQTileBytes = 2 * kQHalfBytes;
+constexpr int kKVHalfBytes = kKeys * 128;    // one 64-dim half of a K or V tile
+constexpr int kKVTileBytes = 2 * kKVHalfBytes;
+constexpr int kKStages = 2;
+constexpr int kVStages = 2;
 constexpr int kSoftmaxThreads = 128;
 constexpr int kProducerWarp = 4;
 constexpr int kMmaWarp = 5;
 constexpr int kThreads = 6 * 32;
-constexpr int kSBufs = 3;            // S/P buffers in TMEM
-constexpr uint32_t kTmemCols = 512;  // S0, S1, S2, O: 128 columns each
+constexpr int kSBufs = 2;            // S/P buffers in TMEM
+constexpr uint32_t kTmemCols = 256;  // S0, S1 (64 columns each), O (128): two CTAs share an SM's 512
+constexpr int kCtasPerSm = 2;        // two softmax warpgroups per SM hide each other's latency
 constexpr float kRescaleThreshold = 8.0f;
 
 struct PrefillArgs {
@@ -64,9 +68,9 @@ struct PrefillArgs {
 };
 
 struct PrefillSmem {
-  alignas(1024) uint8_t q[kTileBytes];
-  alignas(1024) uint8_t k[kKStages][kTileBytes];
-  alignas(1024) uint8_t v[kVStages][kTileBytes];
+  alignas(1024) uint8_t q[kQTileBytes];
+  alignas(1024) uint8_t k[kKStages][kKVTileBytes];
+  alignas(1024) uint8_t v[kVStages][kKVTileBytes];
   uint64_t bar_q;
   uint64_t full_k[kKStages], k_empty[kKStages];
   uint64_t full_v[kVStages], v_empty[kVStages];
@@ -78,14 +82,15 @@ struct PrefillSmem {
   volatile int abort;
 };
 
-static_assert(sizeof(PrefillSmem) + 1024 <= 232448, "prefill shared memory exceeds the 227 KB per-CTA limit");
+static_assert(kCtasPerSm * (sizeof(PrefillSmem) + 1024 + 1024) <= 233472,
+              "prefill shared memory does not let two CTAs share an SM");
 
 __device__ __forceinline__ void flag_error(const PrefillArgs& a, PrefillSmem& sm, int code) {
   if (a.err) atomicOr(a.err, code);
   sm.abort = 1;
 }
 
-__global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_constant__ CUtensorMap qmap,
+__global__ void __launch_bounds__(kThreads, kCtasPerSm) prefill_kernel(const __grid_constant__ CUtensorMap qmap,
                                                               const __grid_constant__ CUtensorMap kmap,
                                                               const __grid_constant__ CUtensorMap vmap,
                                                               const PrefillArgs a) {
@@ -101,7 +106,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
   const int g = h / a.qpk;
   const int i_last = min(qt * kRows + kRows - 1, lq - 1);
   const int lim_last = min(lk - lq + i_last, lk - 1);
-  const int n_kv = lim_last < 0 ? 0 : lim_last / kRows + 1;
+  const int n_kv = lim_last < 0 ? 0 : lim_last / kKeys + 1;  // 64-key tiles
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   __nv_bfloat16* out_row = nullptr;
@@ -146,8 +151,8 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = sm.tmem_base;
-  const uint32_t tmem_s = tmem;            // S(j), then P(j), in columns (j % 3) * 128
-  const uint32_t tmem_o = tmem + kSBufs * kRows;
+  const uint32_t tmem_s = tmem;            // S(j), then P(j), in columns (j % 2) * 64
+  const uint32_t tmem_o = tmem + kSBufs * kKeys;
 
   if (warp == kProducerWarp) {
     // -------------------------------------------------------- producer ----
@@ -157,20 +162,21 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
       tma_prefetch_desc(&qmap);
       tma_prefetch_desc(&kmap);
       tma_prefetch_desc(&vmap);
-      mbar_arrive_expect_tx(&sm.bar_q, kTileBytes);
+      mbar_arrive_expect_tx(&sm.bar_q, kQTileBytes);
       tma_load_3d(sm.q, &qmap, &sm.bar_q, 0, h, q0 + qt * kRows);
-      tma_load_3d(sm.q + kHalfBytes, &qmap, &sm.bar_q, 64, h, q0 + qt * kRows);
+      tma_load_3d(sm.q + kQHalfBytes, &qmap, &sm.bar_q, 64, h, q0 + qt * kRows);
     }
     const int32_t* bt = a.block_tables + static_cast<int64_t>(b) * a.bt_stride;
-    // First pool row of tile j; `chunk` holds this lane's id of the current
-    // 32-tile chunk and is refreshed when j crosses a multiple of 32 (each
-    // caller passes its own register and consecutive j).
+    // First pool row of 64-key tile j (tile j is half j & 1 of block j / 2);
+    // `chunk` holds this lane's block id for tile j & ~31 + lane and is
+    // refreshed when j crosses a multiple of 32 (each caller passes its own
+    // register and consecutive j).
     auto row_of = [&](int j, int& chunk) -> int {
       if ((j & 31) == 0) {
         const int jj = j + lane;
         int blk = 0;
         if (a.paged && jj < n_kv) {
-          blk = bt[jj];
+          blk = bt[jj >> 1];
           if (blk < 0 || blk >= a.num_blocks) {
             if (a.err) atomicOr(a.err, kErrBadBlockId);
             blk = a.num_blocks;  // fully outside the tensor map: zero fill
@@ -179,7 +185,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
         chunk = blk;
       }
       const int blk = __shfl_sync(0xffffffffu, chunk, j & 31);
-      return a.paged ? blk * kRows : kv_row0 + j * kRows;
+      return a.paged ? blk * kRows + (j & 1) * kKeys : kv_row0 + j * kKeys;
     };
     int k_chunk = 0, v_chunk = 0, k_issued = 0, v_issued = 0;
     bool ok = true;
@@ -190,9 +196,9 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
         if (j >= kKStages && !mbar_wait(&sm.k_empty[st], ((j / kKStages) - 1) & 1)) {
           ok = false;
         } else {
-          mbar_arrive_expect_tx(&sm.full_k[st], kTileBytes);
+          mbar_arrive_expect_tx(&sm.full_k[st], kKVTileBytes);
           tma_load_3d(sm.k[st], &kmap, &sm.full_k[st], 0, g, row);
-          tma_load_3d(sm.k[st] + kHalfBytes, &kmap, &sm.full_k[st], 64, g, row);
+          tma_load_3d(sm.k[st] + kKVHalfBytes, &kmap, &sm.full_k[st], 64, g, row);
         }
       }
       ok = __shfl_sync(0xffffffffu, ok, 0);
@@ -205,9 +211,9 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
         if (j >= kVStages && !mbar_wait(&sm.v_empty[st], ((j / kVStages) - 1) & 1)) {
           ok = false;
         } else {
-          mbar_arrive_expect_tx(&sm.full_v[st], kTileBytes);
+          mbar_arrive_expect_tx(&sm.full_v[st], kKVTileBytes);
           tma_load_3d(sm.v[st], &vmap, &sm.full_v[st], 0, g, row);
-          tma_load_3d(sm.v[st] + kHalfBytes, &vmap, &sm.full_v[st], 64, g, row);
+          tma_load_3d(sm.v[st] + kKVHalfBytes, &vmap, &sm.full_v[st], 64, g, row);
         }
       }
       ok = __shfl_sync(0xffffffffu, ok, 0);
@@ -230,7 +236,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
   } else if (warp == kMmaWarp) {
     // ------------------------------------------------------------- MMA ----
     if (lane == 0) {
-      constexpr uint32_t idesc_qk = umma_idesc_bf16(kRows, kRows, false);
+      constexpr uint32_t idesc_qk = umma_idesc_bf16(kRows, kKeys, false);
       constexpr uint32_t idesc_pv = umma_idesc_bf16(kRows, kD, true);
       const uint32_t q_addr = smem_u32(sm.q);
       bool ok = mbar_wait(&sm.bar_q, 0);
@@ -245,9 +251,10 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
         const uint32_t k_addr = smem_u32(sm.k[ks]);
 #pragma unroll
         for (int kk = 0; kk < kD / 16; ++kk) {
-          const uint32_t off = (kk >> 2) * kHalfBytes + (kk & 3) * 32;
-          umma_f16_ss(tmem_s + s * kRows, smem_desc_sw128(q_addr + off, 16, 1024),
-                      smem_desc_sw128(k_addr + off, 16, 1024), idesc_qk, kk > 0);
+          const uint32_t qoff = (kk >> 2) * kQHalfBytes + (kk & 3) * 32;
+          const uint32_t koff = (kk >> 2) * kKVHalfBytes + (kk & 3) * 32;
+          umma_f16_ss(tmem_s + s * kKeys, smem_desc_sw128(q_addr + qoff, 16, 1024),
+                      smem_desc_sw128(k_addr + koff, 16, 1024), idesc_qk, kk > 0);
         }
         umma_commit(&sm.s_full[s]);
         umma_commit(&sm.k_empty[ks]);  // K(j) slot free once S(j) has read it
@@ -263,9 +270,9 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
         tc_fence_after();
         const uint32_t v_addr = smem_u32(sm.v[vs]);
 #pragma unroll
-        for (int kk = 0; kk < kRows / 16; ++kk) {
-          const uint64_t vb = smem_desc_sw128(v_addr + kk * 16 * 128, kHalfBytes, 1024);
-          umma_f16_ts(tmem_o, tmem_s + s * kRows + kk * 8, vb, idesc_pv, (j > 0 || kk > 0) ? 1u : 0u);
+        for (int kk = 0; kk < kKeys / 16; ++kk) {
+          const uint64_t vb = smem_desc_sw128(v_addr + kk * 16 * 128, kKVHalfBytes, 1024);
+          umma_f16_ts(tmem_o, tmem_s + s * kKeys + kk * 8, vb, idesc_pv, (j > 0 || kk > 0) ? 1u : 0u);
         }
         umma_commit(&sm.v_empty[vs]);
         umma_commit(&sm.pv_done[s]);
@@ -286,17 +293,17 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
       const int sb = j % kSBufs;
       if (!__all_sync(0xffffffffu, mbar_wait(&sm.s_full[sb], (j / kSBufs) & 1))) { ok = false; break; }
       tc_fence_after();
-      uint32_t sr[4][32];
+      uint32_t sr[2][32];
 #pragma unroll
-      for (int c = 0; c < 4; ++c) tmem_ld32(tmem_s + sb * kRows + t_lane + c * 32, sr[c]);
+      for (int c = 0; c < 2; ++c) tmem_ld32(tmem_s + sb * kKeys + t_lane + c * 32, sr[c]);
       tmem_ld_wait();
-      const int kbase = j * kRows;
-      const bool need_mask = kbase + kRows - 1 > lim;
+      const int kbase = j * kKeys;
+      const bool need_mask = kbase + kKeys - 1 > lim;
       // The max is taken over raw scores (scale > 0), the scale folded into
       // the exponent's FMA below.
       float mraw = -INFINITY;
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
+      for (int c = 0; c < 2; ++c) {
 #pragma unroll
         for (int e = 0; e < 32; ++e) {
           if (need_mask && kbase + c * 32 + e > lim) sr[c][e] = __float_as_uint(-INFINITY);
@@ -330,10 +337,10 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
       const float neg_mu = (m == -INFINITY) ? 0.f : -m;
       const float sc = a.scale_log2;
       float sum = 0.f;
-      // P over the first 64 columns of the S buffer (S is in registers now):
+      // P over the first 32 columns of the S buffer (S is in registers now):
       // column k holds keys 2k and 2k+1 of this row as a bf16 pair.
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {  // 32 keys -> 16 columns at a time
+      for (int c = 0; c < 2; ++c) {  // 32 keys -> 16 columns at a time
         uint32_t w[16];
 #pragma unroll
         for (int e = 0; e < 16; ++e) {
@@ -342,7 +349,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
           sum += p0 + p1;
           w[e] = pack_bf16x2(p0, p1);
         }
-        tmem_st16(tmem_s + sb * kRows + c * 16 + t_lane, w);
+        tmem_st16(tmem_s + sb * kKeys + c * 16 + t_lane, w);
       }
       l += sum;
       tmem_st_wait();
@@ -430,8 +437,8 @@ extern "C" int nvk_paged_prefill(void* out, const void* query, const void* key_c
   CUtensorMap qm, km, vm;
   if ((rc = kv_tensor_map(&qm, query, total_q, num_heads, kRows)) != NVK_OK) return rc;
   const int64_t rows = static_cast<int64_t>(num_blocks) * block_size;
-  if ((rc = kv_tensor_map(&km, key_cache, rows, num_kv_heads, kRows)) != NVK_OK) return rc;
-  if ((rc = kv_tensor_map(&vm, value_cache, rows, num_kv_heads, kRows)) != NVK_OK) return rc;
+  if ((rc = kv_tensor_map(&km, key_cache, rows, num_kv_heads, kKeys)) != NVK_OK) return rc;
+  if ((rc = kv_tensor_map(&vm, value_cache, rows, num_kv_heads, kKeys)) != NVK_OK) return rc;
   PrefillArgs a{};
   a.out = static_cast<__nv_bfloat16*>(out);
   a.block_tables = block_tables;
@@ -460,8 +467,8 @@ extern "C" int nvk_dense_prefill(void* out, const void* query, const void* key, 
     return fail(NVK_ERR_INVALID_ARGUMENT, "dense_prefill: null pointer or no keys");
   CUtensorMap qm, km, vm;
   if ((rc = kv_tensor_map(&qm, query, total_q, num_heads, kRows)) != NVK_OK) return rc;
-  if ((rc = kv_tensor_map(&km, key, total_kv, num_kv_heads, kRows)) != NVK_OK) return rc;
-  if ((rc = kv_tensor_map(&vm, value, total_kv, num_kv_heads, kRows)) != NVK_OK) return rc;
+  if ((rc = kv_tensor_map(&km, key, total_kv, num_kv_heads, kKeys)) != NVK_OK) return rc;
+  if ((rc = kv_tensor_map(&vm, value, total_kv, num_kv_heads, kKeys)) != NVK_OK) return rc;
   PrefillArgs a{};
   a.out = static_cast<__nv_bfloat16*>(out);
   a.block_tables = nullptr;
