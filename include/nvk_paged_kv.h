@@ -32,6 +32,8 @@
  *   nvk_qk_norm_rope_append
  *                      <- q_norm + k_norm + apply_rotary_pos_emb_tnd + PagedKVCache.write,
  *                         src/nanovllm_ascend/models/qwen3.py:83-96, fused
+ *   nvk_prefix_*       <- BlockManager's prefix-cache keys and lookup,
+ *                         src/nanovllm_ascend/npu/block_manager.py:57-192 (host code)
  *   nvk_decode_metadata
  *                      <- BlockManager.prepare_decode_metadata's table / length / slot
  *                         building, src/nanovllm_ascend/npu/block_manager.py:207-250,304-328
@@ -249,6 +251,33 @@ NVK_API int nvk_decode_metadata(int32_t* table_mirror, int mirror_stride, int mi
                                 const int32_t* update_block, int32_t* block_tables, int block_table_stride,
                                 int block_table_width, int32_t* context_lens, int64_t* slot_mapping, int* error_word,
                                 nvk_stream_t stream);
+
+/*
+ * ---- Prefix-cache index (host code) ----
+ * The chained exact-content block keys and key -> cached-blocks map behind
+ * BlockManager's prefix cache (src/nanovllm_ascend/npu/block_manager.py:57-65,
+ * :76-81, :89, :136-192). A block's key is (parent block's key, the block's
+ * token ids); lookup walks the chain and returns each key's first cached
+ * block; a reused physical block forgets its key (nvk_prefix_forget_block).
+ * Not thread-safe: one index per BlockManager, driven by one host thread.
+ */
+typedef struct nvk_prefix_index nvk_prefix_index;
+
+NVK_API int nvk_prefix_create(int num_blocks, int block_size, nvk_prefix_index** out);
+NVK_API void nvk_prefix_destroy(nvk_prefix_index* index);
+/* Longest chain of cached full blocks of token_ids (at most max_blocks): *count ids into block_ids. */
+NVK_API int nvk_prefix_find_longest(nvk_prefix_index* index, const int64_t* token_ids, int64_t num_tokens,
+                                    int max_blocks, int32_t* block_ids, int* count);
+/* Keys blocks table[num_cached_blocks .. num_full_blocks) by token_ids (blocks already keyed are kept). */
+NVK_API int nvk_prefix_cache_blocks(nvk_prefix_index* index, const int32_t* table, int table_len,
+                                    int num_cached_blocks, int num_full_blocks, const int64_t* token_ids,
+                                    int64_t num_tokens);
+NVK_API int nvk_prefix_forget_block(nvk_prefix_index* index, int block_id);
+/* The block's key (interned id), -1 when it is not cached. */
+NVK_API int64_t nvk_prefix_block_key(const nvk_prefix_index* index, int block_id);
+NVK_API int nvk_prefix_clear(nvk_prefix_index* index);
+NVK_API int64_t nvk_prefix_num_cached_keys(const nvk_prefix_index* index);
+NVK_API int64_t nvk_prefix_num_keys(const nvk_prefix_index* index);
 
 /*
  * ---- KV-head-sharded decode, outputs gathered across GPUs in the kernel ----

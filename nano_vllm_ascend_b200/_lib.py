@@ -65,6 +65,15 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         [_c_void_p, _i32, _i32, _c_void_p, _c_void_p, _i32, _i32, _i32, _c_void_p, _c_void_p, _c_void_p, _c_void_p,
          _i32, _i32, _c_void_p, _c_void_p, _c_void_p, _c_void_p],
     ),
+    "nvk_prefix_create": (_i32, [_i32, _i32, ctypes.POINTER(_c_void_p)]),
+    "nvk_prefix_destroy": (None, [_c_void_p]),
+    "nvk_prefix_find_longest": (_i32, [_c_void_p, _c_void_p, _i64, _i32, _c_void_p, ctypes.POINTER(_i32)]),
+    "nvk_prefix_cache_blocks": (_i32, [_c_void_p, _c_void_p, _i32, _i32, _i32, _c_void_p, _i64]),
+    "nvk_prefix_forget_block": (_i32, [_c_void_p, _i32]),
+    "nvk_prefix_block_key": (_i64, [_c_void_p, _i32]),
+    "nvk_prefix_clear": (_i32, [_c_void_p]),
+    "nvk_prefix_num_cached_keys": (_i64, [_c_void_p]),
+    "nvk_prefix_num_keys": (_i64, [_c_void_p]),
     "nvk_peer_alloc": (_i32, [_size_t, ctypes.POINTER(_c_void_p)]),
     "nvk_peer_free": (_i32, [_c_void_p]),
     "nvk_peer_export": (_i32, [_c_void_p, _c_void_p]),

@@ -20,18 +20,23 @@ push-back and removal by id instead of list.pop(0)/list.remove), and chain
 keys are interned as integers with reference counts, so hashing a block costs
 O(block_size) whatever its depth in the chain; a key lives exactly as long as
 a block or a child key refers to it, which keeps lookups identical to keying
-by the full nested content. Block tables are built with one host-to-device
-copy instead of one per row.
+by the full nested content. By default the keys, the key -> blocks map and
+the longest-prefix walk run in C++ (``nvk_prefix_*`` in libnvk_paged.so);
+``native_prefix=False`` keeps the same rules in Python. Block tables are built
+with one host-to-device copy instead of one per row.
 """
 
 from __future__ import annotations
 
+import ctypes
 import math
 from collections import OrderedDict
 from dataclasses import dataclass
 
 import numpy as np
 import torch
+
+from . import _lib
 
 ChainKey = int
 
@@ -133,6 +138,60 @@ class _ChainKeys:
         return len(self._entries)
 
 
+def _token_array(token_ids) -> np.ndarray:
+    if isinstance(token_ids, torch.Tensor):
+        token_ids = token_ids.detach().cpu().numpy()
+    return np.ascontiguousarray(np.asarray(token_ids, dtype=np.int64).reshape(-1))
+
+
+class _NativePrefixIndex:
+    """The prefix-cache keys in C++ (nvk_prefix_*): same rules as _ChainKeys
+    plus the key -> cached-blocks map and the per-block keys."""
+
+    def __init__(self, num_blocks: int, block_size: int) -> None:
+        self._lib = _lib.load()
+        handle = ctypes.c_void_p()
+        _lib.call("nvk_prefix_create", num_blocks, block_size, ctypes.byref(handle))
+        self._h = handle
+
+    def __del__(self) -> None:
+        if getattr(self, "_h", None) is not None and self._h.value:
+            self._lib.nvk_prefix_destroy(self._h)
+            self._h = None
+
+    def find_longest(self, token_ids, max_blocks: int) -> list[int]:
+        if max_blocks <= 0:
+            return []
+        tokens = _token_array(token_ids)
+        out = np.zeros(max_blocks, dtype=np.int32)
+        count = ctypes.c_int(0)
+        _lib.call("nvk_prefix_find_longest", self._h, tokens.ctypes.data, tokens.size, max_blocks, out.ctypes.data,
+                  ctypes.byref(count))
+        return [int(b) for b in out[: count.value]]
+
+    def cache_blocks(self, table: list[int], num_cached: int, num_full: int, token_ids) -> None:
+        tokens = _token_array(token_ids)
+        tab = np.ascontiguousarray(np.asarray(table, dtype=np.int32))
+        _lib.call("nvk_prefix_cache_blocks", self._h, tab.ctypes.data, tab.size, num_cached, num_full,
+                  tokens.ctypes.data, tokens.size)
+
+    def forget(self, block_id: int) -> None:
+        _lib.call("nvk_prefix_forget_block", self._h, block_id)
+
+    def key(self, block_id: int) -> int | None:
+        k = int(self._lib.nvk_prefix_block_key(self._h, block_id))
+        return None if k < 0 else k
+
+    def clear(self) -> None:
+        _lib.call("nvk_prefix_clear", self._h)
+
+    def num_cached_keys(self) -> int:
+        return int(self._lib.nvk_prefix_num_cached_keys(self._h))
+
+    def __len__(self) -> int:  # interned keys (cached or parents of cached ones)
+        return int(self._lib.nvk_prefix_num_keys(self._h))
+
+
 class BlockManager:
     """Unified block pool for runtime allocation and prefix-cache reuse.
 
@@ -141,13 +200,15 @@ class BlockManager:
     handed out again.
     """
 
-    def __init__(self, num_blocks: int, block_size: int, device: torch.device | str):
+    def __init__(self, num_blocks: int, block_size: int, device: torch.device | str, *,
+                 native_prefix: bool = True):
         self.num_blocks = num_blocks
         self.block_size = block_size
         self.device = device
         self.blocks = [BlockState(block_id=i) for i in range(num_blocks)]
         self._free = _FreeQueue(range(num_blocks))
-        self._keys = _ChainKeys()
+        self._native = _NativePrefixIndex(num_blocks, block_size) if native_prefix else None
+        self._keys = self._native if native_prefix else _ChainKeys()
         self._cached: dict[ChainKey, list[int]] = {}
         self.block_tables: dict[int, list[int]] = {}
         self.seq_lens: dict[int, int] = {}
@@ -173,6 +234,11 @@ class BlockManager:
 
     def _forget_key(self, block_id: int) -> None:
         block = self.blocks[block_id]
+        if self._native is not None:
+            if block.block_hash is not None:
+                self._native.forget(block_id)
+                block.block_hash = None
+            return
         key = block.block_hash
         if key is None:
             return
@@ -236,6 +302,8 @@ class BlockManager:
 
     # ------------------------------------------------------- prefix cache --
     def find_longest_prefix_blocks(self, token_ids, max_cache_blocks: int) -> list[int]:
+        if self._native is not None:
+            return self._native.find_longest(token_ids, max_cache_blocks)
         found: list[int] = []
         parent: ChainKey | None = None
         for block_idx in range(max_cache_blocks):
@@ -253,6 +321,11 @@ class BlockManager:
         total_full = num_full_blocks
         if total_full is None:
             total_full = int(token_ids.numel()) // self.block_size
+        if self._native is not None:
+            self._native.cache_blocks(table, num_cached_blocks, total_full, token_ids)
+            for block_id in table[num_cached_blocks:total_full]:
+                self.blocks[block_id].block_hash = self._native.key(block_id)
+            return
         parent: ChainKey | None = None
         if num_cached_blocks > 0:
             parent = self.blocks[table[num_cached_blocks - 1]].block_hash
@@ -271,11 +344,13 @@ class BlockManager:
         if self.block_tables or any(block.ref_count > 0 for block in self.blocks):
             raise RuntimeError("cannot clear prefix cache with active sequences")
         self._cached.clear()
-        self._keys.clear()
+        self._keys.clear()  # the native index or the Python one
         for block in self.blocks:
             block.block_hash = None
 
     def num_cached_keys(self) -> int:
+        if self._native is not None:
+            return self._native.num_cached_keys()
         return len(self._cached)
 
     # ------------------------------------------------------------ metadata --

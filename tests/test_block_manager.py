@@ -108,3 +108,41 @@ def test_free_queue_setter_permutes_allocation_order():
     assert md.block_tables.tolist() == [[3, 1, 0]]
     assert bm.free_block_ids == [2]
     assert _md(md)["slot_mapping"] == [6, 7, 2, 3, 0]
+
+
+@pytest.mark.parametrize("seed", [1, 2, 3, 4, 5])
+def test_native_prefix_index_matches_python_side_by_side(seed):
+    """The C++ prefix index (nvk_prefix_*) and the Python one give identical
+    observable behaviour on seeded scripts with shared prefixes, decode steps,
+    frees, block reuse and cache clears."""
+    from functools import partial
+
+    from tests.golden.make_golden import random_script
+
+    ops = random_script(seed, num_blocks=48, block_size=4, steps=250)
+    native = run_script(partial(BlockManager, native_prefix=True), ops, 48, 4)
+    python = run_script(partial(BlockManager, native_prefix=False), ops, 48, 4)
+    assert native == python
+    assert any(r.get("cached") for r in native if r["op"] == "admit")
+
+
+def test_native_prefix_index_keys_track_block_reuse():
+    for native in (True, False):
+        bm = BlockManager(num_blocks=6, block_size=2, device="cpu", native_prefix=native)
+        a = torch.tensor([1, 2, 3, 4, 5, 6, 7], dtype=torch.long)
+        bm.prepare_prefill_metadata(slots=[0], seq_lens=[7], start_positions=[0], prefix_block_ids=[[]])
+        bm.cache_full_blocks(slot=0, token_ids=a)
+        assert bm.num_cached_keys() == 3 and len(bm._keys) == 3
+        bm.free_slot(0)
+        assert bm.find_longest_prefix_blocks(a, max_cache_blocks=3) == [0, 1, 2]
+        # a second prompt sharing two blocks
+        b = torch.tensor([1, 2, 3, 4, 9, 9], dtype=torch.long)
+        hit = bm.find_longest_prefix_blocks(b, max_cache_blocks=2)
+        assert hit == [0, 1]
+        bm.prepare_prefill_metadata(slots=[1], seq_lens=[2], start_positions=[4], prefix_block_ids=[hit])
+        bm.cache_full_blocks(slot=1, token_ids=b, num_cached_blocks=2)
+        assert bm.num_cached_keys() == 4
+        bm.free_slot(1)
+        bm.clear_prefix_cache()
+        assert bm.num_cached_keys() == 0 and len(bm._keys) == 0
+        assert all(blk.block_hash is None for blk in bm.blocks)
