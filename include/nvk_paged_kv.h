@@ -32,6 +32,8 @@
  *   nvk_qk_norm_rope_append
  *                      <- q_norm + k_norm + apply_rotary_pos_emb_tnd + PagedKVCache.write,
  *                         src/nanovllm_ascend/models/qwen3.py:83-96, fused
+ *   nvk_lm_head_argmax <- lm_head + greedy Sampler.sample + per-sequence .item(),
+ *                         src/nanovllm_ascend/model_runner.py:284-286, qwen3.py:221
  *   nvk_prefix_*       <- BlockManager's prefix-cache keys and lookup,
  *                         src/nanovllm_ascend/npu/block_manager.py:57-192 (host code)
  *   nvk_decode_metadata
@@ -251,6 +253,23 @@ NVK_API int nvk_decode_metadata(int32_t* table_mirror, int mirror_stride, int mi
                                 const int32_t* update_block, int32_t* block_tables, int block_table_stride,
                                 int block_table_width, int32_t* context_lens, int64_t* slot_mapping, int* error_word,
                                 nvk_stream_t stream);
+
+/*
+ * LM head + greedy argmax for a decode batch: token_ids[b] = argmax_v
+ * bf16(hidden[b] . weight[v]) (ties: the smallest v), i.e. Qwen3ForCausalLM's
+ * lm_head (src/nanovllm_ascend/models/qwen3.py:196,221) followed by the greedy
+ * branch of Sampler.sample (layers/sampler.py:13-14), without the per-sequence
+ * .item() of ModelRunner.decode (model_runner.py:284-286). hidden: bf16
+ * [batch, hidden_size] rows hidden_stride ELEMENTS apart; weight: bf16
+ * [vocab_size, hidden_size] contiguous; token_ids: int64 [batch], device.
+ * workspace: nvk_lm_head_argmax_workspace_size bytes, zeroed once (every call
+ * leaves it zeroed). batch <= 128, hidden_size a multiple of 128. num_ctas 0 =
+ * one CTA per SM. A timed-out wait sets bit 1 of error_word.
+ */
+NVK_API int nvk_lm_head_argmax_workspace_size(int batch, size_t* bytes);
+NVK_API int nvk_lm_head_argmax(const void* hidden, int64_t hidden_stride, const void* weight, int vocab_size,
+                               int hidden_size, int batch, int64_t* token_ids, void* workspace,
+                               size_t workspace_bytes, int num_ctas, int* error_word, nvk_stream_t stream);
 
 /*
  * ---- Prefix-cache index (host code) ----

@@ -65,6 +65,11 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         [_c_void_p, _i32, _i32, _c_void_p, _c_void_p, _i32, _i32, _i32, _c_void_p, _c_void_p, _c_void_p, _c_void_p,
          _i32, _i32, _c_void_p, _c_void_p, _c_void_p, _c_void_p],
     ),
+    "nvk_lm_head_argmax_workspace_size": (_i32, [_i32, ctypes.POINTER(_size_t)]),
+    "nvk_lm_head_argmax": (
+        _i32,
+        [_c_void_p, _i64, _c_void_p, _i32, _i32, _i32, _c_void_p, _c_void_p, _size_t, _i32, _c_void_p, _c_void_p],
+    ),
     "nvk_prefix_create": (_i32, [_i32, _i32, ctypes.POINTER(_c_void_p)]),
     "nvk_prefix_destroy": (None, [_c_void_p]),
     "nvk_prefix_find_longest": (_i32, [_c_void_p, _c_void_p, _i64, _i32, _c_void_p, ctypes.POINTER(_i32)]),

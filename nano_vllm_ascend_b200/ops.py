@@ -138,6 +138,37 @@ def qk_norm_rope_append(
     return query_out
 
 
+# ----------------------------------------------------- lm head + argmax ---
+def lm_head_argmax_workspace_bytes(batch: int) -> int:
+    out = ctypes.c_size_t(0)
+    _lib.call("nvk_lm_head_argmax_workspace_size", batch, ctypes.byref(out))
+    return int(out.value)
+
+
+def lm_head_argmax(hidden: torch.Tensor, weight: torch.Tensor, workspace: torch.Tensor,
+                   token_ids: torch.Tensor | None = None, num_ctas: int = 0,
+                   error_word: torch.Tensor | None = None) -> torch.Tensor:
+    """Greedy next tokens of a decode batch: argmax over the vocabulary of the
+    bf16 logits hidden @ weight.T (first index on ties), int64 [batch] on the
+    device. ``workspace`` (uint8, zeroed once) holds
+    lm_head_argmax_workspace_bytes(batch); ``error_word`` a device int32."""
+    dev = hidden.device
+    for name, t in (("hidden", hidden), ("weight", weight), ("workspace", workspace)):
+        _require_cuda(name, t, dev)
+    if hidden.dtype != _BF16 or weight.dtype != _BF16 or hidden.dim() != 2 or weight.dim() != 2 \
+            or hidden.stride(1) != 1 or not weight.is_contiguous() or weight.shape[1] != hidden.shape[1]:
+        raise ValueError("lm_head_argmax: hidden [batch, H] and weight [vocab, H] must be bf16 with unit inner stride")
+    batch, hsize = hidden.shape
+    if token_ids is None:
+        token_ids = torch.empty(batch, dtype=torch.int64, device=dev)
+    if error_word is None:
+        error_word = torch.zeros(1, dtype=torch.int32, device=dev)
+    _lib.call("nvk_lm_head_argmax", _ptr(hidden), hidden.stride(0), _ptr(weight), weight.shape[0], hsize, batch,
+              _ptr(token_ids), _ptr(workspace), workspace.numel() * workspace.element_size(), int(num_ctas),
+              _ptr(error_word), _stream(dev))
+    return token_ids
+
+
 # ----------------------------------------------------------------- decode ---
 def decode_workspace_bytes(batch: int, num_heads: int, num_kv_heads: int, head_dim: int, num_ctas: int = 0) -> int:
     """Workspace bytes of paged_decode (num_ctas 0 = one CTA per SM of the current device)."""

@@ -116,6 +116,20 @@ def qk_norm_rope_append(q: np.ndarray, k: np.ndarray, v: np.ndarray, q_weight: n
     return q_out
 
 
+# ------------------------------------------------------ lm head + argmax ----
+def lm_head_logits(hidden: np.ndarray, weight: np.ndarray) -> np.ndarray:
+    """bf16 logits of Qwen3ForCausalLM's lm_head (models/qwen3.py:196,221):
+    hidden [B, H] and weight [V, H] as bf16 bits, f32 products summed in f32,
+    rounded to bf16; returned as f32 values."""
+    return bf16_bits_to_f32(f32_to_bf16_bits(as_f32(hidden) @ as_f32(weight).T))
+
+
+def greedy_tokens(logits: np.ndarray) -> np.ndarray:
+    """Sampler.sample's greedy branch (layers/sampler.py:13-14): torch.argmax
+    over the vocabulary, the first index among equal maxima."""
+    return np.argmax(logits, axis=-1).astype(np.int64)
+
+
 # ---------------------------------------------------------------- decode ----
 def as_f32(x: np.ndarray) -> np.ndarray:
     """uint16 arrays are bf16 bit patterns; anything else is cast to f32."""
