@@ -70,8 +70,9 @@ __device__ __forceinline__ void norm_rope_row(uint32_t w_lo, uint32_t w_hi, floa
 
 // One warp per group of group_rows head rows of one token (rows: the q heads,
 // then the k heads, then the v heads): the token's position, slot and
-// cos/sin pairs are loaded once per group, and the group's rows go four at a
-// time (loads of four rows in flight before their reductions).
+// cos/sin pairs are loaded once per group, and the group's rows go kBatch at
+// a time (loads of kBatch rows in flight before their reductions).
+constexpr int kBatch = 8;
 
 __global__ void __launch_bounds__(kWarps * 32) qk_norm_rope_append_kernel(const NormRopeArgs a) {
   pdl_launch_dependents();
@@ -108,10 +109,10 @@ __global__ void __launch_bounds__(kWarps * 32) qk_norm_rope_append_kernel(const 
       s0 = make_float2(round_bf16(sr[2 * lane]), round_bf16(sr[2 * lane + 1]));
       s1 = make_float2(round_bf16(sr[64 + 2 * lane]), round_bf16(sr[65 + 2 * lane]));
     }
-    for (int r0 = r_lo; r0 < r_hi; r0 += 4) {
-      uint32_t lo[4], hi[4];
+    for (int r0 = r_lo; r0 < r_hi; r0 += kBatch) {
+      uint32_t lo[kBatch], hi[kBatch];
 #pragma unroll
-      for (int u = 0; u < 4; ++u) {
+      for (int u = 0; u < kBatch; ++u) {
         const int r = r0 + u;
         const __nv_bfloat16* src = r < a.num_heads ? a.q + t * a.q_stride + r * kD
                                  : r < nqk       ? a.k + t * a.k_stride + (r - a.num_heads) * kD
@@ -120,7 +121,7 @@ __global__ void __launch_bounds__(kWarps * 32) qk_norm_rope_append_kernel(const 
         hi[u] = r < r_hi ? *reinterpret_cast<const uint32_t*>(src + 64 + 2 * lane) : 0u;
       }
 #pragma unroll
-      for (int u = 0; u < 4; ++u) {
+      for (int u = 0; u < kBatch; ++u) {
         const int r = r0 + u;
         if (r >= r_hi) break;
         __nv_bfloat16* dst;
