@@ -19,6 +19,11 @@ Workloads (seeded synthetic inputs with the configs' shapes; no model weights):
       its own pool (sequence-sharded replicas, no collective): weak scaling.
   decode_c4: 256 sequences, context ~ U[2048, 6144], split evenly across
       ranks by sequence (strong scaling).
+  kernels: the path's other kernels timed one by one under CUDA graphs on
+      config-sized inputs (prefill-sized append, decode- and prefill-sized
+      q/k norm + RoPE + append, device decode metadata, LM head + greedy
+      argmax over the 151,936-token vocabulary), with bytes moved and the
+      fraction of the measured HBM copy bandwidth.
   decode_c5: Qwen3-8B KV shapes (36 layers, 32 query / 8 KV heads), 128
       sequences at context 8192, KV-head sharded over N in {2, 4, 8} GPUs
       (the pool does not fit one GPU). Per layer: append of this rank's KV
@@ -80,6 +85,8 @@ WORKLOADS = {
     "decode_c5": Workload("decode_c5", 36, 128, 32, 8, 8192, 8192, "strong",
                           describe="config[4]: Qwen3-8B KV cache, 128 seqs at ctx 8192, KV-head sharded, "
                                    "outputs all-gathered"),
+    "kernels": Workload("kernels", 28, 32, 16, 8, 256, 2304, "weak",
+                        describe="the hot path's other kernels on config-2/3-sized inputs"),
     # prefill: ctx_lo = cached prefix tokens, ctx_hi = new tokens per request
     "prefill_c3": Workload("prefill_c3", 28, 32, 16, 8, 768, 256, "weak",
                            describe="config[2]: Qwen3-0.6B prefix-cache prefill, 32 requests x (768 cached + 256 new)"),
@@ -591,6 +598,108 @@ def run_ours(args, world, rank, local):
     return 0
 
 
+# ------------------------------------------------------------- kernels ----
+def graph_time(fn, launches: int, device) -> float:
+    """Average device time (s) of fn() over `launches` calls captured in one CUDA graph."""
+    stream = torch.cuda.Stream(device)
+    with torch.cuda.stream(stream):
+        fn()
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            for _ in range(launches):
+                fn()
+        for _ in range(2):
+            graph.replay()
+        torch.cuda.synchronize()
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record(stream)
+        for _ in range(3):
+            graph.replay()
+        end.record(stream)
+        end.synchronize()
+    del graph
+    return start.elapsed_time(end) / 1e3 / (3 * launches)
+
+
+def run_kernels(args, world, rank, local):
+    """The hot path's kernels other than decode/prefill attention, one by one."""
+    from nano_vllm_ascend_b200 import BlockManager, ops
+    from nano_vllm_ascend_b200.device_metadata import DeviceBlockTables
+
+    device = torch.device("cuda", local)
+    peak, peak_kind = peaks()
+    g = torch.Generator(device=device).manual_seed(0)
+    kvh, h, d, nb = 8, 16, 128, 2048
+    kc = torch.zeros(nb, BLOCK, kvh, d, dtype=torch.bfloat16, device=device)
+    vc = torch.zeros_like(kc)
+    out = {}
+    n = 4 if args.quick else 20
+
+    # prefill-sized append (config 3: 256 new tokens x 32 requests)
+    rows = 8192
+    slots = torch.randperm(nb * BLOCK, device=device)[:rows].sort().values
+    k = torch.randn(rows, kvh, d, generator=g, device=device).to(torch.bfloat16)
+    v = torch.randn(rows, kvh, d, generator=g, device=device).to(torch.bfloat16)
+    t = graph_time(lambda: ops.kv_append(kc, vc, k, v, slots), n, device)
+    byts = rows * kvh * d * 2 * 2 * 2 + rows * 8
+    out["kv_append_8192"] = {"us": t * 1e6, "bytes": byts, "gbs": byts / t / 1e9, "frac": byts / t / 1e9 / peak}
+
+    # q/k RMSNorm + RoPE + append, decode (32 tokens) and prefill (8192 tokens) sized
+    inv = 1.0 / (1e6 ** (torch.arange(0, d, 2, dtype=torch.float32) / d))
+    emb = torch.cat([torch.outer(torch.arange(40960, dtype=torch.float32), inv)] * 2, dim=-1)
+    cos, sin = emb.cos().to(device), emb.sin().to(device)
+    wq = torch.ones(d, dtype=torch.bfloat16, device=device)
+    for tokens in (32, 8192):
+        qkv = torch.randn(tokens, h + 2 * kvh, d, generator=g, device=device).to(torch.bfloat16)
+        q_out = torch.empty(tokens, h, d, dtype=torch.bfloat16, device=device)
+        pos = torch.randint(0, 40960, (tokens,), device=device)
+        sl = slots[:tokens]
+        t = graph_time(lambda: ops.qk_norm_rope_append(qkv[:, :h], qkv[:, h:h + kvh], qkv[:, h + kvh:], wq, wq, 1e-6,
+                                                       cos, sin, pos, kc, vc, sl, query_out=q_out), n, device)
+        byts = tokens * ((h + 2 * kvh) * d * 2 * 2 + 8 * 2)  # read q, k, v; write q, k, v; positions, slots
+        out[f"qk_norm_rope_append_{tokens}"] = {"us": t * 1e6, "bytes": byts, "gbs": byts / t / 1e9,
+                                                "frac": byts / t / 1e9 / peak}
+
+    # device decode metadata for a 32-sequence step
+    bm = BlockManager(nb, BLOCK, device)
+    ctx = torch.randint(256, 2305, (32,), generator=torch.Generator().manual_seed(1000)).tolist()
+    bm.prepare_prefill_metadata(list(range(32)), ctx, [0] * 32, [[] for _ in range(32)])
+    dt = DeviceBlockTables(bm, 64, 64, device)
+    dt.prepare_decode_metadata(list(range(32)), ctx, 1)
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for i in range(50):
+        dt.prepare_decode_metadata(list(range(32)), [c + 1 + i for c in ctx], 1)
+    torch.cuda.synchronize()
+    t_dev = (time.perf_counter() - t0) / 50
+    bm2 = BlockManager(nb, BLOCK, device)
+    bm2.prepare_prefill_metadata(list(range(32)), ctx, [0] * 32, [[] for _ in range(32)])
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for i in range(50):
+        bm2.prepare_decode_metadata(list(range(32)), [c + 1 + i for c in ctx], 1)
+    torch.cuda.synchronize()
+    t_host = (time.perf_counter() - t0) / 50
+    out["decode_metadata_32"] = {"host_us_device_path": t_dev * 1e6, "host_us_reference_path": t_host * 1e6}
+
+    # LM head + greedy argmax, 32 rows over the Qwen3-0.6B vocabulary
+    vocab, hid = 151936, 1024
+    weight = (torch.randn(vocab, hid, generator=g, device=device) * 0.05).to(torch.bfloat16)
+    hidden = torch.randn(32, hid, generator=g, device=device).to(torch.bfloat16)
+    ws = torch.zeros(ops.lm_head_argmax_workspace_bytes(32), dtype=torch.uint8, device=device)
+    ids = torch.empty(32, dtype=torch.int64, device=device)
+    t = graph_time(lambda: ops.lm_head_argmax(hidden, weight, ws, ids), n, device)
+    byts = vocab * hid * 2
+    out["lm_head_argmax_32"] = {"us": t * 1e6, "bytes": byts, "gbs": byts / t / 1e9, "frac": byts / t / 1e9 / peak}
+    if rank == 0:
+        print(json.dumps({"metric": "kernel GB/s (graph-timed)", "value": out["kv_append_8192"]["gbs"], "unit": "GB/s",
+                          "n_gpus": world, "higher_is_better": True, "dtype": "bf16", "data": "synthetic",
+                          "config": {"workload": WORKLOADS["kernels"].describe}, "peak": peak, "peak_kind": peak_kind,
+                          "kernels": out}), flush=True)
+    return 0
+
+
 # ------------------------------------------------------------ config 5 ----
 def run_c5_ours(args, world, rank, local):
     """KV-head-sharded decode step (config 5) with the outputs all-gathered."""
@@ -1015,6 +1124,8 @@ def main():
         return run_prefill_ours(args, world, rank, local)
     if args.workload == "decode_c5":
         return run_c5_ours(args, world, rank, local)
+    if args.workload == "kernels":
+        return run_kernels(args, world, rank, local)
     return run_ours(args, world, rank, local)
 
 
