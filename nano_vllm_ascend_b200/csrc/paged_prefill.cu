@@ -293,23 +293,32 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) prefill_kernel(const __g
       const int sb = j % kSBufs;
       if (!__all_sync(0xffffffffu, mbar_wait(&sm.s_full[sb], (j / kSBufs) & 1))) { ok = false; break; }
       tc_fence_after();
+      // S row in two 32-column halves: the second half loads while the
+      // first half's maximum is taken.
       uint32_t sr[2][32];
-#pragma unroll
-      for (int c = 0; c < 2; ++c) tmem_ld32(tmem_s + sb * kKeys + t_lane + c * 32, sr[c]);
+      tmem_ld32(tmem_s + sb * kKeys + t_lane, sr[0]);
       tmem_ld_wait();
+      tmem_ld32(tmem_s + sb * kKeys + t_lane + 32, sr[1]);
       const int kbase = j * kKeys;
       const bool need_mask = kbase + kKeys - 1 > lim;
       // The max is taken over raw scores (scale > 0), the scale folded into
-      // the exponent's FMA below.
-      float mraw = -INFINITY;
+      // the exponent's FMA below; max is exact, so its order is free.
+      float mx0 = -INFINITY, mx1 = -INFINITY;
 #pragma unroll
       for (int c = 0; c < 2; ++c) {
+        if (c == 1) tmem_ld_wait();
+        if (need_mask) {
 #pragma unroll
-        for (int e = 0; e < 32; ++e) {
-          if (need_mask && kbase + c * 32 + e > lim) sr[c][e] = __float_as_uint(-INFINITY);
-          mraw = fmaxf(mraw, __uint_as_float(sr[c][e]));
+          for (int e = 0; e < 32; ++e)
+            if (kbase + c * 32 + e > lim) sr[c][e] = __float_as_uint(-INFINITY);
+        }
+#pragma unroll
+        for (int e = 0; e < 32; e += 4) {
+          mx0 = fmax3(mx0, __uint_as_float(sr[c][e]), __uint_as_float(sr[c][e + 1]));
+          mx1 = fmax3(mx1, __uint_as_float(sr[c][e + 2]), __uint_as_float(sr[c][e + 3]));
         }
       }
+      const float mraw = fmaxf(mx0, mx1);
       const float mt = mraw * a.scale_log2;
       const float m_new = fmaxf(m, mt);
       const bool resc = m_new > m + kRescaleThreshold;
@@ -335,8 +344,9 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) prefill_kernel(const __g
         m = m_new;
       }
       const float neg_mu = (m == -INFINITY) ? 0.f : -m;
-      const float sc = a.scale_log2;
-      float sum = 0.f;
+      const uint64_t sc2 = f32x2_pack(a.scale_log2, a.scale_log2);
+      const uint64_t nm2 = f32x2_pack(neg_mu, neg_mu);
+      uint64_t sum2[2] = {f32x2_pack(0.f, 0.f), f32x2_pack(0.f, 0.f)};  // two add chains
       // P over the first 32 columns of the S buffer (S is in registers now):
       // column k holds keys 2k and 2k+1 of this row as a bf16 pair.
 #pragma unroll
@@ -344,14 +354,19 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) prefill_kernel(const __g
         uint32_t w[16];
 #pragma unroll
         for (int e = 0; e < 16; ++e) {
-          const float p0 = fast_exp2(fmaf(__uint_as_float(sr[c][2 * e]), sc, neg_mu));
-          const float p1 = fast_exp2(fmaf(__uint_as_float(sr[c][2 * e + 1]), sc, neg_mu));
-          sum += p0 + p1;
+          const uint64_t x2 = f32x2_fma(
+              f32x2_pack(__uint_as_float(sr[c][2 * e]), __uint_as_float(sr[c][2 * e + 1])), sc2, nm2);
+          float x0, x1;
+          f32x2_unpack(x2, x0, x1);
+          const float p0 = fast_exp2(x0), p1 = fast_exp2(x1);
+          sum2[e & 1] = f32x2_add(sum2[e & 1], f32x2_pack(p0, p1));
           w[e] = pack_bf16x2(p0, p1);
         }
         tmem_st16(tmem_s + sb * kKeys + c * 16 + t_lane, w);
       }
-      l += sum;
+      float s_lo, s_hi;
+      f32x2_unpack(f32x2_add(sum2[0], sum2[1]), s_lo, s_hi);
+      l += s_lo + s_hi;
       tmem_st_wait();
       tc_fence_before();
       mbar_arrive(&sm.p_full[sb]);
