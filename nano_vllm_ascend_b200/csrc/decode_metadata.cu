@@ -26,7 +26,9 @@ __global__ void __launch_bounds__(kRowsPerBlock * 32) decode_metadata_kernel(
     const int32_t* __restrict__ update_offsets, const int32_t* __restrict__ update_idx,
     const int32_t* __restrict__ update_block, int32_t* __restrict__ tables_out, int out_stride, int out_width,
     int32_t* __restrict__ context_lens_out, int64_t* __restrict__ slot_mapping_out, int* __restrict__ error_word) {
-  pdl_launch_dependents();
+  // No early trigger: the decode kernel reads the tables and lengths written
+  // here before its griddepcontrol.wait, so a dependent grid may only start
+  // once this one has finished (the implicit trigger at grid completion).
   pdl_wait();
   const int b = blockIdx.x * kRowsPerBlock + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;

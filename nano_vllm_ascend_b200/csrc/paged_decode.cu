@@ -535,15 +535,17 @@ __global__ void __launch_bounds__(kThreads, 1) paged_decode_kernel(const __grid_
     tmem_relinquish();
   }
   pdl_launch_dependents();
-  // While the predecessor drains: warm L2 with the context lengths (every
-  // CTA scans them), and, spread over the grid, the block tables and queries.
-  if (warp == 0) prefetch_l2_range(a.context_lens, int64_t(a.batch) * 4, 0, 1, lane, 32);
-  else {
+  // Programmatic dependent launch: context_lens and block_tables are step
+  // metadata written before the step's first kernel (host copies, or a
+  // metadata kernel that does not trigger its dependents early), so the
+  // schedule and the first chunk's block ids are computed before
+  // griddepcontrol.wait, while the predecessor drains. Everything the predecessor may write (queries, new K/V rows, the
+  // pool, outputs, workspace) is touched only after each warp's own wait.
+  {
     const int64_t bt_bytes = (int64_t(a.batch - 1) * a.bt_stride + a.max_blocks) * 4;
-    prefetch_l2_range(a.block_tables, bt_bytes, c, ctas, tid - 32, kThreads - 32);
-    prefetch_l2_range(a.query, int64_t(a.batch) * a.num_heads * kD * 2, c, ctas, tid - 32, kThreads - 32);
+    prefetch_l2_range(a.block_tables, bt_bytes, c, ctas, tid, kThreads);
+    prefetch_l2_range(a.query, int64_t(a.batch) * a.num_heads * kD * 2, c, ctas, tid, kThreads);
   }
-  pdl_wait();  // nothing above loads global memory
   // ---- per-sequence tile prefix: every CTA derives the same schedule ----
   // All lengths are loaded at once (one round trip), then warp 0 scans them
   // in place.
@@ -601,6 +603,7 @@ __global__ void __launch_bounds__(kThreads, 1) paged_decode_kernel(const __grid_
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  if (warp != kSchedWarp) pdl_wait();  // the scheduler waits after staging its first chunk
 
   const int total = sm.total_tiles;
   const Sched sc = make_sched(total, ctas);
@@ -616,24 +619,25 @@ __global__ void __launch_bounds__(kThreads, 1) paged_decode_kernel(const __grid_
     // copies, so no segment start waits on a global round trip.
     if (lane == 0) tma_prefetch_desc(&qmap);
     int chunk = 0, seg = 0;
-    bool ok = true;
+    bool ok = true, waited = false;
     SegIter it;
     it.init(sm, a, lo, hi);
     Segment s;
+    auto load_q = [&](int sg, const Segment& sq) {  // lane 0
+      const int qb = sg % kQBufs;
+      if (sg >= kQBufs && !mbar_wait(&sm.q_empty[qb], ((sg / kQBufs) - 1) & 1)) ok = false;
+      if (ok) {
+        mbar_arrive_expect_tx(&sm.q_full[qb], static_cast<uint32_t>(2 * QPK * 128));
+        tma_load_3d(sm.q[qb], &qmap, &sm.q_full[qb], 0, sq.g * QPK, sq.b);
+        tma_load_3d(sm.q[qb] + kQHalf, &qmap, &sm.q_full[qb], 64, sq.g * QPK, sq.b);
+      }
+    };
     auto claim = [&](int ch) -> bool {  // ring slot of chunk ch is free
       if (ch < kRingSlots) return true;
       return __all_sync(0xffffffffu, mbar_wait(&sm.ring_empty[ch % kRingSlots], ((ch / kRingSlots) - 1) & 1));
     };
     for (; ok && it.next(sm, a, s); ++seg) {
-      const int qb = seg % kQBufs;
-      if (lane == 0) {
-        if (seg >= kQBufs && !mbar_wait(&sm.q_empty[qb], ((seg / kQBufs) - 1) & 1)) ok = false;
-        if (ok) {
-          mbar_arrive_expect_tx(&sm.q_full[qb], static_cast<uint32_t>(2 * QPK * 128));
-          tma_load_3d(sm.q[qb], &qmap, &sm.q_full[qb], 0, s.g * QPK, s.b);
-          tma_load_3d(sm.q[qb] + kQHalf, &qmap, &sm.q_full[qb], 64, s.g * QPK, s.b);
-        }
-      }
+      if (waited && lane == 0) load_q(seg, s);  // the first segment's query: after the wait below
       ok = __shfl_sync(0xffffffffu, ok, 0);
       const int32_t* bt = a.block_tables + static_cast<int64_t>(s.b) * a.bt_stride;
       for (int i = s.i0; ok && i < s.i0 + s.ntiles; i += a.chunk_tiles, ++chunk) {
@@ -652,6 +656,15 @@ __global__ void __launch_bounds__(kThreads, 1) paged_decode_kernel(const __grid_
             blk = a.num_blocks;  // fully outside the tensor map: zero fill
           }
           ck.ids[k] = blk;
+        }
+        if (!waited) {
+          // First chunk: its ids are staged from step metadata; now wait for
+          // the predecessor before the query copy and the fused append.
+          __syncwarp();
+          pdl_wait();
+          waited = true;
+          if (lane == 0) load_q(seg, s);
+          ok = __shfl_sync(0xffffffffu, ok, 0);
         }
         if (lane == 0) {
           ck.seg = seg;
