@@ -85,3 +85,79 @@ def test_norm_rope_append_bad_slot(cuda_device):
     assert int(err.item()) & 4
     flat = vc.view(-1, 8, 128)
     assert torch.equal(flat[5], k[0]) and int((vc != 0).sum()) == 8 * 128
+
+
+def _prefill_inputs(dev, tokens, h, kvh, row_pad, seed):
+    """q, k, v as slices of one fused QKV buffer whose token stride is
+    (h + 2 kvh) * 128 + row_pad elements (row_pad = 2 makes the rows 4-byte
+    but not 16-byte aligned)."""
+    g = torch.Generator(device=dev).manual_seed(seed)
+    width = (h + 2 * kvh) * 128
+    buf = torch.zeros(tokens, width + row_pad, dtype=torch.bfloat16, device=dev)
+    buf[:, :width] = (torch.randn(tokens, width, generator=g, device=dev) * 3).to(torch.bfloat16)
+    qkv = buf[:, :width].view(tokens, h + 2 * kvh, 128)
+    return qkv[:, :h], qkv[:, h:h + kvh], qkv[:, h + kvh:]
+
+
+def test_norm_rope_append_row_padding_bit_identical(cuda_device):
+    """A prefill-sized launch (one warp per token) over fused-QKV slices whose
+    token stride is padded to break 16-byte row alignment gives the same bits
+    as the aligned layout (q out, k and v pool rows)."""
+    dev = cuda_device
+    tokens, h, kvh = 4096, 16, 8
+    cos, sin = rope_tables(40960)
+    cos, sin = cos.to(dev), sin.to(dev)
+    positions = torch.randint(0, 40960, (tokens,), generator=torch.Generator().manual_seed(8)).to(dev)
+    nb = tokens // 128 + 2
+    slots = torch.randperm(nb * 128, generator=torch.Generator().manual_seed(9))[:tokens].to(dev)
+    w = (1 + 0.1 * torch.randn(2, 128, generator=torch.Generator().manual_seed(10))).to(torch.bfloat16).to(dev)
+    outs = []
+    for pad in (0, 2):
+        q, k, v = _prefill_inputs(dev, tokens, h, kvh, pad, seed=11)
+        assert (q.stride(0) % 8 == 0) == (pad == 0)
+        kc = torch.zeros(nb, 128, kvh, 128, dtype=torch.bfloat16, device=dev)
+        vc = torch.zeros_like(kc)
+        err = torch.zeros(1, dtype=torch.int32, device=dev)
+        q_out = ops.qk_norm_rope_append(q, k, v, w[0], w[1], 1e-6, cos, sin, positions, kc, vc, slots,
+                                        error_word=err)
+        torch.cuda.synchronize()
+        assert int(err.item()) == 0
+        outs.append((q_out, kc, vc))
+    for a, b in zip(outs[0], outs[1]):
+        assert torch.equal(a.view(torch.int16), b.view(torch.int16))
+
+
+def test_norm_rope_append_prefill_bad_slots(cuda_device):
+    """Prefill-sized launch: tokens whose slot is negative or past the pool
+    are flagged and their k/v rows skipped; every other token lands as the
+    oracle says."""
+    dev = cuda_device
+    tokens, h, kvh = 4096, 16, 8
+    q, k, v = _prefill_inputs(dev, tokens, h, kvh, 0, seed=12)
+    cos, sin = rope_tables(4096)
+    positions = torch.randint(0, 4096, (tokens,), generator=torch.Generator().manual_seed(13))
+    nb = tokens // 128 + 2
+    slots = torch.randperm(nb * 128, generator=torch.Generator().manual_seed(14))[:tokens]
+    bad = [7, 2000, 4095]
+    slots[bad[0]], slots[bad[1]], slots[bad[2]] = -1, nb * 128, -5
+    w = torch.ones(128, dtype=torch.bfloat16, device=dev)
+    kc = torch.zeros(nb, 128, kvh, 128, dtype=torch.bfloat16, device=dev)
+    vc = torch.zeros_like(kc)
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
+    q_out = ops.qk_norm_rope_append(q, k, v, w, w, 1e-6, cos.to(dev), sin.to(dev), positions.to(dev), kc, vc,
+                                    slots.to(dev), error_word=err)
+    torch.cuda.synchronize()
+    assert int(err.item()) & 4
+    good = np.setdiff1d(np.arange(tokens), bad)
+    kc_ref = np.zeros((nb, 128, kvh, 128), dtype=np.uint16)
+    vc_ref = np.zeros_like(kc_ref)
+    q_ref = orc.qk_norm_rope_append(bits(q)[good], bits(k)[good], bits(v)[good], bits(w), bits(w), 1e-6,
+                                    cos.numpy(), sin.numpy(), positions.numpy()[good], kc_ref, vc_ref,
+                                    slots.numpy()[good])
+    assert np.array_equal(bits(vc), vc_ref)
+    for got, want in ((bits(q_out)[good], q_ref), (bits(kc), kc_ref)):
+        d = ulp_diff(got, want)
+        assert (d == 0).mean() > 0.99
+        g32, w32 = orc.bf16_bits_to_f32(got), orc.bf16_bits_to_f32(want)
+        row_max = np.abs(w32).max(axis=-1, keepdims=True)
+        assert not (np.abs(g32 - w32) > (np.abs(w32) + row_max) * 2.0 ** -8).any()
