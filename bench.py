@@ -107,16 +107,16 @@ def peaks(key: str = "hbm_gbs") -> tuple[float, str]:
     return fallback[key], "fallback"
 
 
-def profiled_traffic(workload: str) -> float | None:
-    """Per-launch DRAM bytes of the decode kernel from a committed ncu summary
-    (a line 'traffic_bytes_per_launch: N' in profiles/paged_decode_<workload>.txt)."""
-    p = ROOT / "profiles" / f"paged_decode_{workload}.txt"
+def profiled_traffic(workload: str, kernel: str = "paged_decode") -> float | None:
+    """Per-launch DRAM bytes of a kernel from a committed ncu summary (a line
+    'traffic_bytes_per_launch: N' in profiles/<kernel>_<workload>.txt)."""
+    p = ROOT / "profiles" / f"{kernel}_{workload}.txt"
     if not p.exists():
         return None
     for line in p.read_text().splitlines():
         if line.startswith("traffic_bytes_per_launch:"):
             try:
-                return float(line.split(":", 1)[1].strip())
+                return float(line.split(":", 1)[1].split()[0].replace(",", ""))
             except ValueError:
                 return None
     return None
@@ -1060,7 +1060,8 @@ def run_prefill_ours(args, world, rank, local):
                        "us": t_app * 1e6},
             "roofline": {"kernel": "prefill_kernel", "bound": "tensor", "achieved": achieved, "peak": peak,
                          "peak_kind": kind + " (burst, kernel timed alone)", "unit": "TFLOP/s",
-                         "frac": achieved / peak, "traffic": None, "algorithmic_flops_per_launch": flops_layer,
+                         "frac": achieved / peak, "traffic": profiled_traffic(wl.name, "paged_prefill"),
+                         "algorithmic_flops_per_launch": flops_layer,
                          "us_per_launch": t_pf * 1e6},
             "e2e": {"value": flops_all / t_e2e_max / 1e12, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": h_out.numel() * h_out.element_size(), "ms_per_step": t_e2e_max * 1e3},
