@@ -8,22 +8,26 @@
 // lengths. Masking is bottom-right aligned: query i of a sequence with Lq
 // queries and Lk keys sees key j iff j <= Lk - Lq + i.
 //
-// One CTA = 128 query rows of one sequence x one query head.
-//   warp 4 (producer): TMA loads of the Q tile once, then 128-key K and V
-//     tiles (one pool block each, 128-byte swizzle = the canonical UMMA
-//     operand layout): K into a 3-stage ring freed as soon as S has read it,
-//     V into a 3-stage ring freed by PV; K runs two tiles ahead of V, and
+// One CTA = 128 query rows of one sequence x one query head; two CTAs share
+// an SM (96 KB of shared memory and 256 TMEM columns each), so that one
+// CTA's softmax runs while the other's MMAs do.
+//   warp 4 (producer): TMA loads of the Q tile once, then 64-key K and V
+//     tiles (half a pool block each, 128-byte swizzle = the canonical UMMA
+//     operand layout): K into a 2-stage ring freed as soon as S has read it,
+//     V into a 2-stage ring freed by PV; K runs two tiles ahead of V, and
 //     the block ids come 32 at a time (one parallel load per warp).
-//   warp 5 (MMA): allocates 512 TMEM columns (S/P triple buffered: 0-127,
-//     128-255, 256-383; O: 384-511) and one lane issues S = Q K^T (8 x M128 N128 K16,
-//     both K-major) one key tile ahead of O += P V (8 x M128 N128 K16, P read
+//   warp 5 (MMA): allocates 256 TMEM columns (S/P double buffered: 0-63,
+//     64-127; O: 128-255) and one lane issues S = Q K^T (8 x M128 N64 K16,
+//     both K-major) one key tile ahead of O += P V (4 x M128 N128 K16, P read
 //     from TMEM where the softmax wrote it over S(j), V MN-major from smem),
 //     so the tensor core computes S(j+1) while the softmax warps work on
-//     tile j; tcgen05.commit signals the mbarriers.
+//     tile j; S(j+2) reuses the columns of P(j) and so waits for P V(j);
+//     tcgen05.commit signals the mbarriers.
 //   warps 0-3 (softmax): thread r owns query row r = TMEM lane r: loads its
-//     S row (tcgen05.ld), masks, base-2 online softmax with lazy rescaling
-//     of O in TMEM (only when the running max grows by more than 2^8), writes
-//     P as bf16 pairs into the first 64 columns of its S buffer (tcgen05.st),
+//     S row in two halves (tcgen05.ld), masks, base-2 online softmax with
+//     lazy rescaling of O in TMEM (only when the running max grows by more
+//     than 2^8), packed f32x2 exponent arguments and row sums, writes P as
+//     bf16 pairs into the first 32 columns of its S buffer (tcgen05.st),
 //     and at the end normalises its O row and stores it.
 // Every mbarrier wait is bounded; on a timeout the CTA records the error,
 // drains its in-flight copies and MMAs, frees TMEM and exits.
@@ -75,8 +79,8 @@ struct PrefillSmem {
   uint64_t full_k[kKStages], k_empty[kKStages];
   uint64_t full_v[kVStages], v_empty[kVStages];
   uint64_t s_full[kSBufs];
-  uint64_t p_full[kSBufs];   // P(j) written into S buffer j % 3
-  uint64_t pv_done[kSBufs];  // PV(j) complete (S buffer j % 3 free again)
+  uint64_t p_full[kSBufs];   // P(j) written into S buffer j % 2
+  uint64_t pv_done[kSBufs];  // PV(j) complete (S buffer j % 2 free again)
   uint64_t fin;
   uint32_t tmem_base;
   volatile int abort;
@@ -241,8 +245,8 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) prefill_kernel(const __g
       const uint32_t q_addr = smem_u32(sm.q);
       bool ok = mbar_wait(&sm.bar_q, 0);
       if (!ok) flag_error(a, sm, kErrWaitTimeout);
-      // S(j) = Q K(j)^T into S buffer j % 3, once K(j) has landed and PV(j-3)
-      // has read P(j-3) out of that buffer.
+      // S(j) = Q K(j)^T into S buffer j % 2, once K(j) has landed and PV(j-2)
+      // has read P(j-2) out of that buffer.
       auto issue_s = [&](int j) -> bool {
         const int s = j % kSBufs, ks = j % kKStages;
         if (!mbar_wait(&sm.full_k[ks], (j / kKStages) & 1)) return false;
