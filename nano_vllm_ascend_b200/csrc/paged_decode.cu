@@ -18,10 +18,16 @@
 //    of the pair's ticket) fetches them while its own piece is computed and
 //    merges in registers; otherwise it publishes its piece (two partial
 //    slots per CTA, acq_rel ticket) and the last publisher merges.
-//  * warp 4 (producer): per segment a TMA load of the group's QPK query rows
-//    into a zero-padded 16-row operand; per tile, TMA loads of the K and V
-//    tile (box {64 dims, 1 head, <=32 tokens}, 128-byte swizzle, only the
-//    sub-boxes that hold context tokens) into a 3-stage ring.
+//  * warp 11 (scheduler): scans the context lengths into the schedule and
+//    walks the CTA's segments ahead of the producer: per segment a TMA load
+//    of the group's QPK query rows into a zero-padded 16-row operand, per
+//    chunk of tiles one parallel round of block-id loads into a ring, and
+//    (fused append) the step's new K/V row before any copy of its tile. The
+//    scan and the first chunk's ids come from step metadata and are done
+//    before griddepcontrol.wait.
+//  * warp 4 (producer): per tile, TMA loads of the K and V tile (box {64
+//    dims, 1 head, <=32 tokens}, 128-byte swizzle, only the sub-boxes that
+//    hold context tokens, L2 evict_first) into a 3-stage ring.
 //  * warps 5 and 10 (MMA issuers, one elected thread each): warp 5 issues
 //    S^T[128 tok x 16] = K[128 x 128] . Qpad^T (A and B K-major), warp 10
 //    O^T[128 dims x 16] += V^T . P^T (A = the V tile read MN-major, B = P^T
@@ -36,6 +42,10 @@
 //    max moves only when a tile max exceeds it by more than 2^8); the tile
 //    max is exchanged across the 4 warps once per tile; P^T goes to shared
 //    memory as bf16; l is summed once per segment.
+//  * warps 6-9 (epilogue): thread e owns dim e of O^T: per segment the
+//    normalised output row (to every rank's output over NVLink in gather
+//    mode), or the partial (numerator, max, denominator) of a split pair,
+//    published for the merge.
 // Every mbarrier wait is bounded (%globaltimer); a timeout sets the error
 // word, the CTA drains its copies and MMAs, frees TMEM and exits.
 #include <cfloat>
