@@ -41,7 +41,7 @@ def random_pool(num_blocks: int, block_size: int, kvh: int, d: int, device, seed
 def assert_close(got: np.ndarray, want: np.ndarray, what: str = "") -> tuple[float, float]:
     err = np.abs(got - want)
     max_abs = float(err.max()) if err.size else 0.0
-    bad = err > ATOL + RTOL * np.abs(want)
+    bad = ~(err <= ATOL + RTOL * np.abs(want))  # NaN (an unwritten output) counts as bad
     if bad.any():
         idx = np.argwhere(bad)[0]
         raise AssertionError(f"{what}: {int(bad.sum())} elements outside atol={ATOL} rtol={RTOL}; first at "
