@@ -6,17 +6,21 @@
   rows of other heads are never written;
 * two ranks on two GPUs (skipped with fewer GPUs): each rank holds half the KV
   heads of the same synthetic pool; after every call each rank's gathered
-  output equals the fp32 oracle over ALL heads.
+  output equals the fp32 oracle over ALL heads;
+* a peer that never posts its epoch (a flag nothing sets): the bounded wait
+  runs out, the call reports error bit 16 and the GPU stays usable.
 """
 
+import ctypes
 import os
 import socket
+import time
 
 import numpy as np
 import pytest
 import torch
 
-from nano_vllm_ascend_b200 import ops
+from nano_vllm_ascend_b200 import _lib, ops
 from nano_vllm_ascend_b200.peer_gather import PeerGather
 from oracle import paged_kv_oracle as orc
 from tests.helpers import assert_close, bits, seeded_tables
@@ -110,3 +114,40 @@ def test_gather_two_ranks_two_gpus():
     import torch.multiprocessing as mp
 
     mp.spawn(_two_rank_worker, args=(_free_port(), 2), nprocs=2, join=True)
+
+
+def test_gather_epoch_wait_runs_out_and_reports(cuda_device):
+    """world = 2 in one process, both "ranks'" output and signal areas local:
+    rank 1 never posts its epoch, so the last CTA's wait (bounded at 1 s)
+    gives up, sets bit 16 of the error word and returns. This rank's rows
+    still reached both output buffers, and a following launch works."""
+    dev = cuda_device
+    ctx = [100, 300, 1]
+    kc, vc, q, tables, want = full_problem(ctx, seed=5)
+    kc_d, vc_d, q_d, tables_d = kc.to(dev), vc.to(dev), q.to(dev), tables.to(dev)
+    ctx_t = torch.tensor(ctx, dtype=torch.int32, device=dev)
+    b = len(ctx)
+    ws = torch.zeros(ops.decode_workspace_bytes(b, H, KVH, D), dtype=torch.uint8, device=dev)
+    bufs = [torch.zeros(_lib.PEER_SIGNAL_BYTES + b * H * D * 2, dtype=torch.uint8, device=dev) for _ in range(2)]
+    pad = [0] * (_lib.MAX_PEERS - 2)
+    outs = (ctypes.c_void_p * _lib.MAX_PEERS)(*([t.data_ptr() + _lib.PEER_SIGNAL_BYTES for t in bufs] + pad))
+    sigs = (ctypes.c_void_p * _lib.MAX_PEERS)(*([t.data_ptr() for t in bufs] + pad))
+    stream = torch.cuda.current_stream(dev).cuda_stream
+    torch.cuda.synchronize()
+    t0 = time.time()
+    _lib.call("nvk_paged_decode_gather", q_d.data_ptr(), kc_d.data_ptr(), vc_d.data_ptr(), kc_d.shape[0], BS,
+              tables_d.data_ptr(), tables_d.stride(0), tables_d.shape[1], ctx_t.data_ptr(), b, H, KVH, D, SCALE, 0,
+              ws.data_ptr(), ws.numel(), outs, sigs, 2, 0, H, 0, None, None, 0, 0, None, stream)
+    torch.cuda.synchronize()
+    elapsed = time.time() - t0
+    assert ops.decode_error_word(ws) & 16, "the epoch wait must report its timeout"
+    assert 0.5 < elapsed < 20.0
+    for t in bufs:
+        got = t[_lib.PEER_SIGNAL_BYTES:].view(torch.bfloat16).view(b, H, D).float().cpu().numpy()
+        assert_close(got, want, "rows stored before the wait")
+    out = torch.empty_like(q_d)
+    ws2 = torch.zeros_like(ws)
+    ops.paged_decode(out, q_d, kc_d, vc_d, tables_d, ctx_t, SCALE, ws2)
+    torch.cuda.synchronize()
+    assert ops.decode_error_word(ws2) == 0
+    assert_close(out.float().cpu().numpy(), want, "launch after the timeout")
