@@ -116,11 +116,12 @@ class TinyDecoder:
         self.layers = layers
 
     def __call__(self, input_ids_flat, position_ids_flat, kv_cache, attn_metadata, is_prefill=False):
+        n = input_ids_flat.shape[0]  # the first n sequences (views: fixed addresses for each graph)
         outs = []
         for layer in range(self.layers):
-            kv_cache.write(layer, self.k[layer], self.v[layer], attn_metadata.slot_mapping)
+            kv_cache.write(layer, self.k[layer][:n], self.v[layer][:n], attn_metadata.slot_mapping)
             kc, vc = kv_cache.get_physical_cache(layer)
-            outs.append(self.attn(self.q[layer], kc, vc, attn_metadata.block_tables, attn_metadata.context_lens))
+            outs.append(self.attn(self.q[layer][:n], kc, vc, attn_metadata.block_tables, attn_metadata.context_lens))
         return SimpleNamespace(logits=torch.stack(outs))
 
 
@@ -173,3 +174,43 @@ def test_graph_runner_fused_appends_on_real_graphs(cuda_device):
     assert np.array_equal(k_f, k_u) and np.array_equal(v_f, v_u)
     for a, b in zip(o_f, o_u):
         assert torch.equal(a, b), "fused and unfused graphs must produce identical outputs"
+
+
+def test_graph_runner_capture_sizes(cuda_device):
+    """One runner serving the reference's capture sizes 1, 2, 4, 8, 16, 32
+    (acl_graph.py:110-250): a graph per exact batch size, captured on first
+    use, every replay equal to the oracle for its sequences."""
+    dev = cuda_device
+    sizes = [1, 2, 4, 8, 16, 32]
+    ctx = torch.randint(1, 900, (32,), generator=torch.Generator().manual_seed(21)).tolist()
+    layers, nb = 2, sum((c + 128) // 128 for c in ctx) + 8
+    bm = BlockManager(nb, 128, dev)
+    bm.free_block_ids = torch.randperm(nb, generator=torch.Generator().manual_seed(22)).tolist()
+    seqs = list(range(32))
+    bm.prepare_prefill_metadata(seqs, ctx, [0] * 32, [[] for _ in seqs])
+    kv = PagedKVCache(layers, nb, 128, 8, D, torch.bfloat16, dev)
+    g = torch.Generator(device=dev).manual_seed(23)
+    kv.key_cache.copy_(torch.randn(kv.key_cache.shape, generator=g, device=dev).to(torch.bfloat16))
+    kv.value_cache.copy_(torch.randn(kv.value_cache.shape, generator=g, device=dev).to(torch.bfloat16))
+    pool0 = (bits(kv.key_cache).copy(), bits(kv.value_cache).copy())
+    model = TinyDecoder(layers, 32, 16, 8, dev, seed=24)
+    runner = DecodeGraphRunner(model, kv, batch_sizes=sizes, max_model_len=4096, block_size=128, device=dev)
+    try:
+        for bs in sizes:
+            md = bm.prepare_decode_metadata(seqs[:bs], ctx[:bs], q_len=1)
+            ids = torch.zeros(bs, dtype=torch.long, device=dev)
+            pos = torch.tensor(ctx[:bs], dtype=torch.long, device=dev)
+            logits = runner.forward(ids, pos, md)
+            assert logits is not None, f"batch size {bs} fell back"
+            torch.cuda.synchronize()
+            kc, vc = pool0[0].copy(), pool0[1].copy()
+            slots = md.slot_mapping.cpu().numpy()
+            for layer in range(layers):
+                orc.kv_append(kc[layer], vc[layer], bits(model.k[layer][:bs]), bits(model.v[layer][:bs]), slots)
+                want = orc.paged_decode(bits(model.q[layer][:bs]), kc[layer], vc[layer], md.block_tables.cpu().numpy(),
+                                        md.context_lens.numpy(), SCALE)
+                assert_close(logits[layer].float().cpu().numpy(), want, f"bs={bs} layer {layer}")
+        stats = runner.stats_dict()
+        assert stats["captures"] == len(sizes) and stats["replays"] == len(sizes) and stats["fallbacks"] == 0
+    finally:
+        runner.release()
