@@ -1,7 +1,8 @@
 #!/usr/bin/env python
 """Benchmark of the B200 paged-KV decode hot path.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload decode_c2|decode_c4]
+    python bench.py [--gpus N] [--steps K] [--warmup W]
+                    [--workload decode_c2|decode_c4|decode_c5|prefill_c3|kernels]
                     [--impl ours|reference]
 
 A "step" is one decode step of the configured batch through every layer:
@@ -19,6 +20,10 @@ Workloads (seeded synthetic inputs with the configs' shapes; no model weights):
       its own pool (sequence-sharded replicas, no collective): weak scaling.
   decode_c4: 256 sequences, context ~ U[2048, 6144], split evenly across
       ranks by sequence (strong scaling).
+  prefill_c3: config[2]: 32 requests sharing a hash-hit 768-token prefix
+      (6 cached blocks in the real BlockManager) prefill their 256 new tokens
+      each: per layer the 8192-row append and prefix-aware causal attention
+      over 1024 keys; value = attention TF/s of the step.
   kernels: the path's other kernels timed one by one under CUDA graphs on
       config-sized inputs (prefill-sized append, decode- and prefill-sized
       q/k norm + RoPE + append, device decode metadata, LM head + greedy
@@ -35,7 +40,8 @@ Workloads (seeded synthetic inputs with the configs' shapes; no model weights):
 Printed (rank 0, one JSON line): value = KV bytes read by decode attention
 per step, summed over ranks, / max-over-ranks step time (GB/s); tok/s; the
 dominant kernel's roofline (decode attention timed alone with CUDA events on
-its stream); the prefill-sized append GB/s; an end-to-end figure through the
+its stream, as one launch per layer captured in a CUDA graph); the
+prefill-sized append GB/s; an end-to-end figure through the
 public API with pinned host inputs and a device->host read of the outputs;
 SM clocks sampled by nvidia-smi during the measurement; the CPU baseline
 (eager torch-CPU expression of the reference path on a bounded sample).
