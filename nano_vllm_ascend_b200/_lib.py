@@ -134,10 +134,13 @@ def load() -> ctypes.CDLL:
 
 def call(name: str, *args) -> None:
     """Calls ``name`` and raises NvkError (a RuntimeError) on a non-zero status."""
-    lib = load()
-    rc = getattr(lib, name)(*args)
+    check(name, getattr(load(), name)(*args))
+
+
+def check(name: str, rc: int) -> None:
+    """Raises for the status ``rc`` that entry point ``name`` returned, as ``call`` does."""
     if rc != NVK_OK:
-        msg = lib.nvk_last_error().decode(errors="replace")
+        msg = load().nvk_last_error().decode(errors="replace")
         if rc in (NVK_ERR_INVALID_ARGUMENT, NVK_ERR_UNSUPPORTED):
             raise ValueError(f"{name}: {msg}")
         raise NvkError(name, rc, msg)

@@ -15,11 +15,14 @@ tensor (as the CUDA-graph path wants it).
 
 from __future__ import annotations
 
+import numpy as np
 import torch
 
 from . import _lib
 from .block_manager import PagedKVCacheMetadata
-from .ops import _ptr, _stream
+
+
+_STAGING_BUFFERS = 4  # pinned host staging buffers used round robin
 
 
 class DeviceBlockTables:
@@ -28,26 +31,33 @@ class DeviceBlockTables:
         self.device = torch.device(device if device is not None else block_manager.device)
         self.mirror = torch.zeros(max_slots, max_blocks_per_seq, dtype=torch.int32, device=self.device)
         # slot -> (the table list last sent, entries of it already on the device); holding the list
-        # keeps its identity from being reused by a new table of a re-initialised slot
+        # keeps its identity from being reused by a new table of a re-initialised slot. A missing
+        # entry only means "send the whole table", so dropping entries is always safe.
         self._synced: dict[int, tuple[list[int], int]] = {}
         self.error_word = torch.zeros(1, dtype=torch.int32, device=self.device)
-
-    def _updates(self, slots: list[int]) -> tuple[list[int], list[int], list[int]]:
-        offsets, idx, blk = [0], [], []
-        for slot in slots:
-            table = self.bm.block_tables[slot]
-            sent, done = self._synced.get(slot, (None, 0))
-            if sent is not table:
-                done = 0
-            idx.extend(range(done, len(table)))
-            blk.extend(table[done:])
-            offsets.append(len(idx))
-            self._synced[slot] = (table, len(table))
-        return offsets, idx, blk
+        # pinned int64 staging buffers; each one's event marks the end of the copy that last read it
+        self._staging = [(torch.empty(0, dtype=torch.int64), np.empty(0, dtype=np.int64))] * _STAGING_BUFFERS
+        self._events = [torch.cuda.Event() for _ in range(_STAGING_BUFFERS)]
+        self._next = 0
+        self._fn = _lib.load().nvk_decode_metadata
 
     def forget(self, slot: int) -> None:
         """Drops what was sent for ``slot`` (optional: a new table is detected anyway)."""
         self._synced.pop(slot, None)
+
+    def _staging_buffer(self, words: int) -> tuple[torch.Tensor, np.ndarray, torch.cuda.Event]:
+        """A pinned int64 buffer of at least ``words`` words whose previous copy has finished,
+        and the event to record after the next copy from it."""
+        i = self._next
+        self._next = (i + 1) % _STAGING_BUFFERS
+        event = self._events[i]
+        event.synchronize()  # returns at once for an event never recorded
+        host, view = self._staging[i]
+        if view.shape[0] < words:
+            host = torch.empty(max(words, 2 * view.shape[0], 1024), dtype=torch.int64, pin_memory=True)
+            view = host.numpy()
+            self._staging[i] = (host, view)
+        return host, view, event
 
     def prepare_decode_metadata(self, slots: list[int], start_positions: list[int], q_len: int,
                                 width: int | None = None) -> PagedKVCacheMetadata:
@@ -60,34 +70,68 @@ class DeviceBlockTables:
         if len(slots) != len(start_positions):
             raise ValueError("slots and start_positions length mismatch")
         bm = self.bm
-        for slot, start in zip(slots, start_positions):
-            end = start + q_len
-            bm.ensure_blocks(slot, end)
-            bm.seq_lens[slot] = max(bm.seq_lens[slot], end)
+        bs = bm.block_size
+        tables, seq_lens, synced = bm.block_tables, bm.seq_lens, self._synced
         rows, cols = self.mirror.shape
-        for slot in slots:
-            if not 0 <= slot < rows or len(bm.block_tables[slot]) > cols:
-                raise ValueError(f"sequence slot {slot} (table of {len(bm.block_tables[slot])} blocks) outside the "
+        # the allocator's bookkeeping (ensure_blocks, seq_lens) and the update lists, in one pass;
+        # ``synced`` is marked as it goes, so any error empties it (nothing was sent this step and
+        # the next step sends whole tables)
+        offsets, idx, blk = [0], [], []
+        widest, bad = 0, None
+        try:
+            for slot, start in zip(slots, start_positions):
+                end = start + q_len
+                table = tables[slot]
+                if len(table) * bs < end:
+                    bm.ensure_blocks(slot, end)
+                if seq_lens[slot] < end:
+                    seq_lens[slot] = end
+                n = len(table)
+                if n > widest:
+                    widest = n
+                if not 0 <= slot < rows or n > cols:
+                    if bad is None:
+                        bad = slot
+                    continue
+                sent = synced.get(slot)
+                done = sent[1] if sent is not None and sent[0] is table else 0
+                if done < n:
+                    idx.extend(range(done, n))
+                    blk.extend(table[done:])
+                offsets.append(len(idx))
+                synced[slot] = (table, n)
+            if bad is not None:
+                raise ValueError(f"sequence slot {bad} (table of {len(tables[bad])} blocks) outside the "
                                  f"device mirror [{rows}, {cols}]")
-        offsets, idx, blk = self._updates(slots)
-        b = len(slots)
-        width = width or max(len(bm.block_tables[s]) for s in slots)
-        # one packed copy: int32 [slots | offsets | idx | blk], then int64 starts
-        n32 = b + (b + 1) + 2 * len(idx)
-        n32_pad = (n32 + 1) // 2 * 2
-        host = torch.empty(n32_pad // 2 + b, dtype=torch.int64)
-        h32 = host[: n32_pad // 2].view(torch.int32)
-        h32[:n32] = torch.tensor(list(slots) + offsets + idx + blk, dtype=torch.int32)
-        host[n32_pad // 2:] = torch.tensor(list(start_positions), dtype=torch.int64)
-        dev = host.to(self.device)
-        d32 = dev[: n32_pad // 2].view(torch.int32)
-        d_slots, d_off = d32[:b], d32[b: 2 * b + 1]
-        d_idx, d_blk = d32[2 * b + 1: 2 * b + 1 + len(idx)], d32[2 * b + 1 + len(idx): n32]
-        d_start = dev[n32_pad // 2:]
-        tables = torch.empty(b, width, dtype=torch.int32, device=self.device)
-        ctx = torch.empty(b, dtype=torch.int32, device=self.device)
-        slot_mapping = torch.empty(b * q_len, dtype=torch.int64, device=self.device)
-        _lib.call("nvk_decode_metadata", _ptr(self.mirror), cols, rows, _ptr(d_slots), _ptr(d_start), b, q_len,
-                  bm.block_size, _ptr(d_off), _ptr(d_idx), _ptr(d_blk), _ptr(tables), width, width, _ptr(ctx),
-                  _ptr(slot_mapping), _ptr(self.error_word), _stream(self.device))
-        return PagedKVCacheMetadata(block_tables=tables, context_lens=ctx, slot_mapping=slot_mapping)
+        except BaseException:
+            synced.clear()
+            raise
+        b, m = len(slots), len(idx)
+        width = width or widest
+        # device buffer, int64 words: staged inputs int32 [slots | offsets | idx | blk] (even length)
+        # and int64 starts; then the outputs: int32 tables [b, width], int32 context lens, int64 slots
+        n32 = 2 * b + 1 + 2 * m
+        w_in32 = (n32 + 1) // 2
+        w_in = w_in32 + b
+        w_tab = (b * width + 1) // 2
+        w_ctx = (b + 1) // 2
+        host, view, event = self._staging_buffer(w_in)
+        view.view(np.int32)[:n32] = list(slots) + offsets + idx + blk
+        view[w_in32:w_in] = start_positions
+        stream = torch.cuda.current_stream(self.device)
+        buf = torch.empty(w_in + w_tab + w_ctx + b * q_len, dtype=torch.int64, device=self.device)
+        buf[:w_in].copy_(host[:w_in], non_blocking=True)
+        event.record(stream)
+        out32 = buf[w_in:w_in + w_tab + w_ctx].view(torch.int32)
+        block_tables = out32[:b * width].view(b, width)
+        context_lens = out32[2 * w_tab:2 * w_tab + b]
+        slot_mapping = buf[w_in + w_tab + w_ctx:]
+        base = buf.data_ptr()
+        p_off = base + 4 * b
+        p_idx = p_off + 4 * (b + 1)
+        p_tab = base + 8 * w_in
+        _lib.check("nvk_decode_metadata", self._fn(
+            self.mirror.data_ptr(), cols, rows, base, base + 8 * w_in32, b, q_len, bs, p_off, p_idx,
+            p_idx + 4 * m, p_tab, width, width, p_tab + 8 * w_tab, p_tab + 8 * (w_tab + w_ctx),
+            self.error_word.data_ptr(), stream.cuda_stream))
+        return PagedKVCacheMetadata(block_tables=block_tables, context_lens=context_lens, slot_mapping=slot_mapping)

@@ -69,3 +69,50 @@ def test_device_decode_metadata_padded_width(cuda_device):
     t = md.block_tables.cpu()
     assert t.shape == (2, 32) and int(t[0, 3:].abs().sum()) == 0 and int(t[1, 1:].abs().sum()) == 0
     assert t[0, :3].tolist() == bm.block_tables[0] and t[1, :1].tolist() == bm.block_tables[1]
+
+
+def test_device_decode_metadata_back_to_back_steps_without_sync(cuda_device):
+    """Twelve steps queued with no synchronisation in between (more than the
+    pinned staging buffers, so each is reused while earlier copies may be in
+    flight); every step's tensors still hold that step's metadata."""
+    bs = 16
+    host_bm, dev_bm = BlockManager(512, bs, "cpu"), BlockManager(512, bs, cuda_device)
+    ctx = [5, 17, 31, 16, 1, 47, 64, 3]
+    slots = list(range(len(ctx)))
+    for bm in (host_bm, dev_bm):
+        bm.prepare_prefill_metadata(slots, ctx, [0] * len(ctx), [[] for _ in slots])
+    dt = DeviceBlockTables(dev_bm, 16, 64, cuda_device)
+    wants, gots = [], []
+    for step in range(12):
+        starts = [c + step for c in ctx]
+        wants.append(host_bm.prepare_decode_metadata(slots, starts, 1))
+        gots.append(dt.prepare_decode_metadata(slots, starts, 1, width=16))
+    torch.cuda.synchronize()
+    for step, (want, got) in enumerate(zip(wants, gots)):
+        w = want.block_tables.cpu()
+        assert torch.equal(got.block_tables.cpu()[:, : w.shape[1]], w), step
+        assert int(got.block_tables.cpu()[:, w.shape[1]:].abs().sum()) == 0, step
+        assert torch.equal(got.context_lens.cpu(), want.context_lens.cpu()), step
+        assert torch.equal(got.slot_mapping.cpu(), want.slot_mapping.cpu()), step
+
+
+def test_device_decode_metadata_rejected_step_then_recovers(cuda_device):
+    """A slot outside the mirror raises ValueError before any device work; the
+    steps after it still match the host path (whole tables are re-sent)."""
+    bs = 16
+    host_bm, dev_bm = BlockManager(64, bs, "cpu"), BlockManager(64, bs, cuda_device)
+    for bm in (host_bm, dev_bm):
+        bm.prepare_prefill_metadata([0, 1, 5], [40, 5, 3], [0, 0, 0], [[], [], []])
+    dt = DeviceBlockTables(dev_bm, 4, 32, cuda_device)
+    dt.prepare_decode_metadata([0, 1], [40, 5], 1)
+    host_bm.prepare_decode_metadata([0, 1], [40, 5], 1)
+    with pytest.raises(ValueError, match="outside the device mirror"):
+        dt.prepare_decode_metadata([0, 5], [41, 3], 1)
+    host_bm.prepare_decode_metadata([0, 5], [41, 3], 1)  # the same allocator bookkeeping
+    want = host_bm.prepare_decode_metadata([1, 0], [6, 48], 1)
+    got = dt.prepare_decode_metadata([1, 0], [6, 48], 1)
+    torch.cuda.synchronize()
+    assert torch.equal(got.block_tables.cpu(), want.block_tables.cpu())
+    assert torch.equal(got.context_lens.cpu(), want.context_lens.cpu())
+    assert torch.equal(got.slot_mapping.cpu(), want.slot_mapping.cpu())
+    assert int(dt.error_word.item()) == 0
