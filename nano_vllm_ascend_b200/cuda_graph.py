@@ -55,11 +55,11 @@ class DecodeGraphEntry:
     workspace: torch.Tensor | None = None
 
     def copy_inputs(self, input_ids: torch.Tensor, position_ids: torch.Tensor, attn_metadata) -> None:
-        self.input_ids.copy_(input_ids)
-        self.position_ids.copy_(position_ids)
+        copy_in(self.input_ids, input_ids)
+        copy_in(self.position_ids, position_ids)
         copy_block_tables(self.block_tables, attn_metadata.block_tables)
-        self.context_lens.copy_(attn_metadata.context_lens)
-        self.slot_mapping.copy_(attn_metadata.slot_mapping)
+        copy_in(self.context_lens, attn_metadata.context_lens)
+        copy_in(self.slot_mapping, attn_metadata.slot_mapping)
 
     def decode_workspace(self, attn) -> torch.Tensor:
         """This entry's decode workspace, sized and zeroed by the eager warm-up
@@ -259,4 +259,19 @@ def copy_block_tables(target: torch.Tensor, source: torch.Tensor) -> None:
             f"decode graph block table width {target_shape[1]} is smaller than runtime width {source_shape[1]}"
         )
     target.zero_()
-    target[:, : source_shape[1]].copy_(source)
+    copy_in(target[:, : source_shape[1]], source)
+
+
+def copy_in(target: torch.Tensor, source: torch.Tensor) -> None:
+    """``target.copy_(source)`` without blocking the host. A host ``source`` bound
+    for a CUDA ``target`` (``context_lens`` from the host BlockManager, for one)
+    is first copied into a fresh pinned buffer, so the caller may change its
+    tensor at once, and crosses asynchronously on the current stream; torch's
+    pinned allocator keeps that buffer until the copy has run. A plain blocking
+    copy would drain the stream before every replay."""
+    if getattr(target, "is_cuda", False) and isinstance(source, torch.Tensor) and not source.is_cuda:
+        staged = torch.empty(source.shape, dtype=source.dtype, pin_memory=True)
+        staged.copy_(source)
+        target.copy_(staged, non_blocking=True)
+    else:
+        target.copy_(source)

@@ -214,3 +214,35 @@ def test_graph_runner_capture_sizes(cuda_device):
         assert stats["captures"] == len(sizes) and stats["replays"] == len(sizes) and stats["fallbacks"] == 0
     finally:
         runner.release()
+
+
+def test_graph_runner_host_context_lens_overwritten_after_forward(cuda_device):
+    """context_lens from the host (pinned, as a serving loop may keep it):
+    forward() queues its copy without blocking the host, and the caller may
+    overwrite its tensor as soon as forward() returns. A spin kernel queued
+    first keeps the copy from running before the overwrite."""
+    dev = cuda_device
+    ctx = [700, 3, 1200, 129]
+    bm, md, kv, model, runner = build_runner(dev, True, ctx, layers=2)
+    pool0 = (bits(kv.key_cache).copy(), bits(kv.value_cache).copy())
+    want_ctx = md.context_lens.clone()
+    host_ctx = md.context_lens.to(torch.int32).pin_memory()
+    step_md = type(md)(block_tables=md.block_tables, context_lens=host_ctx, slot_mapping=md.slot_mapping)
+    ids = torch.zeros(len(ctx), dtype=torch.long, device=dev)
+    pos = torch.tensor(ctx, dtype=torch.long, device=dev)
+    try:
+        assert runner.forward(ids, pos, step_md) is not None  # capture + first replay
+        torch.cuda.synchronize()
+        torch.cuda._sleep(20_000_000)
+        logits = runner.forward(ids, pos, step_md)
+        host_ctx.fill_(1)
+        torch.cuda.synchronize()
+        kc, vc = pool0[0].copy(), pool0[1].copy()
+        slots = md.slot_mapping.cpu().numpy()
+        for layer in range(2):
+            orc.kv_append(kc[layer], vc[layer], bits(model.k[layer]), bits(model.v[layer]), slots)
+            want = orc.paged_decode(bits(model.q[layer]), kc[layer], vc[layer], md.block_tables.cpu().numpy(),
+                                    want_ctx.numpy(), SCALE)
+            assert_close(logits[layer].float().cpu().numpy(), want, f"layer {layer}")
+    finally:
+        runner.release()
