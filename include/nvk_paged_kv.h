@@ -77,7 +77,8 @@ NVK_API const char* nvk_last_error(void);
 
 /* ABI version, bumped on any signature change (2: persistent decode, num_ctas;
    3: KV-head-sharded decode with in-kernel gather, peer buffers, fused append,
-   device-side decode metadata). */
+   device-side decode metadata; 4: per-row lengths and table sizes for
+   nvk_decode_metadata). */
 NVK_API int nvk_abi_version(void);
 
 /*
@@ -239,16 +240,22 @@ NVK_API int nvk_qk_norm_rope_append(const void* query, const void* key, const vo
  * by this call: sequence b first gets its new entries
  * table_mirror[seq_slots[b]][update_idx[u]] = update_block[u] for u in
  * [update_offsets[b], update_offsets[b+1]), then
- *   block_tables[b][j] = j < ceil(end_b / block_size) ? table[j] : 0  (j < block_table_width)
- *   context_lens[b]    = end_b = start_positions[b] + q_len
+ *   block_tables[b][j] = j < n_b ? table[j] : 0  (j < block_table_width)
+ *   context_lens[b]    = ctx_b
  *   slot_mapping[b * q_len + t] = table[p / block_size] * block_size + p % block_size,
  *                        p = start_positions[b] + t
- * bit-exact with the host path. All arrays are device memory. A sequence
- * whose table would not fit (or a bad slot) gets a zero row, length 0, slots
- * -1, and bit 8 in error_word (may be NULL).
+ * where ctx_b = row_context_lens[b] and n_b = row_blocks[b] (the host path's
+ * seq_lens[slot] after this step and its whole table length, which is what
+ * it returns when a slot is named twice or decoded behind its length), or,
+ * when those pointers are NULL, ctx_b = start_positions[b] + q_len and
+ * n_b = ceil(ctx_b / block_size). Bit-exact with the host path. All arrays
+ * are device memory. A sequence whose table would not fit, whose table does
+ * not cover its new tokens, or with a bad slot gets a zero row, length 0,
+ * slots -1, and bit 8 in error_word (may be NULL).
  */
 NVK_API int nvk_decode_metadata(int32_t* table_mirror, int mirror_stride, int mirror_rows, const int32_t* seq_slots,
-                                const int64_t* start_positions, int batch, int q_len, int block_size,
+                                const int64_t* start_positions, const int32_t* row_context_lens,
+                                const int32_t* row_blocks, int batch, int q_len, int block_size,
                                 const int32_t* update_offsets, const int32_t* update_idx,
                                 const int32_t* update_block, int32_t* block_tables, int block_table_stride,
                                 int block_table_width, int32_t* context_lens, int64_t* slot_mapping, int* error_word,

@@ -62,8 +62,8 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     ),
     "nvk_decode_metadata": (
         _i32,
-        [_c_void_p, _i32, _i32, _c_void_p, _c_void_p, _i32, _i32, _i32, _c_void_p, _c_void_p, _c_void_p, _c_void_p,
-         _i32, _i32, _c_void_p, _c_void_p, _c_void_p, _c_void_p],
+        [_c_void_p, _i32, _i32, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _i32, _i32, _i32, _c_void_p, _c_void_p,
+         _c_void_p, _c_void_p, _i32, _i32, _c_void_p, _c_void_p, _c_void_p, _c_void_p],
     ),
     "nvk_lm_head_argmax_workspace_size": (_i32, [_i32, ctypes.POINTER(_size_t)]),
     "nvk_lm_head_argmax": (

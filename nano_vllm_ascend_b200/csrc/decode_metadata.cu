@@ -22,7 +22,8 @@ constexpr int kRowsPerBlock = 8;  // one warp per sequence
 
 __global__ void __launch_bounds__(kRowsPerBlock * 32) decode_metadata_kernel(
     int32_t* __restrict__ mirror, int mirror_stride, int mirror_rows, const int32_t* __restrict__ seq_slots,
-    const int64_t* __restrict__ start_positions, int batch, int q_len, int block_size,
+    const int64_t* __restrict__ start_positions, const int32_t* __restrict__ row_context_lens,
+    const int32_t* __restrict__ row_blocks, int batch, int q_len, int block_size,
     const int32_t* __restrict__ update_offsets, const int32_t* __restrict__ update_idx,
     const int32_t* __restrict__ update_block, int32_t* __restrict__ tables_out, int out_stride, int out_width,
     int32_t* __restrict__ context_lens_out, int64_t* __restrict__ slot_mapping_out, int* __restrict__ error_word) {
@@ -36,8 +37,12 @@ __global__ void __launch_bounds__(kRowsPerBlock * 32) decode_metadata_kernel(
   const int row = seq_slots[b];
   const int64_t start = start_positions[b];
   const int64_t end = start + q_len;
-  const int64_t nblk = (end + block_size - 1) / block_size;
-  if (row < 0 || row >= mirror_rows || start < 0 || nblk > mirror_stride || nblk > out_width) {
+  // the host path's length and table size for this slot (they exceed end when the slot is named
+  // twice in the batch or decoded behind its length), else what this step's tokens need
+  const int64_t ctx = row_context_lens ? row_context_lens[b] : end;
+  const int64_t nblk = row_blocks ? row_blocks[b] : (end + block_size - 1) / block_size;
+  if (row < 0 || row >= mirror_rows || start < 0 || ctx < end || nblk * block_size < end || nblk > mirror_stride ||
+      nblk > out_width) {
     if (lane == 0 && error_word) atomicOr(error_word, kErrContextTooLong);
     for (int j = lane; j < out_width; j += 32) tables_out[static_cast<int64_t>(b) * out_stride + j] = 0;
     if (lane == 0) context_lens_out[b] = 0;
@@ -55,7 +60,7 @@ __global__ void __launch_bounds__(kRowsPerBlock * 32) decode_metadata_kernel(
   int32_t* trow = tables_out + static_cast<int64_t>(b) * out_stride;
   for (int j = lane; j < out_width; j += 32) trow[j] = j < nblk ? mrow[j] : 0;
   // 3. context length (includes the appended tokens) and their slots
-  if (lane == 0) context_lens_out[b] = static_cast<int32_t>(end);
+  if (lane == 0) context_lens_out[b] = static_cast<int32_t>(ctx);
   for (int t = lane; t < q_len; t += 32) {
     const int64_t pos = start + t;
     slot_mapping_out[static_cast<int64_t>(b) * q_len + t] =
@@ -67,7 +72,8 @@ __global__ void __launch_bounds__(kRowsPerBlock * 32) decode_metadata_kernel(
 }  // namespace nvk
 
 extern "C" int nvk_decode_metadata(int32_t* table_mirror, int mirror_stride, int mirror_rows,
-                                   const int32_t* seq_slots, const int64_t* start_positions, int batch, int q_len,
+                                   const int32_t* seq_slots, const int64_t* start_positions,
+                                   const int32_t* row_context_lens, const int32_t* row_blocks, int batch, int q_len,
                                    int block_size, const int32_t* update_offsets, const int32_t* update_idx,
                                    const int32_t* update_block, int32_t* block_tables, int block_table_stride,
                                    int block_table_width, int32_t* context_lens, int64_t* slot_mapping,
@@ -85,7 +91,8 @@ extern "C" int nvk_decode_metadata(int32_t* table_mirror, int mirror_stride, int
   const int grid = (batch + kRowsPerBlock - 1) / kRowsPerBlock;
   const cudaError_t e =
       launch_pdl(decode_metadata_kernel, dim3(grid), dim3(kRowsPerBlock * 32), 0, reinterpret_cast<cudaStream_t>(stream),
-                 table_mirror, mirror_stride, mirror_rows, seq_slots, start_positions, batch, q_len, block_size,
+                 table_mirror, mirror_stride, mirror_rows, seq_slots, start_positions, row_context_lens, row_blocks,
+                 batch, q_len, block_size,
                  update_offsets, update_idx, update_block, block_tables, block_table_stride, block_table_width,
                  context_lens, slot_mapping, error_word);
   return check_cuda(e, "decode_metadata launch");

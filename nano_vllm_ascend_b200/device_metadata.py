@@ -31,8 +31,7 @@ class DeviceBlockTables:
         self.device = torch.device(device if device is not None else block_manager.device)
         self.mirror = torch.zeros(max_slots, max_blocks_per_seq, dtype=torch.int32, device=self.device)
         # slot -> (the table list last sent, entries of it already on the device); holding the list
-        # keeps its identity from being reused by a new table of a re-initialised slot. A missing
-        # entry only means "send the whole table", so dropping entries is always safe.
+        # keeps its identity from being reused by a new table of a re-initialised slot
         self._synced: dict[int, tuple[list[int], int]] = {}
         self.error_word = torch.zeros(1, dtype=torch.int32, device=self.device)
         # pinned int64 staging buffers; each one's event marks the end of the copy that last read it
@@ -73,50 +72,66 @@ class DeviceBlockTables:
         bs = bm.block_size
         tables, seq_lens, synced = bm.block_tables, bm.seq_lens, self._synced
         rows, cols = self.mirror.shape
-        # the allocator's bookkeeping (ensure_blocks, seq_lens) and the update lists, in one pass;
-        # ``synced`` is marked as it goes, so any error empties it (nothing was sent this step and
-        # the next step sends whole tables)
-        offsets, idx, blk = [0], [], []
-        widest, bad = 0, None
-        try:
-            for slot, start in zip(slots, start_positions):
-                end = start + q_len
+        # the allocator's bookkeeping (ensure_blocks, seq_lens) and the update lists, in one pass.
+        # What is sent is recorded only after the launch, so an error leaves the record as it was.
+        # Each row carries the host path's context length (seq_lens[slot] after the pass) and
+        # table size; a slot named twice gets its final ones, and the same updates, in both rows.
+        offsets, idx, blk, ctxs, ns = [0], [], [], [], []
+        widest, bad, twice = 0, None, False
+        sending = {}
+        for slot, start in zip(slots, start_positions):
+            end = start + q_len
+            table = tables[slot]
+            if len(table) * bs < end:
+                bm.ensure_blocks(slot, end)
+            ctx = seq_lens[slot]
+            if ctx < end:
+                seq_lens[slot] = ctx = end
+            n = len(table)
+            if n > widest:
+                widest = n
+            if not 0 <= slot < rows or n > cols:
+                if bad is None:
+                    bad = slot
+                continue
+            if slot in sending:
+                twice = True
+            sent = synced.get(slot)
+            done = sent[1] if sent is not None and sent[0] is table else 0
+            if done < n:
+                idx.extend(range(done, n))
+                blk.extend(table[done:])
+            offsets.append(len(idx))
+            ctxs.append(ctx)
+            ns.append(n)
+            sending[slot] = (table, n)
+        if bad is not None:
+            raise ValueError(f"sequence slot {bad} (table of {len(tables[bad])} blocks) outside the "
+                             f"device mirror [{rows}, {cols}]")
+        if twice:
+            offsets, idx, blk, ctxs, ns = [0], [], [], [], []
+            for slot in slots:
                 table = tables[slot]
-                if len(table) * bs < end:
-                    bm.ensure_blocks(slot, end)
-                if seq_lens[slot] < end:
-                    seq_lens[slot] = end
                 n = len(table)
-                if n > widest:
-                    widest = n
-                if not 0 <= slot < rows or n > cols:
-                    if bad is None:
-                        bad = slot
-                    continue
                 sent = synced.get(slot)
                 done = sent[1] if sent is not None and sent[0] is table else 0
-                if done < n:
-                    idx.extend(range(done, n))
-                    blk.extend(table[done:])
+                idx.extend(range(done, n))
+                blk.extend(table[done:])
                 offsets.append(len(idx))
-                synced[slot] = (table, n)
-            if bad is not None:
-                raise ValueError(f"sequence slot {bad} (table of {len(tables[bad])} blocks) outside the "
-                                 f"device mirror [{rows}, {cols}]")
-        except BaseException:
-            synced.clear()
-            raise
+                ctxs.append(seq_lens[slot])
+                ns.append(n)
         b, m = len(slots), len(idx)
         width = width or widest
-        # device buffer, int64 words: staged inputs int32 [slots | offsets | idx | blk] (even length)
-        # and int64 starts; then the outputs: int32 tables [b, width], int32 context lens, int64 slots
-        n32 = 2 * b + 1 + 2 * m
+        # device buffer, int64 words: staged inputs int32 [slots | offsets | idx | blk | ctxs | ns]
+        # (even length) and int64 starts; then the outputs: int32 tables [b, width], int32 context
+        # lengths, int64 slots
+        n32 = 4 * b + 1 + 2 * m
         w_in32 = (n32 + 1) // 2
         w_in = w_in32 + b
         w_tab = (b * width + 1) // 2
         w_ctx = (b + 1) // 2
         host, view, event = self._staging_buffer(w_in)
-        view.view(np.int32)[:n32] = list(slots) + offsets + idx + blk
+        view.view(np.int32)[:n32] = list(slots) + offsets + idx + blk + ctxs + ns
         view[w_in32:w_in] = start_positions
         stream = torch.cuda.current_stream(self.device)
         buf = torch.empty(w_in + w_tab + w_ctx + b * q_len, dtype=torch.int64, device=self.device)
@@ -129,9 +144,11 @@ class DeviceBlockTables:
         base = buf.data_ptr()
         p_off = base + 4 * b
         p_idx = p_off + 4 * (b + 1)
+        p_ctx = p_idx + 8 * m
         p_tab = base + 8 * w_in
         _lib.check("nvk_decode_metadata", self._fn(
-            self.mirror.data_ptr(), cols, rows, base, base + 8 * w_in32, b, q_len, bs, p_off, p_idx,
-            p_idx + 4 * m, p_tab, width, width, p_tab + 8 * w_tab, p_tab + 8 * (w_tab + w_ctx),
+            self.mirror.data_ptr(), cols, rows, base, base + 8 * w_in32, p_ctx, p_ctx + 4 * b, b, q_len, bs,
+            p_off, p_idx, p_idx + 4 * m, p_tab, width, width, p_tab + 8 * w_tab, p_tab + 8 * (w_tab + w_ctx),
             self.error_word.data_ptr(), stream.cuda_stream))
+        synced.update(sending)  # after the launch: a refused launch leaves the record as it was
         return PagedKVCacheMetadata(block_tables=block_tables, context_lens=context_lens, slot_mapping=slot_mapping)

@@ -46,7 +46,7 @@ def test_library_exports_every_declared_symbol():
 
 def test_version_and_error_string():
     lib = _lib.load()
-    assert lib.nvk_abi_version() == 3
+    assert lib.nvk_abi_version() == 4
     assert isinstance(lib.nvk_last_error(), bytes)
 
 

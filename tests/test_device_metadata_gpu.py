@@ -116,3 +116,66 @@ def test_device_decode_metadata_rejected_step_then_recovers(cuda_device):
     assert torch.equal(got.context_lens.cpu(), want.context_lens.cpu())
     assert torch.equal(got.slot_mapping.cpu(), want.slot_mapping.cpu())
     assert int(dt.error_word.item()) == 0
+
+
+def test_device_decode_metadata_slot_named_twice(cuda_device):
+    """A batch that names a sequence slot twice (with new table entries to
+    send) gives both rows the host path's values: the slot's final length and
+    whole table (BlockManager.prepare_decode_metadata runs every row's
+    ensure_blocks and seq_lens update before building any tensor)."""
+    bs = 16
+    host_bm, dev_bm = BlockManager(64, bs, "cpu"), BlockManager(64, bs, cuda_device)
+    for bm in (host_bm, dev_bm):
+        bm.prepare_prefill_metadata([0, 1], [31, 5], [0, 0], [[], []])
+    dt = DeviceBlockTables(dev_bm, 4, 32, cuda_device)
+    for starts in ([31, 32, 5], [47, 48, 6]):  # the first step sends whole tables, the second a new block
+        want = host_bm.prepare_decode_metadata([0, 0, 1], starts, 1)
+        got = dt.prepare_decode_metadata([0, 0, 1], starts, 1)
+        torch.cuda.synchronize()
+        assert torch.equal(got.block_tables.cpu(), want.block_tables.cpu())
+        assert torch.equal(got.context_lens.cpu(), want.context_lens.cpu())
+        assert torch.equal(got.slot_mapping.cpu(), want.slot_mapping.cpu())
+    assert int(dt.error_word.item()) == 0
+
+
+def test_device_decode_metadata_rewinds_and_repeats_over_a_seeded_script(cuda_device):
+    """The seeded script again, now also with rows decoded behind their
+    sequence's length (the host path then reports seq_lens, not start + q_len)
+    and slots named twice in a batch."""
+    rnd = random.Random(11)
+    bs, nb = 16, 4000
+    host_bm, dev_bm = BlockManager(nb, bs, "cpu"), BlockManager(nb, bs, cuda_device)
+    perm = list(range(nb))
+    rnd.shuffle(perm)
+    host_bm.free_block_ids = perm
+    dev_bm.free_block_ids = perm
+    dt = DeviceBlockTables(dev_bm, max_slots=32, max_blocks_per_seq=128, device=cuda_device)
+    pos: dict[int, int] = {}
+    for step in range(200):
+        free_slots = [s for s in range(32) if s not in pos]
+        if (rnd.random() < 0.15 or not pos) and free_slots:
+            slot = rnd.choice(free_slots)
+            n = rnd.randint(1, 200)
+            for bm in (host_bm, dev_bm):
+                bm.prepare_prefill_metadata([slot], [n], [0], [[]])
+            pos[slot] = n
+            continue
+        q_len = 2 if rnd.random() < 0.2 else 1
+        slots = rnd.sample(list(pos), rnd.randint(1, len(pos)))
+        starts = [pos[s] for s in slots]
+        if rnd.random() < 0.3:
+            j = rnd.randrange(len(slots))
+            slots.append(slots[j])
+            starts.append(starts[j] + q_len)
+        if rnd.random() < 0.3:
+            j = rnd.randrange(len(slots))
+            starts[j] = max(0, starts[j] - rnd.randint(1, 40))
+        want = host_bm.prepare_decode_metadata(slots, starts, q_len)
+        got = dt.prepare_decode_metadata(slots, starts, q_len)
+        torch.cuda.synchronize()
+        assert np.array_equal(got.block_tables.cpu().numpy(), want.block_tables.cpu().numpy()), step
+        assert np.array_equal(got.context_lens.cpu().numpy(), want.context_lens.numpy()), step
+        assert np.array_equal(got.slot_mapping.cpu().numpy(), want.slot_mapping.cpu().numpy()), step
+        for s, st in zip(slots, starts):
+            pos[s] = max(pos[s], st + q_len)
+    assert int(dt.error_word.item()) == 0
