@@ -11,7 +11,10 @@
 // entries added since the last step (block ids appended by ensure_blocks, or a
 // whole table for a new sequence) as per-sequence update lists; the warp of a
 // sequence applies its updates to the mirror, then writes that sequence's
-// outputs. Integer work, one warp per sequence.
+// outputs. The host may also pass each row's context length and table size
+// (the host path's seq_lens[slot] and whole table, which differ from
+// start + q_len when a slot is named twice or decoded behind its length).
+// Integer work, one warp per sequence.
 #include "host_common.h"
 #include "nvk_common.cuh"
 
