@@ -161,22 +161,40 @@ NVK_API int nvk_paged_decode_append(void* out, const void* query, void* key_cach
  * all device buffers, a cgo/JNI/N-API binding with no device allocator, a
  * serving thread that must not take cudaMalloc's implicit synchronisation).
  *
- * Same arguments and results as nvk_paged_decode. The scratch is a
- * fixed 16 MiB array in the library's device memory, present on every GPU
- * that loads the library until the process exits; a call whose scratch need
- * (nvk_paged_decode_workspace_size) exceeds 16 MiB returns
- * NVK_ERR_UNSUPPORTED. It calls no allocator. The first call on each device
- * resolves the array's device address (cudaGetSymbolAddress) and caches it;
- * make that first call before any stream capture begins on the device. Every
- * call clears the scratch's error word and counters on `stream` and then uses
- * the same array, so calls whose execution overlaps on the GPU (different
- * streams, or different host threads) race: order them on one stream.
+ * Same arguments and outputs as nvk_paged_decode minus the workspace. The
+ * scratch is a fixed 16 MiB array in the library's device memory, present on
+ * every GPU that loads the library until the process exits; a call whose
+ * scratch need (nvk_paged_decode_workspace_size) exceeds 16 MiB returns
+ * NVK_ERR_UNSUPPORTED, after the same argument checks as nvk_paged_decode.
+ * It calls no allocator. The first call in each CUDA context (the device's
+ * primary context, or one a host framework made current) resolves the array's
+ * device address there (cudaGetSymbolAddress) and caches it under the
+ * context's unique id, so a context created later (after cudaDeviceReset, for
+ * one) resolves it afresh; make that first call before any stream capture
+ * begins in the context. Every call clears the scratch's error word and
+ * counters on `stream` and then uses the same array, so calls whose execution
+ * overlaps on the GPU (different streams, or different host threads) race:
+ * order them on one stream.
+ *
+ * The kernel's error word (bits as for nvk_paged_decode: 1 wait timeout, 2
+ * block id outside the pool, 8 context longer than the table) lives in the
+ * scratch, and the next call clears it: read it with
+ * nvk_paged_decode_noalloc_error before the next call.
  */
 NVK_API int nvk_paged_decode_noalloc(void* out, const void* query, const void* key_cache, const void* value_cache,
                                      int num_blocks, int block_size, const int32_t* block_tables,
                                      int block_table_stride, int max_blocks_per_seq, const int32_t* context_lens,
                                      int batch, int num_heads, int num_kv_heads, int head_dim, float scale,
                                      int num_ctas, nvk_stream_t stream);
+
+/*
+ * Device error word of the last nvk_paged_decode_noalloc call ordered before
+ * this one on `stream`, copied to *error_word (host memory). Waits for
+ * `stream`, so it must not be called while the stream is capturing (returns
+ * NVK_ERR_INVALID_ARGUMENT). Allocates nothing. No counterpart in the
+ * reference (the Ascend operator reports bad input by raising).
+ */
+NVK_API int nvk_paged_decode_noalloc_error(int* error_word, nvk_stream_t stream);
 
 /*
  * Paged causal prefill attention (prefix-cache aware). Sequence b owns query

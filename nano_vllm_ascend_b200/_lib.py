@@ -45,6 +45,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _i32, _i32, _c_void_p, _i32, _i32, _c_void_p, _i32, _i32, _i32,
          _i32, _f32, _i32, _c_void_p],
     ),
+    "nvk_paged_decode_noalloc_error": (_i32, [ctypes.POINTER(_i32), _c_void_p]),
     "nvk_paged_prefill": (
         _i32,
         [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _i32, _i32, _c_void_p, _i32, _c_void_p, _c_void_p, _i32, _i32,

@@ -144,4 +144,4 @@ int ensure_dynamic_smem(const void* kernel, size_t bytes) {
 
 extern "C" const char* nvk_last_error(void) { return nvk::g_last_error; }
 
-extern "C" int nvk_abi_version(void) { return 4; }
+extern "C" int nvk_abi_version(void) { return 5; }

@@ -1221,11 +1221,11 @@ struct GatherTargets {
   int world, rank, out_heads, head_offset;
 };
 
-int decode_impl(void* out, const void* query, const void* key_cache, const void* value_cache, int num_blocks,
-                int block_size, const int32_t* block_tables, int block_table_stride, int max_blocks_per_seq,
-                const int32_t* context_lens, int batch, int num_heads, int num_kv_heads, int head_dim, float scale,
-                int num_ctas, void* workspace, size_t workspace_bytes, const GatherTargets* gt, const AppendRows* ap,
-                nvk_stream_t stream) {
+// Every host-side argument check of a decode call except the workspace's.
+int decode_check_args(const void* out, const void* query, const void* key_cache, const void* value_cache,
+                      int num_blocks, int block_size, const int32_t* block_tables, int block_table_stride,
+                      int max_blocks_per_seq, const int32_t* context_lens, int batch, int num_heads,
+                      int num_kv_heads, int head_dim, int num_ctas, const GatherTargets* gt, const AppendRows* ap) {
   if (batch < 0 || num_blocks <= 0 || num_heads <= 0 || num_kv_heads <= 0 || num_ctas < 0)
     return fail(NVK_ERR_INVALID_ARGUMENT, "paged_decode: bad sizes (batch=%d blocks=%d heads=%d kv_heads=%d ctas=%d)",
                 batch, num_blocks, num_heads, num_kv_heads, num_ctas);
@@ -1255,8 +1255,21 @@ int decode_impl(void* out, const void* query, const void* key_cache, const void*
                   "paged_decode_append: new rows null, misaligned or strides (%lld, %lld) below a row / not 16-byte",
                   (long long)ap->key_stride, (long long)ap->value_stride);
   }
+  return NVK_OK;
+}
+
+int decode_impl(void* out, const void* query, const void* key_cache, const void* value_cache, int num_blocks,
+                int block_size, const int32_t* block_tables, int block_table_stride, int max_blocks_per_seq,
+                const int32_t* context_lens, int batch, int num_heads, int num_kv_heads, int head_dim, float scale,
+                int num_ctas, void* workspace, size_t workspace_bytes, const GatherTargets* gt, const AppendRows* ap,
+                nvk_stream_t stream) {
+  int rc = decode_check_args(out, query, key_cache, value_cache, num_blocks, block_size, block_tables,
+                             block_table_stride, max_blocks_per_seq, context_lens, batch, num_heads, num_kv_heads,
+                             head_dim, num_ctas, gt, ap);
+  if (rc != NVK_OK || batch == 0) return rc;
+  const int qpk = num_heads / num_kv_heads;
   int ctas = 0;
-  int rc = resolve_ctas(num_ctas, &ctas);
+  rc = resolve_ctas(num_ctas, &ctas);
   if (rc != NVK_OK) return rc;
   const WsLayout wl = ws_layout(batch, num_heads, num_kv_heads, ctas);
   if (!workspace || workspace_bytes < wl.total || !aligned16(workspace))
@@ -1417,25 +1430,67 @@ static __device__ __align__(256) uint8_t g_noalloc_decode_scratch[kNoAllocScratc
 
 namespace {
 
-// Device address of the scratch array on the current device. The symbol's
-// host-side name is only a handle: the address is fetched with
-// cudaGetSymbolAddress once per device (with that device current) and cached.
-int noalloc_scratch(void** out) {
-  static std::mutex mu;
-  static void* addr[kNoAllocMaxDevices] = {};
-  int dev = 0;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess) return nvk::check_cuda(e, "paged_decode_noalloc: cudaGetDevice");
-  if (dev < 0 || dev >= kNoAllocMaxDevices)
-    return nvk::fail(NVK_ERR_UNSUPPORTED, "paged_decode_noalloc: device %d above %d", dev, kNoAllocMaxDevices);
-  std::lock_guard<std::mutex> lock(mu);
-  if (addr[dev] == nullptr) {
+using CtxGetCurrentFn = CUresult (*)(CUcontext*);
+using CtxGetIdFn = CUresult (*)(CUcontext, unsigned long long*);
+
+// Unique id of the CUDA context current on this thread (0 if none). Ids are
+// never reused within a process, so a context created after a device reset,
+// or a second context a plugin host made current on the same device, gets a
+// fresh one. The driver functions are resolved through the runtime, like
+// cuTensorMapEncodeTiled, so the library does not link libcuda.
+unsigned long long current_context_id() {
+  static CtxGetCurrentFn get_current = nullptr;
+  static CtxGetIdFn get_id = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
     void* p = nullptr;
-    e = cudaGetSymbolAddress(&p, g_noalloc_decode_scratch);
-    if (e != cudaSuccess) return nvk::check_cuda(e, "paged_decode_noalloc: cudaGetSymbolAddress");
-    addr[dev] = p;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_current = reinterpret_cast<CtxGetCurrentFn>(p);
+    p = nullptr;
+    if (cudaGetDriverEntryPoint("cuCtxGetId", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_id = reinterpret_cast<CtxGetIdFn>(p);
+  });
+  CUcontext ctx = nullptr;
+  unsigned long long id = 0;
+  if (!get_current || !get_id || get_current(&ctx) != CUDA_SUCCESS || ctx == nullptr) return 0;
+  if (get_id(ctx, &id) != CUDA_SUCCESS) return 0;
+  return id;
+}
+
+// Device address of the scratch array in the current context. The symbol's
+// host-side name is only a handle: the address is fetched with
+// cudaGetSymbolAddress once per CUDA context (the first call on a device does
+// it, with that device current) and cached under the context's id.
+int noalloc_scratch(void** out) {
+  struct Entry {
+    unsigned long long ctx_id;
+    void* addr;
+  };
+  static std::mutex mu;
+  static Entry cache[kNoAllocMaxDevices] = {};
+  static int next = 0;
+  std::lock_guard<std::mutex> lock(mu);
+  unsigned long long id = current_context_id();
+  if (id != 0) {
+    for (const Entry& e : cache)
+      if (e.ctx_id == id) {
+        *out = e.addr;
+        return NVK_OK;
+      }
   }
-  *out = addr[dev];
+  void* p = nullptr;
+  // With no context current yet this call also initialises the device's primary context.
+  cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_decode_scratch);
+  if (e != cudaSuccess) return nvk::check_cuda(e, "paged_decode_noalloc: cudaGetSymbolAddress");
+  if (id == 0) id = current_context_id();
+  if (id != 0) {
+    cache[next] = Entry{id, p};
+    next = (next + 1) % kNoAllocMaxDevices;
+  }
+  *out = p;
   return NVK_OK;
 }
 
@@ -1447,32 +1502,51 @@ extern "C" int nvk_paged_decode_noalloc(void* out, const void* query, const void
                                         const int32_t* context_lens, int batch, int num_heads, int num_kv_heads,
                                         int head_dim, float scale, int num_ctas, nvk_stream_t stream) {
   using namespace nvk;
-  size_t header = 0;
-  const bool sane = batch > 0 && num_heads > 0 && num_kv_heads > 0 && num_heads % num_kv_heads == 0 &&
-                    num_ctas >= 0 && head_dim == kD;
-  if (sane) {
-    int ctas = 0;
-    const int rc = resolve_ctas(num_ctas, &ctas);
-    if (rc != NVK_OK) return rc;
-    const WsLayout wl = ws_layout(batch, num_heads, num_kv_heads, ctas);
-    header = wl.ml_off;  // error word + arrival tickets
-    if (wl.total > kNoAllocScratchBytes)
-      return fail(NVK_ERR_UNSUPPORTED,
-                  "paged_decode_noalloc: %zu bytes of split-K scratch needed, the static scratch holds %zu "
-                  "(a smaller batch, or nvk_paged_decode with a caller workspace)",
-                  wl.total, kNoAllocScratchBytes);
-  }
-  void* scratch = nullptr;
-  int rc = noalloc_scratch(&scratch);
+  // Arguments first, so that a call refused for them queues nothing on the stream.
+  int rc = decode_check_args(out, query, key_cache, value_cache, num_blocks, block_size, block_tables,
+                             block_table_stride, max_blocks_per_seq, context_lens, batch, num_heads, num_kv_heads,
+                             head_dim, num_ctas, nullptr, nullptr);
+  if (rc != NVK_OK || batch == 0) return rc;
+  int ctas = 0;
+  rc = resolve_ctas(num_ctas, &ctas);
   if (rc != NVK_OK) return rc;
-  if (sane) {
-    // The array keeps the previous call's contents: clear the error word and
-    // the arrival tickets, which must start at zero.
-    rc = check_cuda(cudaMemsetAsync(scratch, 0, header, reinterpret_cast<cudaStream_t>(stream)),
-                    "paged_decode_noalloc: clear scratch header");
-    if (rc != NVK_OK) return rc;
-  }
+  const WsLayout wl = ws_layout(batch, num_heads, num_kv_heads, ctas);
+  if (wl.total > kNoAllocScratchBytes)
+    return fail(NVK_ERR_UNSUPPORTED,
+                "paged_decode_noalloc: %zu bytes of split-K scratch needed, the static scratch holds %zu "
+                "(a smaller batch, or nvk_paged_decode with a caller workspace)",
+                wl.total, kNoAllocScratchBytes);
+  void* scratch = nullptr;
+  rc = noalloc_scratch(&scratch);
+  if (rc != NVK_OK) return rc;
+  // The array keeps the previous call's contents: clear the error word and
+  // the arrival tickets, which must start at zero.
+  rc = check_cuda(cudaMemsetAsync(scratch, 0, wl.ml_off, reinterpret_cast<cudaStream_t>(stream)),
+                  "paged_decode_noalloc: clear scratch header");
+  if (rc != NVK_OK) return rc;
   return nvk_paged_decode(out, query, key_cache, value_cache, num_blocks, block_size, block_tables,
                           block_table_stride, max_blocks_per_seq, context_lens, batch, num_heads, num_kv_heads,
                           head_dim, scale, num_ctas, scratch, kNoAllocScratchBytes, stream);
+}
+
+extern "C" int nvk_paged_decode_noalloc_error(int* error_word, nvk_stream_t stream) {
+  using namespace nvk;
+  if (!error_word) return fail(NVK_ERR_INVALID_ARGUMENT, "paged_decode_noalloc_error: null output pointer");
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+  int rc = check_cuda(cudaStreamIsCapturing(st, &cap), "paged_decode_noalloc_error: capture status");
+  if (rc != NVK_OK) return rc;
+  if (cap != cudaStreamCaptureStatusNone)
+    return fail(NVK_ERR_INVALID_ARGUMENT, "paged_decode_noalloc_error: the stream is capturing (this call waits)");
+  void* scratch = nullptr;
+  rc = noalloc_scratch(&scratch);
+  if (rc != NVK_OK) return rc;
+  int word = 0;
+  rc = check_cuda(cudaMemcpyAsync(&word, scratch, sizeof(int), cudaMemcpyDeviceToHost, st),
+                  "paged_decode_noalloc_error: copy");
+  if (rc != NVK_OK) return rc;
+  rc = check_cuda(cudaStreamSynchronize(st), "paged_decode_noalloc_error: synchronize");
+  if (rc != NVK_OK) return rc;
+  *error_word = word;
+  return NVK_OK;
 }

@@ -46,7 +46,7 @@ def test_library_exports_every_declared_symbol():
 
 def test_version_and_error_string():
     lib = _lib.load()
-    assert lib.nvk_abi_version() == 4
+    assert lib.nvk_abi_version() == 5
     assert isinstance(lib.nvk_last_error(), bytes)
 
 
@@ -72,6 +72,12 @@ def test_host_side_validation_codes():
     # batch 0 is a no-op
     rc = lib.nvk_paged_decode(n, n, n, n, 8, 128, n, 4, 4, n, 0, 16, 8, 128, 0.1, 0, n, 0, n)
     assert rc == _lib.NVK_OK
+    # the no-alloc entry point runs the same checks first, before its scratch-size check
+    rc = lib.nvk_paged_decode_noalloc(n, n, n, n, 8, 128, n, 4, 4, n, 1 << 20, 16, 8, 128, 0.1, 0, n)
+    assert rc == _lib.NVK_ERR_INVALID_ARGUMENT and b"null pointer" in lib.nvk_last_error()
+    rc = lib.nvk_paged_decode_noalloc(n, n, n, n, 8, 128, n, 4, 4, n, 2, 24, 8, 128, 0.1, 0, n)
+    assert rc == _lib.NVK_ERR_UNSUPPORTED and b"GQA" in lib.nvk_last_error()
+    assert lib.nvk_paged_decode_noalloc_error(None, n) == _lib.NVK_ERR_INVALID_ARGUMENT
     # append: row not a multiple of 16 bytes, zero tokens is a no-op
     rc = lib.nvk_kv_append(n, n, 3, 3, n, n, n, 1, 8, 1, 3, n, n)
     assert rc == _lib.NVK_ERR_UNSUPPORTED

@@ -6,28 +6,43 @@ buffer, a cgo/JNI/N-API binding with no device allocator, a serving thread
 that must not take cudaMalloc's implicit synchronisation -- by keeping the
 split-K scratch in a fixed array of the library's device memory.
 
-Checks, through the C ABI: two calls in a row (the second reuses the array
-the first left behind, with a different split count and different inputs)
-each match the workspace entry point nvk_paged_decode within the attention
-tolerance of the other tests; a shape whose scratch need exceeds the array is
-refused on the host with NVK_ERR_UNSUPPORTED. This file sorts last so that a
-stop-at-first-failure run has already run every other test.
+Checks, through the C ABI:
+* two calls in a row (the second reuses the array the first left behind, with
+  a different split count and different inputs) each match the workspace
+  entry point nvk_paged_decode within the attention tolerance of the other
+  tests, and the fp32 oracle;
+* the calls leave the device's free memory unchanged (nothing is allocated);
+* a call with a block id outside the pool reports bit 2 through
+  nvk_paged_decode_noalloc_error, and the good call after it (which starts
+  from the scratch the bad one left) reports 0 and matches nvk_paged_decode;
+* a shape whose scratch need exceeds the array is refused on the host with
+  NVK_ERR_UNSUPPORTED, after the ordinary argument checks.
+This file sorts last so that a stop-at-first-failure run has already run
+every other test.
 """
 
 import ctypes
+
+import numpy as np
 import pytest
 import torch
 
 from nano_vllm_ascend_b200 import _lib, ops
-from tests.helpers import assert_close, random_pool, seeded_tables
+from oracle import paged_kv_oracle as orc
+from tests.helpers import assert_close, bits, random_pool, seeded_tables
 
 pytestmark = pytest.mark.gpu
 
 SCRATCH_BYTES = 16 << 20
+SCALE = 128 ** -0.5
 
 
 def _p(t):
     return ctypes.c_void_p(t.data_ptr())
+
+
+def _stream(device):
+    return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
 
 
 def _inputs(device, ctx, seed, h=16, kvh=8, bs=128):
@@ -44,9 +59,25 @@ def _inputs(device, ctx, seed, h=16, kvh=8, bs=128):
 def _noalloc(lib, out, q, kc, vc, tables, ctx_t, num_ctas):
     b, h, d = q.shape
     nb, bs, kvh, _ = kc.shape
-    stream = ctypes.c_void_p(torch.cuda.current_stream(q.device).cuda_stream)
     return lib.nvk_paged_decode_noalloc(_p(out), _p(q), _p(kc), _p(vc), nb, bs, _p(tables), tables.stride(0),
-                                        tables.shape[1], _p(ctx_t), b, h, kvh, d, 128 ** -0.5, num_ctas, stream)
+                                        tables.shape[1], _p(ctx_t), b, h, kvh, d, SCALE, num_ctas,
+                                        _stream(q.device))
+
+
+def _noalloc_error(lib, device) -> int:
+    word = ctypes.c_int(-1)
+    rc = lib.nvk_paged_decode_noalloc_error(ctypes.byref(word), _stream(device))
+    assert rc == _lib.NVK_OK, lib.nvk_last_error()
+    return word.value
+
+
+def _workspace_decode(q, kc, vc, tables, ctx_t, num_ctas):
+    ws = torch.zeros(ops.decode_workspace_bytes(q.shape[0], q.shape[1], kc.shape[2], 128, num_ctas),
+                     dtype=torch.uint8, device=q.device)
+    want = torch.empty_like(q)
+    ops.paged_decode(want, q, kc, vc, tables, ctx_t, SCALE, ws, num_ctas)
+    torch.cuda.synchronize()
+    return want, ops.decode_error_word(ws)
 
 
 def test_noalloc_decode_matches_workspace_decode_on_two_calls(cuda_device):
@@ -56,34 +87,57 @@ def test_noalloc_decode_matches_workspace_decode_on_two_calls(cuda_device):
     prepared = []
     for ctx, seed, num_ctas in cases:
         q, kc, vc, tables, ctx_t = _inputs(cuda_device, ctx, seed)
-        ws = torch.zeros(ops.decode_workspace_bytes(len(ctx), 16, 8, 128, num_ctas), dtype=torch.uint8,
-                         device=cuda_device)
-        want = torch.empty_like(q)
-        ops.paged_decode(want, q, kc, vc, tables, ctx_t, 128 ** -0.5, ws, num_ctas)
-        torch.cuda.synchronize()
-        assert ops.decode_error_word(ws) == 0
+        want, err = _workspace_decode(q, kc, vc, tables, ctx_t, num_ctas)
+        assert err == 0
         prepared.append((q, kc, vc, tables, ctx_t, num_ctas, want))
+    outs = [torch.full_like(p[0], float("nan")) for p in prepared]
+    torch.cuda.synchronize()
+    free_before = torch.cuda.mem_get_info(cuda_device)[0]
     # two calls in a row on one stream: the second reuses the scratch the first left behind
-    outs = []
-    for q, kc, vc, tables, ctx_t, num_ctas, _ in prepared:
-        got = torch.full_like(q, float("nan"))
+    for got, (q, kc, vc, tables, ctx_t, num_ctas, _) in zip(outs, prepared):
         rc = _noalloc(lib, got, q, kc, vc, tables, ctx_t, num_ctas)
         assert rc == _lib.NVK_OK, lib.nvk_last_error()
-        outs.append(got)
     torch.cuda.synchronize()
+    assert torch.cuda.mem_get_info(cuda_device)[0] == free_before, "the no-alloc calls changed free device memory"
+    assert _noalloc_error(lib, cuda_device) == 0
     for i, (got, prep) in enumerate(zip(outs, prepared)):
-        want = prep[-1]
+        q, kc, vc, tables, ctx_t, _, want = prep
         assert not torch.isnan(got.float()).any()
         assert_close(got.float().cpu().numpy(), want.float().cpu().numpy(), f"noalloc call {i + 1} vs workspace")
+        ref = orc.paged_decode(bits(q), bits(kc), bits(vc), tables.cpu().numpy(), ctx_t.cpu().numpy(), SCALE)
+        assert_close(got.float().cpu().numpy(), ref, f"noalloc call {i + 1} vs oracle")
+
+
+def test_noalloc_decode_reports_a_bad_block_id_then_recovers(cuda_device):
+    lib = _lib.load()
+    ctx = [700, 130, 2048]
+    q, kc, vc, tables, ctx_t = _inputs(cuda_device, ctx, 7)
+    bad_tables = tables.clone()
+    bad_tables[1, 1] = kc.shape[0] + 3  # outside the pool: zero-filled and flagged, never read
+    got = torch.empty_like(q)
+    assert _noalloc(lib, got, q, kc, vc, bad_tables, ctx_t, 0) == _lib.NVK_OK, lib.nvk_last_error()
+    assert _noalloc_error(lib, cuda_device) & 2, "bad block id not reported"
+    # the next call starts from the scratch the flagged call left behind
+    got = torch.full_like(q, float("nan"))
+    assert _noalloc(lib, got, q, kc, vc, tables, ctx_t, 0) == _lib.NVK_OK, lib.nvk_last_error()
+    assert _noalloc_error(lib, cuda_device) == 0
+    want, err = _workspace_decode(q, kc, vc, tables, ctx_t, 0)
+    assert err == 0
+    assert_close(got.float().cpu().numpy(), want.float().cpu().numpy(), "call after a flagged call")
 
 
 def test_noalloc_decode_refuses_shapes_beyond_its_scratch(cuda_device):
     lib = _lib.load()
-    # one arrival ticket per (sequence, KV head): 1M sequences x 8 heads x 4 B > 16 MiB
-    need = ops.decode_workspace_bytes(1 << 20, 16, 8, 128)
+    # one arrival ticket per (sequence, KV head): 1M sequences x 8 heads x 128 B > 16 MiB
+    batch = 1 << 20
+    need = ops.decode_workspace_bytes(batch, 16, 8, 128)
     assert need > SCRATCH_BYTES
-    n = ctypes.c_void_p(0)
-    rc = lib.nvk_paged_decode_noalloc(n, n, n, n, 8, 128, n, 64, 64, n, 1 << 20, 16, 8, 128, 0.1, 0,
-                                      ctypes.c_void_p(torch.cuda.current_stream(cuda_device).cuda_stream))
+    q = torch.empty(1, 16, 128, dtype=torch.bfloat16, device=cuda_device)
+    kc = torch.empty(8, 128, 8, 128, dtype=torch.bfloat16, device=cuda_device)
+    tables = torch.zeros(1, 64, dtype=torch.int32, device=cuda_device)
+    ctx_t = torch.zeros(1, dtype=torch.int32, device=cuda_device)
+    # the pointers are never dereferenced: the size check refuses the call before any launch
+    rc = lib.nvk_paged_decode_noalloc(_p(q), _p(q), _p(kc), _p(kc), 8, 128, _p(tables), 64, 64, _p(ctx_t), batch,
+                                      16, 8, 128, SCALE, 0, _stream(cuda_device))
     assert rc == _lib.NVK_ERR_UNSUPPORTED
     assert b"static scratch" in lib.nvk_last_error()
