@@ -6,9 +6,18 @@ src/nanovllm_ascend/layers/npu_paged_attention.py:14-100).
 new [tokens, num_heads, head_dim] tensor like the reference. ``context_lens``
 may be the reference's CPU int32 tensor (it is copied to the device) or a
 device tensor (the CUDA-graph path). Inside PagedKVCache.deferred_appends()
-(the CUDA-graph decode runner) the layer's append is fused into the kernel. Inside a decode-graph capture the
-workspace comes from the capturing graph entry, mirroring the per-task
-workspace of src/nanovllm_ascend/npu/acl_graph.py:229-242.
+(the CUDA-graph decode runner) the layer's append is fused into the kernel.
+While DecodeGraphRunner records a batch size, the split-K workspace is that
+graph's own (cuda_graph.graph_workspace), as the reference gives each
+captured task its workspace (src/nanovllm_ascend/npu/acl_graph.py:229-242).
+
+Bad metadata raises like the reference: a CPU ``context_lens`` longer than
+its block-table row raises ``RuntimeError("missing block ...")`` before the
+launch (block_manager.py:194-205); what only the device can see (a block id
+outside the pool, a device ``context_lens`` too long, a fused-append slot
+that is not the sequence's last position) is reported through the decode
+workspace's error word and raised by ``device_errors`` on a following call
+or by ``device_errors.check_errors()``.
 """
 
 from __future__ import annotations
@@ -16,8 +25,8 @@ from __future__ import annotations
 import torch
 from torch import nn
 
-from . import ops
-from .cuda_graph import PagedAttentionGraphTask, current_decode_graph_entry, record_paged_attention_task
+from . import device_errors, ops
+from .cuda_graph import graph_workspace
 from .paged_kv_cache import take_deferred
 
 _NUM_SMS: dict[int, int] = {}
@@ -73,27 +82,34 @@ class PagedAttention(nn.Module):
         if total_tokens == 0:
             return output
         device = q.device
-        entry = current_decode_graph_entry()
+        if not context_lens.is_cuda and context_lens.numel() and block_tables.dim() == 2:
+            longest = int(context_lens.max())
+            if longest > block_tables.shape[1] * key_cache.shape[1]:
+                raise RuntimeError(f"missing block: context length {longest} exceeds the "
+                                   f"{block_tables.shape[1]}-block table")
         with torch.cuda.device(device):
-            if entry is not None:
-                workspace = entry.decode_workspace(self)
+            errors = device_errors.state(device)
+            errors.raise_if_flagged()
+            workspace = graph_workspace(self, total_tokens)
+            if workspace is not None:
+                word = None  # the graph runner reads its slot's word after each replay
             else:
                 workspace = shared_workspace(device, self.workspace_bytes(total_tokens))
+                word = errors.watch("paged decode", workspace)
             ctx = context_lens if context_lens.is_cuda else context_lens.to(device=device, dtype=torch.int32)
             tables = block_tables if block_tables.is_cuda else block_tables.to(device)
             # This layer's append, when PagedKVCache.deferred_appends() held it
             # back, is done by the decode kernel itself.
             pending = take_deferred(key_cache)
             if pending is not None and pending[0].shape[0] != total_tokens:
-                ops.kv_append(key_cache, value_cache, *pending)  # not one row per sequence: plain append first
+                # not one row per sequence: plain append first
+                ops.kv_append(key_cache, value_cache, *pending, error_word=errors.word)
+                errors.launched()
                 pending = None
             new_key, new_value, slots = pending if pending is not None else (None, None, None)
             ops.paged_decode(output, q.contiguous(), key_cache, value_cache, tables.to(torch.int32),
                              ctx.to(torch.int32), self.scale, workspace, self.num_ctas, new_key=new_key,
                              new_value=new_value, slot_mapping=slots)
-        if entry is not None:
-            record_paged_attention_task(PagedAttentionGraphTask(
-                query=q, key_cache=key_cache, value_cache=value_cache, num_kv_heads=self.num_key_value_heads,
-                num_heads=self.num_heads, scale=self.scale, block_tables=block_tables, context_lens=context_lens,
-                output=output, workspace=workspace))
+            if word is not None:
+                errors.launched(word)
         return output

@@ -14,6 +14,12 @@ Both are bottom-right-aligned causal (the reference's ``sparse_mode=3``):
 query i of a sequence with q_len Lq and kv_len Lk sees key j iff
 j <= Lk - Lq + i. There is no mask tensor; the reference's 2048x2048 int8
 mask (:23-29) only existed for the Ascend op.
+
+A paged-mode ``context_lens`` longer than its block-table row raises
+``RuntimeError("missing block ...")`` before the launch (block_manager.py:194-205);
+a block id outside the pool is reported through the device's error word and
+raised by ``device_errors`` on a following call or by
+``device_errors.check_errors()``.
 """
 
 from __future__ import annotations
@@ -21,7 +27,7 @@ from __future__ import annotations
 import torch
 from torch import nn
 
-from . import ops
+from . import device_errors, ops
 
 
 def _cu(values: list[int], device: torch.device) -> torch.Tensor:
@@ -74,12 +80,21 @@ class BatchPrefillAttention(nn.Module):
                 pass
         _, cu_q, cu_kv, ctx, tables = cache
         with torch.cuda.device(device):
+            errors = device_errors.state(device)
+            errors.raise_if_flagged()
             if attn_metadata.use_paged_prefill:
                 if key_cache is None or value_cache is None:
                     raise ValueError("paged prefill requires physical key/value cache")
+                lens = attn_metadata.context_lens
+                if not getattr(lens, "is_cuda", True) and lens.numel():
+                    longest = int(lens.max())
+                    if longest > tables.shape[1] * key_cache.shape[1]:
+                        raise RuntimeError(f"missing block: context length {longest} exceeds the "
+                                           f"{tables.shape[1]}-block table")
                 ops.paged_prefill(out, query, key_cache, value_cache, tables, cu_q, ctx, max_prompt_len,
-                                  self.scale)
+                                  self.scale, error_word=errors.word)
             else:
                 ops.dense_prefill(out, query, k.contiguous(), v.contiguous(), cu_q, cu_kv, max_prompt_len,
-                                  self.scale)
+                                  self.scale, error_word=errors.word)
+            errors.launched()
         return out.view(total_tokens, self.num_heads, self.head_dim)

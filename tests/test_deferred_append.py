@@ -1,22 +1,36 @@
 """Host logic of the fused decode append, on CPU (the kernels are replaced by
 recorders): PagedKVCache.deferred_appends() holds each layer's rows back
 instead of launching the append, PagedAttention takes them (take_deferred)
-by the layer's key view, rows nobody took are appended when the block exits,
-a second write of a layer lands the first, and DecodeGraphRunner runs the
-model inside the block only when fuse_appends is on."""
+by the layer's key view -- owned by (cache, layer), so two caches never
+mix -- rows nobody took are appended when the block exits and the exit
+raises, a second write of a layer lands the first, and DecodeGraphRunner runs
+the model inside the block only when fuse_appends is on."""
 
+import pytest
 import torch
 
 import nano_vllm_ascend_b200.paged_kv_cache as pkc
 from nano_vllm_ascend_b200 import PagedKVCacheMetadata
-from nano_vllm_ascend_b200.cuda_graph import PagedAttentionGraphTask, record_paged_attention_task
-from tests.test_graph_runner import FakeRunner
+from nano_vllm_ascend_b200.cuda_graph import DecodeGraphRunner, graph_workspace
+from tests.test_graph_runner import FakeAttention, FakeBackend
+
+
+class NoErrors:
+    word = None
+
+    def raise_if_flagged(self):
+        pass
+
+    def launched(self, *names):
+        pass
 
 
 def make_cache(monkeypatch, layers=3):
     calls = []
-    monkeypatch.setattr(pkc.ops, "kv_append", lambda kc, vc, k, v, slots: calls.append((kc.data_ptr(), k, slots)))
+    monkeypatch.setattr(pkc.ops, "kv_append",
+                        lambda kc, vc, k, v, slots, error_word=None: calls.append((kc.data_ptr(), k, slots)))
     monkeypatch.setattr(pkc.torch.cuda, "device", lambda *_: __import__("contextlib").nullcontext())
+    monkeypatch.setattr(pkc.device_errors, "state", lambda *_: NoErrors())
     cache = pkc.PagedKVCache(layers, 4, 16, 2, 8, torch.bfloat16, "cpu")
     return cache, calls
 
@@ -45,9 +59,33 @@ def test_deferred_rows_are_taken_by_layer_view(monkeypatch):
         got = pkc.take_deferred(cache.key_cache[2])
         assert got is not None and torch.equal(got[0], k) and torch.equal(got[2], s)
         assert pkc.take_deferred(cache.key_cache[2]) is None  # taken once
-    # layer 0 was never taken: appended when the block exits
+        assert torch.equal(pkc.take_deferred(cache.key_cache[0])[0], k)
+    assert calls == []
+    assert pkc.take_deferred(cache.key_cache[0]) is None  # outside the block nothing is deferred
+
+
+def test_rows_no_attention_took_are_appended_and_the_exit_raises(monkeypatch):
+    cache, calls = make_cache(monkeypatch)
+    k, v, s = rows()
+    with pytest.raises(RuntimeError, match=r"layer\(s\) \[0\] was not consumed"):
+        with cache.deferred_appends():
+            cache.write(0, k, v, s)
     assert [c[0] for c in calls] == [cache.key_cache[0].data_ptr()]
-    assert pkc.take_deferred(cache.key_cache[0]) is None
+    assert not pkc._DEFERRING
+
+
+def test_two_caches_keep_their_own_rows(monkeypatch):
+    a, _ = make_cache(monkeypatch)
+    b, _ = make_cache(monkeypatch)
+    ka, va, sa = rows(seed=3)
+    kb, vb, sb = rows(seed=4)
+    with a.deferred_appends(), b.deferred_appends():
+        a.write(1, ka, va, sa)
+        b.write(1, kb, vb, sb)
+        assert torch.equal(pkc.take_deferred(b.key_cache[1])[0], kb)
+        assert torch.equal(pkc.take_deferred(a.key_cache[1])[0], ka)
+        # a view that is not one whole layer of a pool owns nothing
+        assert pkc.take_deferred(a.key_cache[1, 1:]) is None
 
 
 def test_second_write_of_a_layer_lands_the_first(monkeypatch):
@@ -70,7 +108,8 @@ def test_nested_blocks_flush_only_at_the_outermost(monkeypatch):
         with cache.deferred_appends():
             cache.write(0, k, v, s)
         assert calls == []
-    assert len(calls) == 1
+        assert pkc.take_deferred(cache.key_cache[0]) is not None
+    assert calls == []
 
 
 class DeferringCache:
@@ -92,10 +131,7 @@ class DeferringCache:
 
 class Model:
     def __call__(self, input_ids_flat, position_ids_flat, kv_cache, attn_metadata, is_prefill):
-        record_paged_attention_task(PagedAttentionGraphTask(
-            query=torch.zeros(1), key_cache=None, value_cache=None, num_kv_heads=1, num_heads=1, scale=1.0,
-            block_tables=attn_metadata.block_tables, context_lens=attn_metadata.context_lens,
-            output=torch.zeros(1), workspace=None))
+        graph_workspace(FakeAttention(), input_ids_flat.numel())
 
         class Out:
             logits = torch.zeros(2)
@@ -112,7 +148,8 @@ def metadata():
 def test_graph_runner_defers_appends_only_when_fusing():
     for fuse, expected in ((True, 2), (False, 0)):  # warm-up run + capture
         cache = DeferringCache()
-        runner = FakeRunner(Model(), cache, batch_sizes=[2], fuse_appends=fuse)
+        runner = DecodeGraphRunner(Model(), cache, batch_sizes=[2], device="cpu", fuse_appends=fuse,
+                                   backend=FakeBackend())
         ids = torch.zeros(2, dtype=torch.long)
         assert runner.forward(ids, ids, metadata()) is not None
         assert cache.entered == expected

@@ -44,3 +44,22 @@ def test_prefill_attention_errors():
         attn(q, kv[:99], kv, md)
     with pytest.raises(ValueError, match=re.escape("prompt length 100 exceeds max_mask_len 64")):
         attn(q, kv, kv, md)
+
+
+def test_host_slot_outside_the_pool_raises_index_error_before_the_launch():
+    # the reference's index_copy_ raises IndexError for it (paged_kv_cache.py:68-69)
+    kv = PagedKVCache(1, 4, 16, 8, 128, BF16, "cpu")
+    k = torch.zeros(2, 8, 128, dtype=BF16)
+    with pytest.raises(IndexError, match="out of bounds for dimension 0 with size 64"):
+        kv.write(0, k, k, torch.tensor([3, 64], dtype=torch.long))
+    with pytest.raises(IndexError, match="index -1 is out of bounds"):
+        kv.write(0, k, k, torch.tensor([-1, 2], dtype=torch.long))
+
+
+def test_host_context_longer_than_its_table_raises_missing_block():
+    # BlockManager._physical_slot raises RuntimeError("missing block ...") (block_manager.py:194-205)
+    attn = NpuPagedAttention(16, 8, 128)
+    q = torch.zeros(2, 16, 128, dtype=BF16)
+    kc = torch.zeros(4, 16, 8, 128, dtype=BF16)
+    with pytest.raises(RuntimeError, match="missing block: context length 33 exceeds the 2-block table"):
+        attn(q, kc, kc, torch.zeros(2, 2, dtype=torch.int32), torch.tensor([5, 33], dtype=torch.int32))
