@@ -1,34 +1,37 @@
 #!/usr/bin/env python
-"""Benchmark of the B200 paged-KV decode hot path.
+"""Benchmark of the B200 paged-KV hot path.
 
     python bench.py [--gpus N] [--steps K] [--warmup W]
                     [--workload decode_c2|decode_c4|decode_c5|prefill_c3|kernels]
                     [--impl ours|reference]
 
-A "step" is one decode step of the configured batch through every layer:
-per layer, the KV append of this step's token and paged GQA decode attention
-over the whole context, replayed as ONE CUDA graph captured by
+Without --workload (what the driver runs) one JSON line is printed whose
+headline is config 2 (decode_c2) and whose ``sub_results`` carry the other
+configs measured in the same run, one after another on the same GPUs:
+prefill_c3 and decode_c4 at N = 1; decode_c4 and decode_c5 at N > 1. Every
+workload first measures, then checks a sampled slice of its own output on the
+box against an fp32 torch-CPU reference (``parity``), so each number is
+backed by a parity verdict of the same run. --workload X prints X alone.
+
+A decode "step" is one decode step of the configured batch through every
+layer: per layer, the KV append of this step's token and paged GQA decode
+attention over the whole context, replayed as ONE CUDA graph captured by
 DecodeGraphRunner at the batch size. The runner defers each layer's
 PagedKVCache.write so that the decode kernel performs the append itself
 (nvk_paged_decode_append): one launch per layer.
 
 Workloads (seeded synthetic inputs with the configs' shapes; no model weights):
-  decode_c2 (default, N=1 headline): 28 layers, 32 sequences, context ~
-      U[256, 2304], 16 query / 8 KV heads, head_dim 128, block 128, pool =
-      80% of free HBM, block tables drawn without replacement from a seeded
-      permutation of the pool. At N > 1 every rank runs its own such batch on
-      its own pool (sequence-sharded replicas, no collective): weak scaling.
+  decode_c2 (headline): 28 layers, 32 sequences, context ~ U[256, 2304], 16
+      query / 8 KV heads, head_dim 128, block 128, pool = 80% of free HBM,
+      block tables drawn without replacement from a seeded permutation of the
+      pool. At N > 1 every rank runs its own such batch on its own pool
+      (sequence-sharded replicas, no collective): weak scaling.
   decode_c4: 256 sequences, context ~ U[2048, 6144], split evenly across
       ranks by sequence (strong scaling).
   prefill_c3: config[2]: 32 requests sharing a hash-hit 768-token prefix
       (6 cached blocks in the real BlockManager) prefill their 256 new tokens
       each: per layer the 8192-row append and prefix-aware causal attention
       over 1024 keys; value = attention TF/s of the step.
-  kernels: the path's other kernels timed one by one under CUDA graphs on
-      config-sized inputs (prefill-sized append, decode- and prefill-sized
-      q/k norm + RoPE + append, device decode metadata, LM head + greedy
-      argmax over the 151,936-token vocabulary), with bytes moved and the
-      fraction of the measured HBM copy bandwidth.
   decode_c5: Qwen3-8B KV shapes (36 layers, 32 query / 8 KV heads), 128
       sequences at context 8192, KV-head sharded over N in {2, 4, 8} GPUs
       (the pool does not fit one GPU). Per layer: append of this rank's KV
@@ -36,22 +39,32 @@ Workloads (seeded synthetic inputs with the configs' shapes; no model weights):
       into every rank's gathered [128, 32, 128] output (in-kernel all-gather
       over NVLink, --gather kernel) or, as the baseline, decode followed by an
       NCCL all_gather_into_tensor and a permuting copy (--gather nccl).
+  kernels: the path's other kernels timed one by one under CUDA graphs on
+      config-sized inputs (prefill-sized append, decode- and prefill-sized
+      q/k norm + RoPE + append, device decode metadata, LM head + greedy
+      argmax over the 151,936-token vocabulary), with bytes moved and the
+      fraction of the measured HBM copy bandwidth.
 
-Printed (rank 0, one JSON line): value = KV bytes read by decode attention
-per step, summed over ranks, / max-over-ranks step time (GB/s); tok/s; the
-dominant kernel's roofline (decode attention timed alone with CUDA events on
-its stream, as one launch per layer captured in a CUDA graph); the
-prefill-sized append GB/s; an end-to-end figure through the
+Printed per workload: value = KV bytes read by decode attention per step,
+summed over ranks, / max-over-ranks step time (GB/s) for decode, attention
+TF/s for prefill; the dominant kernel's roofline (timed alone with CUDA events
+on its stream, one launch per layer captured in a CUDA graph, cycling layers
+so that every launch reads HBM); appends over four rotating source sets
+(block-contiguous and scattered slots); an end-to-end figure through the
 public API with pinned host inputs and a device->host read of the outputs;
-SM clocks sampled by nvidia-smi during the measurement; the CPU baseline
-(eager torch-CPU expression of the reference path on a bounded sample).
+SM clocks sampled by nvidia-smi during the measurement; per-rank step times
+and clocks at N > 1; the CPU baseline (eager torch-CPU expression of the
+reference path on a bounded sample, rank 0 at N = 1).
 
---impl reference times that CPU path alone on the host cores (rank 0 only).
+--impl reference times that CPU path alone on the host cores (rank 0 only):
+whole decode steps (every layer of the workload on the same one-layer host
+pool), with the same ``config`` as this arm.
 """
 
 from __future__ import annotations
 
 import argparse
+import gc
 import json
 import os
 import statistics
@@ -66,6 +79,7 @@ import torch
 
 ROOT = Path(__file__).resolve().parent
 KVH, HEAD_DIM, BLOCK = 8, 128, 128
+ATOL, RTOL = 2e-2, 1e-2  # attention tolerance vs fp32 (bf16 outputs)
 
 
 @dataclass
@@ -112,19 +126,24 @@ def peaks(key: str = "hbm_gbs") -> tuple[float, str]:
     return fallback[key], "fallback"
 
 
-def profiled_traffic(workload: str, kernel: str = "paged_decode") -> float | None:
-    """Per-launch DRAM bytes of a kernel from a committed ncu summary (a line
-    'traffic_bytes_per_launch: N' in profiles/<kernel>_<workload>.txt)."""
+def profiled_value(workload: str, kernel: str, key: str) -> float | None:
+    """A figure from a committed ncu summary: the line '<key>: N' in
+    profiles/<kernel>_<workload>.txt."""
     p = ROOT / "profiles" / f"{kernel}_{workload}.txt"
     if not p.exists():
         return None
     for line in p.read_text().splitlines():
-        if line.startswith("traffic_bytes_per_launch:"):
+        if line.startswith(key + ":"):
             try:
                 return float(line.split(":", 1)[1].split()[0].replace(",", ""))
             except ValueError:
                 return None
     return None
+
+
+def profiled_traffic(workload: str, kernel: str = "paged_decode") -> float | None:
+    """Per-launch DRAM bytes of a kernel from its committed ncu summary."""
+    return profiled_value(workload, kernel, "traffic_bytes_per_launch")
 
 
 class ClockSampler:
@@ -170,11 +189,13 @@ class ClockSampler:
             os.unlink(self.path)
         if not rows:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
+
         def num(x):
             try:
                 return float(x)
             except ValueError:
                 return None
+
         sm = [num(r[1]) for r in rows if num(r[1]) is not None]
         smax = [num(r[2]) for r in rows if num(r[2]) is not None]
         power = [num(r[3]) for r in rows if num(r[3]) is not None]
@@ -210,24 +231,38 @@ def barrier_sync(world):
     torch.cuda.synchronize()
 
 
-def max_over_ranks(x: float, world: int) -> float:
+def _reduce(x: float, world: int, op: str) -> float:
     if world == 1:
         return x
     import torch.distributed as dist
 
     t = torch.tensor([x], dtype=torch.float64, device="cuda")
-    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    dist.all_reduce(t, op={"max": dist.ReduceOp.MAX, "sum": dist.ReduceOp.SUM, "min": dist.ReduceOp.MIN}[op])
     return float(t.item())
+
+
+def max_over_ranks(x: float, world: int) -> float:
+    return _reduce(x, world, "max")
 
 
 def sum_over_ranks(x: float, world: int) -> float:
+    return _reduce(x, world, "sum")
+
+
+def all_ranks(obj, world: int) -> list:
     if world == 1:
-        return x
+        return [obj]
     import torch.distributed as dist
 
-    t = torch.tensor([x], dtype=torch.float64, device="cuda")
-    dist.all_reduce(t, op=dist.ReduceOp.SUM)
-    return float(t.item())
+    out = [None] * world
+    dist.all_gather_object(out, obj)
+    return out
+
+
+def free_device_memory() -> None:
+    gc.collect()
+    torch.cuda.synchronize()
+    torch.cuda.empty_cache()
 
 
 # ----------------------------------------------------------------- setup ----
@@ -241,6 +276,25 @@ def rank_contexts(wl: Workload, world: int, rank: int) -> list[int]:
         return [ctx[i] for i in sequence_shard(wl.batch, world, rank)]
     g = torch.Generator().manual_seed(1000 + rank)
     return torch.randint(wl.ctx_lo, wl.ctx_hi + 1, (wl.batch,), generator=g).tolist()
+
+
+def decode_config(wl: Workload, world: int) -> dict:
+    """The workload as both arms name it (``config`` of the JSON line)."""
+    batch_per_gpu = wl.batch if wl.scaling == "weak" else -(-wl.batch // world)
+    global_batch = wl.batch * world if wl.scaling == "weak" else wl.batch
+    ctx_after = [c + 1 for r in range(world) for c in rank_contexts(wl, world, r)]
+    return {
+        "workload": wl.describe,
+        "layers": wl.layers,
+        "batch_per_gpu": batch_per_gpu,
+        "global_batch": global_batch,
+        "seq_len": [wl.ctx_lo, wl.ctx_hi],
+        "heads": [wl.heads, wl.kv_heads, HEAD_DIM],
+        "block_size": BLOCK,
+        "parallelism": f"sequence-sharded x{world}, independent pools, no collective",
+        "cache": "inputs larger than L2: every step reads %.2f GB of KV"
+                 % (kv_bytes_per_layer(ctx_after, wl.kv_heads) * wl.layers / 1e9),
+    }
 
 
 class AttentionOnlyDecoder:
@@ -302,10 +356,88 @@ def kv_bytes_per_layer(ctx_after: list[int], kv_heads: int) -> int:
     return sum(ctx_after) * kv_heads * HEAD_DIM * 2 * 2
 
 
+# ---------------------------------------------------------------- parity ----
+def _gather_rows(cache_layer: torch.Tensor, table_row: torch.Tensor, n: int) -> torch.Tensor:
+    """First n token rows [n, KVH, D] of one sequence, as fp32 on the host."""
+    nblk = -(-n // BLOCK)
+    rows = cache_layer.index_select(0, table_row[:nblk].to(torch.int64))
+    return rows.reshape(nblk * BLOCK, *cache_layer.shape[2:])[:n].float().cpu()
+
+
+def _attend_fp32(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: float, causal_lq: int = 0):
+    """q [Tq, H, D], k/v [Tk, KVH, D] fp32 -> [Tq, H, D]; bottom-right causal
+    when causal_lq > 0 (query i sees key j <= Tk - Tq + i)."""
+    tq, h, d = q.shape
+    tk, kvh, _ = k.shape
+    qg = q.view(tq, kvh, h // kvh, d)
+    s = torch.einsum("tgqd,ngd->gqtn", qg, k) * scale
+    if causal_lq:
+        i = torch.arange(tq)[:, None]
+        j = torch.arange(tk)[None, :]
+        s = s.masked_fill(~(j <= (tk - tq) + i), float("-inf"))
+    p = torch.softmax(s, dim=-1)
+    return torch.einsum("gqtn,ngd->tgqd", p, v).reshape(tq, h, d)
+
+
+def _compare(got: torch.Tensor, want: torch.Tensor) -> tuple[bool, float]:
+    err = (got - want).abs()
+    ok = bool((err <= ATOL + RTOL * want.abs()).all()) and not bool(torch.isnan(got).any())
+    return ok, float(err.max()) if err.numel() else 0.0
+
+
+def decode_parity(out: torch.Tensor, q: torch.Tensor, kc: torch.Tensor, vc: torch.Tensor, tables: torch.Tensor,
+                  ctx_after: list[int], layer: int, sample: list[int]) -> dict:
+    """A few sequences of one layer's decode output vs an fp32 torch-CPU
+    gather + softmax of the same pool rows."""
+    ok, worst = True, 0.0
+    for b in sample:
+        n = ctx_after[b]
+        k = _gather_rows(kc, tables[b], n)
+        v = _gather_rows(vc, tables[b], n)
+        want = _attend_fp32(q[b:b + 1].float().cpu(), k, v, HEAD_DIM ** -0.5)[0]
+        good, err = _compare(out[b].float().cpu(), want)
+        ok, worst = ok and good, max(worst, err)
+    return {"parity_ok": ok, "max_abs_err": worst, "layer": layer, "sequences_checked": len(sample),
+            "tolerance": f"|err| <= {ATOL} + {RTOL}*|ref| vs fp32 torch-CPU gather+softmax"}
+
+
+def spread(n: int, k: int = 4) -> list[int]:
+    return sorted({round(i * (n - 1) / max(k - 1, 1)) for i in range(k)}) if n else []
+
+
 # --------------------------------------------------------------- measure ----
+def graph_time(fns, launches: int, device, reps: int = 3) -> float:
+    """Average device time (s) of one call over `launches` calls captured in one
+    CUDA graph; call i is fns[i % len(fns)] (fns are the same kernel on
+    rotating input/output sets, so that L2 does not hold a launch's data from
+    the previous one)."""
+    fns = fns if isinstance(fns, (list, tuple)) else [fns]
+    stream = torch.cuda.Stream(device)
+    with torch.cuda.stream(stream):
+        for fn in fns:
+            fn()
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            for i in range(launches):
+                fns[i % len(fns)]()
+        for _ in range(2):
+            graph.replay()
+        torch.cuda.synchronize()
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record(stream)
+        for _ in range(reps):
+            graph.replay()
+        end.record(stream)
+        end.synchronize()
+    del graph
+    return start.elapsed_time(end) / 1e3 / (reps * launches)
+
+
 def time_decode_kernel(wl, md, kv, model, device, launches: int, seconds: float = 0.8) -> float:
     """Average duration (s) of one nvk_paged_decode launch, cycling layers so
-    that every launch reads a different 100+ MB slice of HBM."""
+    that every launch reads a different slice of HBM (each larger than L2
+    for the configs timed here)."""
     from nano_vllm_ascend_b200 import ops
 
     b = model.q.shape[1]
@@ -353,132 +485,46 @@ def time_decode_kernel(wl, md, kv, model, device, launches: int, seconds: float 
     return per
 
 
-def time_append(kv, bm, device, rows: int, launches: int) -> float:
-    """Average duration (s) of one prefill-sized append (rows tokens, K+V) into free blocks."""
+def time_appends(kv, bm, device, rows: int = 8192, launches: int = 56) -> dict:
+    """Prefill-sized appends (rows tokens, K+V) into free pool slots, timed
+    under a CUDA graph over four rotating source sets (4 x 33.5 MB of rows,
+    more than L2, so every launch reads its rows from HBM), each set into its
+    own layer and slots:
+      contiguous -- a set's rows fill whole free blocks in order (a prefill's layout);
+      scattered  -- a set's rows go to distinct random free slots across the pool."""
     from nano_vllm_ascend_b200 import ops
 
-    free = bm.free_block_ids[: (rows + BLOCK - 1) // BLOCK]
-    slots = torch.cat([torch.arange(f * BLOCK, (f + 1) * BLOCK) for f in free])[:rows].to(device)
+    sets, nblk = 4, -(-rows // BLOCK)
+    free = torch.tensor(bm.free_block_ids, dtype=torch.int64)
+    if free.numel() < sets * nblk:
+        return {"skipped": f"needs {sets * nblk} free pool blocks, {free.numel()} free (small profiling pool)"}
     g = torch.Generator(device=device).manual_seed(3)
-    k = torch.randn(rows, kv.num_kv_heads, HEAD_DIM, generator=g, device=device).to(torch.bfloat16)
-    v = torch.randn(rows, kv.num_kv_heads, HEAD_DIM, generator=g, device=device).to(torch.bfloat16)
-    # One CUDA graph of `launches` appends (cycling layers): a Python call per
-    # append costs more host time than the kernel takes on the device.
-    stream = torch.cuda.Stream(device)
-    with torch.cuda.stream(stream):
-        for i in range(3):
-            ops.kv_append(kv.key_cache[i % kv.num_layers], kv.value_cache[i % kv.num_layers], k, v, slots)
-        torch.cuda.synchronize()
-        graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(graph, stream=stream):
-            for i in range(launches):
-                layer = i % kv.num_layers
-                ops.kv_append(kv.key_cache[layer], kv.value_cache[layer], k, v, slots)
-        for _ in range(2):
-            graph.replay()
-        torch.cuda.synchronize()
-        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        start.record(stream)
-        for _ in range(3):
-            graph.replay()
-        end.record(stream)
-        end.synchronize()
-    del graph
-    return start.elapsed_time(end) / 1e3 / (3 * launches)
+    gc_ = torch.Generator().manual_seed(4)
+    src = [(torch.randn(rows, kv.num_kv_heads, HEAD_DIM, generator=g, device=device).to(torch.bfloat16),
+            torch.randn(rows, kv.num_kv_heads, HEAD_DIM, generator=g, device=device).to(torch.bfloat16))
+           for _ in range(sets)]
+    offs = torch.arange(BLOCK, dtype=torch.int64)
+    contiguous = [(free[r * nblk:(r + 1) * nblk, None] * BLOCK + offs).reshape(-1)[:rows].to(device)
+                  for r in range(sets)]
+    scattered = []
+    for r in range(sets):
+        pick = torch.randperm(free.numel() * BLOCK, generator=gc_)[:rows]
+        scattered.append((free[pick // BLOCK] * BLOCK + pick % BLOCK).to(device))
+    byts = rows * kv.num_kv_heads * HEAD_DIM * 2 * 2 * 2 + rows * 8
+    peak, _ = peaks()
+    out = {"rows": rows, "bytes": byts, "source_sets": sets}
+    for name, slot_sets in (("contiguous", contiguous), ("scattered", scattered)):
+        fns = [lambda r=r, sl=sl: ops.kv_append(kv.key_cache[r % kv.num_layers], kv.value_cache[r % kv.num_layers],
+                                                src[r][0], src[r][1], sl) for r, sl in enumerate(slot_sets)]
+        t = graph_time(fns, launches, device)
+        out[name] = {"us": t * 1e6, "gbs": byts / t / 1e9, "frac": byts / t / 1e9 / peak}
+    return out
 
 
-class CpuBaseline:
-    """Eager torch-CPU reference path (oracle/cpu_baseline.py) on one layer's
-    worth of this workload: the sequences' blocks in a host pool, this step's
-    append (index_copy_) and decode attention (gather + fp32 softmax). Every
-    layer of a step is identical work, so a step costs layers x one layer."""
+def measure_decode(args, wl: Workload, world: int, rank: int, local: int, with_cpu: bool) -> dict:
+    """One decode workload (config 2 or 4) on this rank: the JSON line's fields."""
+    from nano_vllm_ascend_b200 import DecodeGraphRunner, check_errors
 
-    def __init__(self, wl: Workload, ctx: list[int], threads: int):
-        torch.set_num_threads(threads)
-        self.wl, self.ctx, self.threads = wl, ctx, threads
-        b = len(ctx)
-        g = torch.Generator().manual_seed(0)
-        nblk = [(n + 1 + BLOCK - 1) // BLOCK for n in ctx]
-        nb = sum(nblk)
-        self.kc = torch.randn(nb, BLOCK, wl.kv_heads, HEAD_DIM, generator=g).to(torch.bfloat16)
-        self.vc = torch.randn(nb, BLOCK, wl.kv_heads, HEAD_DIM, generator=g).to(torch.bfloat16)
-        perm = torch.randperm(nb, generator=g).to(torch.int32)
-        self.tables = torch.zeros(b, max(nblk), dtype=torch.int32)
-        self.slots = torch.zeros(b, dtype=torch.int64)
-        used = 0
-        for i, m in enumerate(nblk):
-            self.tables[i, :m] = perm[used : used + m]
-            used += m
-            self.slots[i] = int(self.tables[i, ctx[i] // BLOCK]) * BLOCK + ctx[i] % BLOCK
-        self.q = torch.randn(b, wl.heads, HEAD_DIM, generator=g).to(torch.bfloat16)
-        self.k = torch.randn(b, wl.kv_heads, HEAD_DIM, generator=g).to(torch.bfloat16)
-        self.v = torch.randn(b, wl.kv_heads, HEAD_DIM, generator=g).to(torch.bfloat16)
-        self.ctx_after = torch.tensor([n + 1 for n in ctx], dtype=torch.int32)
-        self.bytes_layer = kv_bytes_per_layer([n + 1 for n in ctx], wl.kv_heads)
-
-    def layer(self) -> None:
-        from oracle import cpu_baseline
-
-        cpu_baseline.append(self.kc, self.vc, self.k, self.v, self.slots)
-        cpu_baseline.decode(self.q, self.kc, self.vc, self.tables, self.ctx_after, HEAD_DIM ** -0.5)
-
-    def time_layers(self, seconds: float, min_layers: int = 1) -> tuple[float, int]:
-        """Runs layer() until ``seconds`` elapsed (at least min_layers); returns (s per layer, layers)."""
-        n = 0
-        t0 = time.perf_counter()
-        while True:
-            self.layer()
-            n += 1
-            el = time.perf_counter() - t0
-            if n >= min_layers and el >= seconds:
-                return el / n, n
-
-
-def cpu_baseline_decode(wl: Workload, ctx: list[int], seconds: float, threads: int) -> dict:
-    base = CpuBaseline(wl, ctx, threads)
-    base.layer()  # warm-up
-    per_layer, n = base.time_layers(seconds)
-    gbs = base.bytes_layer / per_layer / 1e9
-    return {"value": gbs, "unit": "GB/s", "cores": threads, "kind": "port",
-            "sample": f"{n} layer-steps (append + decode attention) of {len(ctx)} seqs on one layer's pool, "
-                      f"{n * per_layer:.1f}s", "ms_per_layer": per_layer * 1e3,
-            "tok_per_s": len(ctx) / (per_layer * wl.layers)}
-
-
-# ------------------------------------------------------------------ arms ----
-def run_reference(args, world, rank):
-    if rank != 0:
-        return 0
-    wl = WORKLOADS[args.workload]
-    threads = os.cpu_count() or 1
-    ctx = rank_contexts(wl, 1, 0)
-    base = CpuBaseline(wl, ctx, threads)
-    # a step = one layer of the workload (append + decode attention); the
-    # full step costs layers x that, reported in ms_per_step
-    for _ in range(args.warmup):
-        base.layer()
-    per_layer, n = base.time_layers(0.0, min_layers=args.steps)
-    gbs = base.bytes_layer / per_layer / 1e9
-    line = {
-        "impl": "reference", "metric": "paged decode-attn KV GB/s", "value": gbs, "unit": "GB/s",
-        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": per_layer * wl.layers * 1e3, "higher_is_better": True, "scaling": wl.scaling,
-        "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": wl.describe, "layers": wl.layers, "batch": len(ctx), "seq_len": [wl.ctx_lo, wl.ctx_hi],
-                   "parallelism": "host CPU"},
-        "tok_per_s": len(ctx) / (per_layer * wl.layers),
-        "cpu_baseline": {"value": gbs, "unit": "GB/s", "cores": threads, "kind": "port",
-                         "sample": f"{n} layer-steps (append + decode attention, one layer of the workload each)"},
-        "e2e": {"value": gbs, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
-    }
-    print(json.dumps(line), flush=True)
-    return 0
-
-
-def run_ours(args, world, rank, local):
-    from nano_vllm_ascend_b200 import DecodeGraphRunner
-
-    wl = WORKLOADS[args.workload]
     device = torch.device("cuda", local)
     ctx, bm, md, kv, model, num_blocks = build(wl, world, rank, device, args.pool_blocks)
     b = len(ctx)
@@ -492,23 +538,23 @@ def run_ours(args, world, rank, local):
     positions = torch.tensor(ctx, dtype=torch.long, device=device)
     if runner.forward(input_ids, positions, md) is None:
         raise RuntimeError("decode graph capture failed")
-    entry = runner.entries[b]
+    slot = runner.slot(b)
     torch.cuda.synchronize()
 
     with ClockSampler(local) as clocks:
         # dominant kernel alone (roofline)
         t_dec = time_decode_kernel(wl, md, kv, model, device, launches=max(56, 4 * wl.layers),
                                    seconds=0.0 if args.quick else 0.8)
-        t_app = time_append(kv, bm, device, rows=8192, launches=8 if args.quick else 56)
+        appends = time_appends(kv, bm, device, launches=8 if args.quick else 56)
         # the step: W warm-up replays, then exactly K timed replays
         for _ in range(args.warmup):
-            entry.graph.replay()
+            slot.graph.replay()
         barrier_sync(world)
         stream = torch.cuda.current_stream(device)
         start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         start.record(stream)
         for _ in range(args.steps):
-            entry.graph.replay()
+            slot.graph.replay()
         end.record(stream)
         barrier_sync(world)
         t_step = start.elapsed_time(end) / 1e3 / args.steps
@@ -518,7 +564,7 @@ def run_ours(args, world, rank, local):
         h_q = model.q.cpu().pin_memory()
         h_k = model.k.cpu().pin_memory()
         h_v = model.v.cpu().pin_memory()
-        h_out = torch.empty(entry.logits.shape, dtype=entry.logits.dtype).pin_memory()
+        h_out = torch.empty(slot.logits.shape, dtype=slot.logits.dtype).pin_memory()
         h_tables = md.block_tables.cpu().pin_memory()
         h_slots = md.slot_mapping.cpu().pin_memory()
         h_ctx = md.context_lens.pin_memory()
@@ -546,104 +592,68 @@ def run_ours(args, world, rank, local):
         barrier_sync(world)
         t_e2e = e_start.elapsed_time(e_end) / 1e3 / args.steps
     clk = clocks.summary()
+    check_errors(device)  # every device error word of the run is clear
+
+    # parity of the step's own output: the last layer of the last replay
+    layer = wl.layers - 1
+    kc, vc = kv.get_physical_cache(layer)
+    parity = decode_parity(slot.logits[layer], model.q[layer], kc, vc, md.block_tables.to(device), ctx_after, layer,
+                           spread(b))
+    parity["parity_ok"] = _reduce(1.0 if parity["parity_ok"] else 0.0, world, "min") > 0.5
+    parity["max_abs_err"] = max_over_ranks(parity["max_abs_err"], world)
 
     h2d = sum(t.numel() * t.element_size() for t in (h_q, h_k, h_v, h_tables, h_slots, h_ctx, h_pos, h_ids))
     d2h = h_out.numel() * h_out.element_size()
-
+    per_rank = all_ranks({"rank": rank, "ms_per_step": t_step * 1e3, "sm_mhz": clk.get("sm_mhz"),
+                          "us_per_decode_launch": t_dec * 1e6, "reasons": clk.get("reasons")}, world)
     t_step_max = max_over_ranks(t_step, world)
     t_e2e_max = max_over_ranks(t_e2e, world)
+    t_dec_max = max_over_ranks(t_dec, world)
     bytes_all = sum_over_ranks(float(bytes_step), world)
     seqs_all = sum_over_ranks(float(b), world)
     peak, peak_kind = peaks()
     dec_bytes_launch = bytes_layer + b * wl.heads * HEAD_DIM * 2 * 2 + md.block_tables.numel() * 4 + b * 4
-    achieved = dec_bytes_launch / t_dec / 1e9
-    app_bytes = 8192 * wl.kv_heads * HEAD_DIM * 2 * 2 * 2 + 8192 * 8
-    traffic = profiled_traffic(wl.name)
-
-    if rank == 0:
-        cpu = None
-        if world == 1 and not args.no_cpu_baseline:
-            cpu = cpu_baseline_decode(wl, ctx, seconds=args.cpu_seconds, threads=os.cpu_count() or 1)
-        line = {
-            "metric": "paged decode-attn KV GB/s",
-            "value": bytes_all / t_step_max / 1e9,
-            "unit": "GB/s",
-            "n_gpus": world,
-            "steps": args.steps,
-            "warmup": args.warmup,
-            "ms_per_step": t_step_max * 1e3,
-            "higher_is_better": True,
-            "scaling": wl.scaling,
-            "vs_baseline": None,
-            "dtype": "bf16",
-            "data": "synthetic: seeded N(0,1) q/K/V, seeded context lengths and block tables (no weights)",
-            "config": {
-                "workload": wl.describe,
-                "layers": wl.layers,
-                "batch_per_gpu": b,
-                "global_batch": int(seqs_all),
-                "seq_len": [wl.ctx_lo, wl.ctx_hi],
-                "heads": [wl.heads, wl.kv_heads, HEAD_DIM],
-                "block_size": BLOCK,
-                "pool_blocks": num_blocks,
-                "parallelism": f"sequence-sharded x{world}, independent pools, no collective",
-                "cache": "inputs larger than L2: every step reads %.2f GB of KV" % (bytes_step / 1e9),
-                "decode_grid": "persistent, one CTA per SM",
-                "append": "fused into the decode kernel" if runner.fuse_appends else "separate kernel",
-            },
-            "tok_per_s": seqs_all / t_step_max,
-            "hbm_frac_of_step": (bytes_all / t_step_max / 1e9) / (peak * world),
-            "append": {"gbs": app_bytes / t_app / 1e9, "rows": 8192, "us": t_app * 1e6,
-                       "frac": app_bytes / t_app / 1e9 / peak},
-            "roofline": {"kernel": "paged_decode_kernel", "bound": "hbm", "achieved": achieved, "peak": peak,
-                         "peak_kind": peak_kind, "unit": "GB/s", "frac": achieved / peak,
-                         "frac_of_nominal_8tbs": achieved / 8000.0, "traffic": traffic,
-                         "algorithmic_bytes_per_launch": dec_bytes_launch, "us_per_launch": t_dec * 1e6},
-            "e2e": {"value": bytes_all / t_e2e_max / 1e9, "unit": "GB/s", "h2d_bytes_per_step": h2d,
-                    "d2h_bytes_per_step": d2h, "ms_per_step": t_e2e_max * 1e3},
-            "clocks": clk,
-            "gpu_launches": args.steps * wl.layers * (1 if runner.fuse_appends else 2),
-            "cpu_baseline": cpu,
-        }
-        print(json.dumps(line), flush=True)
+    achieved = dec_bytes_launch / t_dec_max / 1e9
+    traffic = profiled_traffic(wl.name) if world == 1 else None
     runner.release()
+    line = {
+        "metric": "paged decode-attn KV GB/s",
+        "value": bytes_all / t_step_max / 1e9,
+        "unit": "GB/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": t_step_max * 1e3,
+        "higher_is_better": True,
+        "scaling": wl.scaling,
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic: seeded N(0,1) q/K/V, seeded context lengths and block tables (no weights)",
+        "config": decode_config(wl, world),
+        "setup": {"pool_blocks": num_blocks, "decode_grid": "persistent, one CTA per SM",
+                  "append": "fused into the decode kernel" if runner.fuse_appends else "separate kernel"},
+        "tok_per_s": seqs_all / t_step_max,
+        "hbm_frac_of_step": (bytes_all / t_step_max / 1e9) / (peak * world),
+        "parity": parity,
+        "append": appends,
+        "roofline": {"kernel": "paged_decode_kernel", "bound": "hbm", "achieved": achieved, "peak": peak,
+                     "peak_kind": peak_kind, "unit": "GB/s", "frac": achieved / peak,
+                     "frac_of_nominal_8tbs": achieved / 8000.0, "traffic": traffic,
+                     "algorithmic_bytes_per_launch": dec_bytes_launch, "us_per_launch": t_dec_max * 1e6},
+        "e2e": {"value": bytes_all / t_e2e_max / 1e9, "unit": "GB/s", "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h, "ms_per_step": t_e2e_max * 1e3},
+        "clocks": clk,
+        "gpu_launches": args.steps * wl.layers * (1 if runner.fuse_appends else 2),
+        "cpu_baseline": None,
+    }
     if world > 1:
-        import torch.distributed as dist
-
-        dist.barrier()
-        dist.destroy_process_group()
-    return 0
+        line["per_rank"] = per_rank
+    if with_cpu and rank == 0:
+        line["cpu_baseline"] = cpu_baseline_decode(wl, ctx, seconds=args.cpu_seconds, threads=os.cpu_count() or 1)
+    return line
 
 
 # ------------------------------------------------------------- kernels ----
-def graph_time(fns, launches: int, device) -> float:
-    """Average device time (s) of one call over `launches` calls captured in one
-    CUDA graph; call i is fns[i % len(fns)] (fns are the same kernel on
-    rotating input/output sets, so that L2 does not hold a launch's data from
-    the previous one)."""
-    fns = fns if isinstance(fns, (list, tuple)) else [fns]
-    stream = torch.cuda.Stream(device)
-    with torch.cuda.stream(stream):
-        for fn in fns:
-            fn()
-        torch.cuda.synchronize()
-        graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(graph, stream=stream):
-            for i in range(launches):
-                fns[i % len(fns)]()
-        for _ in range(2):
-            graph.replay()
-        torch.cuda.synchronize()
-        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        start.record(stream)
-        for _ in range(3):
-            graph.replay()
-        end.record(stream)
-        end.synchronize()
-    del graph
-    return start.elapsed_time(end) / 1e3 / (3 * launches)
-
-
 def run_kernels(args, world, rank, local):
     """The hot path's kernels other than decode/prefill attention, one by one.
     Each timed kernel rotates over input/output sets whose sum exceeds the
@@ -733,7 +743,7 @@ def run_kernels(args, world, rank, local):
 
 
 # ------------------------------------------------------------ config 5 ----
-def run_c5_ours(args, world, rank, local):
+def measure_c5(args, world: int, rank: int, local: int, gather: str) -> dict:
     """KV-head-sharded decode step (config 5) with the outputs all-gathered."""
     from nano_vllm_ascend_b200 import BlockManager, PagedKVCache, ops
     from nano_vllm_ascend_b200.peer_gather import PeerGather
@@ -772,7 +782,7 @@ def run_c5_ours(args, world, rank, local):
     slot_map = md.slot_mapping.to(device)
     scale = HEAD_DIM ** -0.5
     ws = torch.zeros(ops.decode_workspace_bytes(b, hl, kvh, HEAD_DIM), dtype=torch.uint8, device=device)
-    in_kernel = args.gather == "kernel"
+    in_kernel = gather == "kernel"
     pg = PeerGather(b, wl.heads, HEAD_DIM, slots=layers, device=device) if in_kernel else None
     local_out = torch.empty(layers, b, hl, HEAD_DIM, dtype=torch.bfloat16, device=device)
     gathered = torch.empty(layers, b, wl.heads, HEAD_DIM, dtype=torch.bfloat16, device=device)
@@ -805,8 +815,8 @@ def run_c5_ours(args, world, rank, local):
     torch.cuda.synchronize()
 
     with torch.cuda.stream(stream), ClockSampler(local) as clocks:
-        # decode kernel alone (roofline; with --gather kernel the kernel includes
-        # its gather), cycling layers: every rank runs the same launches
+        # decode kernel alone (roofline; with the in-kernel gather the kernel
+        # includes its gather), cycling layers: every rank runs the same launches
         for i in range(layers):
             attend(i, gather=False)
         barrier_sync(world)
@@ -854,11 +864,34 @@ def run_c5_ours(args, world, rank, local):
         ev1.record(stream)
         barrier_sync(world)
         t_e2e = ev0.elapsed_time(ev1) / 1e3 / args.steps
+
+        # parity: layer 0 gathered once more (the pool already holds this
+        # step's rows); every rank checks all heads of a few sequences
+        out0 = attend(0).clone()
+        barrier_sync(world)
     clk = clocks.summary()
     if ops.decode_error_word(ws) != 0:
         raise RuntimeError(f"decode error word {ops.decode_error_word(ws)}")
+    sample = spread(b)
+    kc0, vc0 = kv.get_physical_cache(0)
+    mine = []
+    for s in sample:
+        k = _gather_rows(kc0, tables[s], ctx[s] + 1)
+        v = _gather_rows(vc0, tables[s], ctx[s] + 1)
+        mine.append(_attend_fp32(q[0, s:s + 1].float().cpu(), k, v, scale)[0])
+    refs = all_ranks((hoff, torch.stack(mine)), world)
+    want = torch.zeros(len(sample), wl.heads, HEAD_DIM)
+    for off, rows in refs:
+        want[:, off:off + rows.shape[1]] = rows
+    ok, err = _compare(out0[sample].float().cpu(), want)  # [sample, all heads] on every rank
+    parity = {"parity_ok": _reduce(1.0 if ok else 0.0, world, "min") > 0.5,
+              "max_abs_err": max_over_ranks(err, world), "layer": 0, "sequences_checked": len(sample),
+              "heads_checked_per_rank": wl.heads,
+              "tolerance": f"|err| <= {ATOL} + {RTOL}*|ref| vs fp32 torch-CPU gather+softmax, all ranks"}
 
     bytes_layer = kv_bytes_per_layer([n + 1 for n in ctx], kvh)
+    per_rank = all_ranks({"rank": rank, "ms_per_step": t_step * 1e3, "sm_mhz": clk.get("sm_mhz"),
+                          "us_per_decode_launch": t_dec * 1e6, "reasons": clk.get("reasons")}, world)
     t_step_max = max_over_ranks(t_step, world)
     t_e2e_max = max_over_ranks(t_e2e, world)
     t_dec_max = max_over_ranks(t_dec, world)
@@ -868,46 +901,43 @@ def run_c5_ours(args, world, rank, local):
     nvlink_bytes = b * hl * HEAD_DIM * 2 * (world - 1)
     h2d = sum(t.numel() * t.element_size() for t in (h_q, h_k, h_v, h_tables, h_slots, h_ctx))
     d2h = h_out.numel() * h_out.element_size()
-    if rank == 0:
-        line = {
-            "metric": "paged decode-attn KV GB/s", "value": bytes_all / t_step_max / 1e9, "unit": "GB/s",
-            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": t_step_max * 1e3,
-            "higher_is_better": True, "scaling": wl.scaling, "vs_baseline": None, "dtype": "bf16",
-            "data": "synthetic: seeded N(0,1) q/K/V (pool layer 0 random, copied to the other layers), "
-                    "seeded block tables",
-            "config": {"workload": wl.describe, "layers": layers, "global_batch": b, "seq_len": wl.ctx_lo + 1,
-                       "heads": [wl.heads, wl.kv_heads, HEAD_DIM], "heads_per_gpu": [hl, kvh],
-                       "block_size": BLOCK, "pool_blocks": num_blocks,
-                       "parallelism": f"KV-head sharded x{world}",
-                       "gather": "in-kernel peer stores over NVLink + epoch flags" if in_kernel
-                       else "NCCL all_gather_into_tensor + permute",
-                       "append": "fused into the decode kernel",
-                       "cache": "inputs larger than L2: every step reads %.1f GB of KV per GPU"
-                                % (bytes_layer * layers / 1e9)},
-            "tok_per_s": b / t_step_max,
-            "hbm_frac_of_step": (bytes_all / t_step_max / 1e9) / (peak * world),
-            "roofline": {"kernel": "paged_decode_kernel (gather)" if in_kernel else "paged_decode_kernel",
-                         "bound": "hbm", "achieved": dec_bytes / t_dec_max / 1e9, "peak": peak,
-                         "peak_kind": peak_kind, "unit": "GB/s", "frac": dec_bytes / t_dec_max / 1e9 / peak,
-                         "traffic": None, "algorithmic_bytes_per_launch": dec_bytes,
-                         "nvlink_bytes_per_launch": nvlink_bytes if in_kernel else 0,
-                         "us_per_launch": t_dec_max * 1e6},
-            "e2e": {"value": bytes_all / t_e2e_max / 1e9, "unit": "GB/s", "h2d_bytes_per_step": h2d,
-                    "d2h_bytes_per_step": d2h, "ms_per_step": t_e2e_max * 1e3},
-            "clocks": clk,
-            "gpu_launches": args.steps * layers,
-            "cpu_baseline": None,
-        }
-        print(json.dumps(line), flush=True)
+    line = {
+        "metric": "paged decode-attn KV GB/s", "value": bytes_all / t_step_max / 1e9, "unit": "GB/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": t_step_max * 1e3,
+        "higher_is_better": True, "scaling": wl.scaling, "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic: seeded N(0,1) q/K/V (pool layer 0 random, copied to the other layers), "
+                "seeded block tables",
+        "config": {"workload": wl.describe, "layers": layers, "global_batch": b, "seq_len": wl.ctx_lo + 1,
+                   "heads": [wl.heads, wl.kv_heads, HEAD_DIM], "heads_per_gpu": [hl, kvh],
+                   "block_size": BLOCK, "parallelism": f"KV-head sharded x{world}",
+                   "gather": "in-kernel peer stores over NVLink + epoch flags" if in_kernel
+                   else "NCCL all_gather_into_tensor + permute",
+                   "append": "fused into the decode kernel",
+                   "cache": "inputs larger than L2: every step reads %.1f GB of KV per GPU"
+                            % (bytes_layer * layers / 1e9)},
+        "setup": {"pool_blocks": num_blocks},
+        "tok_per_s": b / t_step_max,
+        "hbm_frac_of_step": (bytes_all / t_step_max / 1e9) / (peak * world),
+        "parity": parity,
+        "comm": {"kind": "in-kernel all-gather (plain peer stores, no multicast)" if in_kernel else "NCCL all-gather",
+                 "nvlink_bytes_per_launch": nvlink_bytes, "ranks": world},
+        "roofline": {"kernel": "paged_decode_kernel (gather)" if in_kernel else "paged_decode_kernel",
+                     "bound": "hbm", "achieved": dec_bytes / t_dec_max / 1e9, "peak": peak,
+                     "peak_kind": peak_kind, "unit": "GB/s", "frac": dec_bytes / t_dec_max / 1e9 / peak,
+                     "traffic": None, "algorithmic_bytes_per_launch": dec_bytes,
+                     "nvlink_bytes_per_launch": nvlink_bytes if in_kernel else 0,
+                     "us_per_launch": t_dec_max * 1e6},
+        "e2e": {"value": bytes_all / t_e2e_max / 1e9, "unit": "GB/s", "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h, "ms_per_step": t_e2e_max * 1e3},
+        "clocks": clk,
+        "per_rank": per_rank,
+        "gpu_launches": args.steps * layers,
+        "cpu_baseline": None,
+    }
     del graph
     if pg is not None:
         pg.close()
-    if world > 1:
-        import torch.distributed as dist
-
-        dist.barrier()
-        dist.destroy_process_group()
-    return 0
+    return line
 
 
 # ---------------------------------------------------------------- prefill ----
@@ -963,10 +993,10 @@ def build_prefill(wl: Workload, device, pool_blocks: int = 0):
     return bm, md, kv, attn, q, k, v, num_blocks
 
 
-def run_prefill_ours(args, world, rank, local):
-    from nano_vllm_ascend_b200 import ops
+def measure_prefill(args, world: int, rank: int, local: int, cpu_seconds: float) -> dict:
+    from nano_vllm_ascend_b200 import check_errors, ops
 
-    wl = WORKLOADS[args.workload]
+    wl = WORKLOADS["prefill_c3"]
     device = torch.device("cuda", local)
     bm, md, kv, attn, q, k, v, num_blocks = build_prefill(wl, device, args.pool_blocks)
     b = wl.batch
@@ -1007,7 +1037,6 @@ def run_prefill_ours(args, world, rank, local):
             t_pf = start.elapsed_time(end) / 1e3 / launches
             if rep == 0 and not args.quick:
                 launches = max(launches, int(0.8 / t_pf))
-        t_app = time_append(kv, bm, device, rows=8192, launches=8 if args.quick else 56)
         for _ in range(args.warmup):
             step()
         barrier_sync(world)
@@ -1040,45 +1069,124 @@ def run_prefill_ours(args, world, rank, local):
         barrier_sync(world)
         t_e2e = start.elapsed_time(end) / 1e3 / args.steps
     clk = clocks.summary()
+    check_errors(device)
+
+    # parity: two requests of the last layer's output (h_out of the last e2e
+    # step) vs fp32 over their 1024 paged keys (6 shared + 2 own blocks)
+    layer, ok, worst = wl.layers - 1, True, 0.0
+    kc, vc = kv.get_physical_cache(layer)
+    for r in spread(b, 2):
+        n = kv_lens[r]
+        kr = _gather_rows(kc, tables[r], n)
+        vr = _gather_rows(vc, tables[r], n)
+        rows = slice(r * wl.ctx_hi, (r + 1) * wl.ctx_hi)
+        want = _attend_fp32(q[layer, rows].float().cpu(), kr, vr, HEAD_DIM ** -0.5, causal_lq=wl.ctx_hi)
+        good, err = _compare(h_out[layer, rows].float(), want)
+        ok, worst = ok and good, max(worst, err)
+    parity = {"parity_ok": ok, "max_abs_err": worst, "layer": layer, "requests_checked": 2,
+              "tolerance": f"|err| <= {ATOL} + {RTOL}*|ref| vs fp32 torch-CPU paged gather + causal softmax"}
+
     t_step_max = max_over_ranks(t_step, world)
     t_e2e_max = max_over_ranks(t_e2e, world)
     flops_all = sum_over_ranks(flops_layer * wl.layers, world)
     peak, kind = peaks("bf16_tflops")
     achieved = flops_layer / t_pf / 1e12
     h2d = sum(t.numel() * t.element_size() for t in (h_q, h_k, h_v))
-    if rank == 0:
-        cpu = None
-        if world == 1 and not args.no_cpu_baseline:
-            cpu = cpu_baseline_prefill(wl, args.cpu_seconds, os.cpu_count() or 1)
-        line = {
-            "metric": "prefix prefill attention TFLOP/s", "value": flops_all / t_step_max / 1e12, "unit": "TFLOP/s",
-            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": t_step_max * 1e3,
-            "higher_is_better": True, "scaling": wl.scaling, "vs_baseline": None, "dtype": "bf16",
-            "data": "synthetic: seeded prompts sharing a 768-token prefix (hash-hit), seeded N(0,1) q/K/V",
-            "config": {"workload": wl.describe, "layers": wl.layers, "global_batch": b * world,
-                       "seq_len": wl.ctx_lo + wl.ctx_hi, "new_tokens": wl.ctx_hi, "cached_prefix": wl.ctx_lo,
-                       "heads": [wl.heads, wl.kv_heads, HEAD_DIM], "block_size": BLOCK, "pool_blocks": num_blocks,
-                       "parallelism": f"request-sharded x{world}, no collective",
-                       "cache": "per step 28 x (8192-row append + 60.16 GFLOP attention)"},
-            "tok_per_s": b * wl.ctx_hi * world / t_step_max,
-            "append": {"gbs": (8192 * wl.kv_heads * HEAD_DIM * 8 + 8192 * 8) / t_app / 1e9, "rows": 8192,
-                       "us": t_app * 1e6},
-            "roofline": {"kernel": "prefill_kernel", "bound": "tensor", "achieved": achieved, "peak": peak,
-                         "peak_kind": kind + " (burst, kernel timed alone)", "unit": "TFLOP/s",
-                         "frac": achieved / peak, "traffic": profiled_traffic(wl.name, "paged_prefill"),
-                         "algorithmic_flops_per_launch": flops_layer,
-                         "us_per_launch": t_pf * 1e6},
-            "e2e": {"value": flops_all / t_e2e_max / 1e12, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d,
-                    "d2h_bytes_per_step": h_out.numel() * h_out.element_size(), "ms_per_step": t_e2e_max * 1e3},
-            "clocks": clk, "gpu_launches": args.steps * wl.layers * 2, "cpu_baseline": cpu,
-        }
-        print(json.dumps(line), flush=True)
-    if world > 1:
-        import torch.distributed as dist
+    line = {
+        "metric": "prefix prefill attention TFLOP/s", "value": flops_all / t_step_max / 1e12, "unit": "TFLOP/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": t_step_max * 1e3,
+        "higher_is_better": True, "scaling": wl.scaling, "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic: seeded prompts sharing a 768-token prefix (hash-hit), seeded N(0,1) q/K/V",
+        "config": prefill_config(wl, world),
+        "setup": {"pool_blocks": num_blocks},
+        "tok_per_s": b * wl.ctx_hi * world / t_step_max,
+        "parity": parity,
+        "roofline": {"kernel": "prefill_kernel", "bound": "tensor", "achieved": achieved, "peak": peak,
+                     "peak_kind": kind + " (burst, kernel timed alone)", "unit": "TFLOP/s",
+                     "frac": achieved / peak, "traffic": profiled_traffic(wl.name, "paged_prefill"),
+                     "tensor_pipe_active_pct_ncu": profiled_value(wl.name, "paged_prefill",
+                                                                  "tensor_pipe_active_pct"),
+                     "algorithmic_flops_per_launch": flops_layer,
+                     "us_per_launch": t_pf * 1e6},
+        "e2e": {"value": flops_all / t_e2e_max / 1e12, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": h_out.numel() * h_out.element_size(), "ms_per_step": t_e2e_max * 1e3},
+        "clocks": clk, "gpu_launches": args.steps * wl.layers * 2, "cpu_baseline": None,
+    }
+    if world == 1 and rank == 0 and cpu_seconds > 0:
+        line["cpu_baseline"] = cpu_baseline_prefill(wl, cpu_seconds, os.cpu_count() or 1)
+    return line
 
-        dist.barrier()
-        dist.destroy_process_group()
-    return 0
+
+def prefill_config(wl: Workload, world: int) -> dict:
+    return {"workload": wl.describe, "layers": wl.layers, "global_batch": wl.batch * world,
+            "seq_len": wl.ctx_lo + wl.ctx_hi, "new_tokens": wl.ctx_hi, "cached_prefix": wl.ctx_lo,
+            "heads": [wl.heads, wl.kv_heads, HEAD_DIM], "block_size": BLOCK,
+            "parallelism": f"request-sharded x{world}, no collective",
+            "cache": "per step 28 x (8192-row append + 60.16 GFLOP attention)"}
+
+
+# ------------------------------------------------------------- CPU legs ----
+class CpuBaseline:
+    """Eager torch-CPU reference path (oracle/cpu_baseline.py) on one layer's
+    worth of this workload: the sequences' blocks in a host pool, this step's
+    append (index_copy_) and decode attention (gather + fp32 softmax). Every
+    layer of a step is identical work, so a step runs layer() once per layer
+    on the same host pool."""
+
+    def __init__(self, wl: Workload, ctx: list[int], threads: int):
+        torch.set_num_threads(threads)
+        self.wl, self.ctx, self.threads = wl, ctx, threads
+        b = len(ctx)
+        g = torch.Generator().manual_seed(0)
+        nblk = [(n + 1 + BLOCK - 1) // BLOCK for n in ctx]
+        nb = sum(nblk)
+        self.kc = torch.randn(nb, BLOCK, wl.kv_heads, HEAD_DIM, generator=g).to(torch.bfloat16)
+        self.vc = torch.randn(nb, BLOCK, wl.kv_heads, HEAD_DIM, generator=g).to(torch.bfloat16)
+        perm = torch.randperm(nb, generator=g).to(torch.int32)
+        self.tables = torch.zeros(b, max(nblk), dtype=torch.int32)
+        self.slots = torch.zeros(b, dtype=torch.int64)
+        used = 0
+        for i, m in enumerate(nblk):
+            self.tables[i, :m] = perm[used : used + m]
+            used += m
+            self.slots[i] = int(self.tables[i, ctx[i] // BLOCK]) * BLOCK + ctx[i] % BLOCK
+        self.q = torch.randn(b, wl.heads, HEAD_DIM, generator=g).to(torch.bfloat16)
+        self.k = torch.randn(b, wl.kv_heads, HEAD_DIM, generator=g).to(torch.bfloat16)
+        self.v = torch.randn(b, wl.kv_heads, HEAD_DIM, generator=g).to(torch.bfloat16)
+        self.ctx_after = torch.tensor([n + 1 for n in ctx], dtype=torch.int32)
+        self.bytes_layer = kv_bytes_per_layer([n + 1 for n in ctx], wl.kv_heads)
+
+    def layer(self) -> None:
+        from oracle import cpu_baseline
+
+        cpu_baseline.append(self.kc, self.vc, self.k, self.v, self.slots)
+        cpu_baseline.decode(self.q, self.kc, self.vc, self.tables, self.ctx_after, HEAD_DIM ** -0.5)
+
+    def step(self) -> None:
+        for _ in range(self.wl.layers):
+            self.layer()
+
+    def time_layers(self, seconds: float, min_layers: int = 1) -> tuple[float, int]:
+        """Runs layer() until ``seconds`` elapsed (at least min_layers); returns (s per layer, layers)."""
+        n = 0
+        t0 = time.perf_counter()
+        while True:
+            self.layer()
+            n += 1
+            el = time.perf_counter() - t0
+            if n >= min_layers and el >= seconds:
+                return el / n, n
+
+
+def cpu_baseline_decode(wl: Workload, ctx: list[int], seconds: float, threads: int) -> dict:
+    base = CpuBaseline(wl, ctx, threads)
+    base.layer()  # warm-up
+    per_layer, n = base.time_layers(seconds)
+    gbs = base.bytes_layer / per_layer / 1e9
+    return {"value": gbs, "unit": "GB/s", "cores": threads, "kind": "port",
+            "sample": f"{n} layer-steps (append + decode attention) of {len(ctx)} seqs on one layer's pool, "
+                      f"{n * per_layer:.1f}s", "ms_per_layer": per_layer * 1e3,
+            "tok_per_s": len(ctx) / (per_layer * wl.layers)}
 
 
 def cpu_baseline_prefill(wl: Workload, seconds: float, threads: int, min_layers: int = 1) -> dict:
@@ -1116,13 +1224,72 @@ def cpu_baseline_prefill(wl: Workload, seconds: float, threads: int, min_layers:
                       f"{el:.1f}s", "ms_per_layer": el / n * 1e3}
 
 
+def run_reference(args, world, rank) -> int:
+    """The reference's path as eager torch-CPU code on the host cores (rank 0
+    only): whole steps of the workload, every layer on the same one-layer
+    host pool, `warmup` untimed steps then `steps` timed ones."""
+    if rank != 0:
+        return 0
+    threads = os.cpu_count() or 1
+    name = args.workload or "decode_c2"
+    wl = WORKLOADS[name]
+    if name.startswith("prefill"):
+        cpu_baseline_prefill(wl, 0.0, threads, min_layers=max(1, args.warmup))
+        r = cpu_baseline_prefill(wl, 0.0, threads, min_layers=args.steps)
+        line = {"impl": "reference", "metric": "prefix prefill attention TFLOP/s", "value": r["value"],
+                "unit": "TFLOP/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+                "ms_per_step": r["ms_per_layer"], "higher_is_better": True, "scaling": wl.scaling,
+                "vs_baseline": None, "dtype": "bf16", "data": "synthetic", "config": prefill_config(wl, world),
+                "cpu_baseline": r,
+                "e2e": {"value": r["value"], "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+        line["cpu_baseline"]["sample"] += "; a step here is one layer"
+        print(json.dumps(line), flush=True)
+        return 0
+    if name not in ("decode_c2", "decode_c4"):
+        print(json.dumps({"impl": "reference", "unavailable": f"no CPU reference leg for workload {name}"}))
+        return 0
+    ctx = rank_contexts(wl, world, 0)
+    base = CpuBaseline(wl, ctx, threads)
+    for _ in range(args.warmup):
+        base.step()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        base.step()
+    per_step = (time.perf_counter() - t0) / args.steps
+    gbs = base.bytes_layer * wl.layers / per_step / 1e9
+    line = {
+        "impl": "reference", "metric": "paged decode-attn KV GB/s", "value": gbs, "unit": "GB/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": per_step * 1e3,
+        "higher_is_better": True, "scaling": wl.scaling, "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic: seeded N(0,1) q/K/V, seeded context lengths and block tables (no weights)",
+        "config": decode_config(wl, world),
+        "tok_per_s": len(ctx) / per_step,
+        "cpu_baseline": {"value": gbs, "unit": "GB/s", "cores": threads, "kind": "port",
+                         "sample": f"{args.steps} whole steps ({wl.layers} x append + decode attention of rank 0's "
+                                   f"{len(ctx)} sequences, each layer on the same one-layer host pool)"},
+        "e2e": {"value": gbs, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ------------------------------------------------------------------ main ----
+def summarize(line: dict) -> dict:
+    """The fields of a workload's line kept in the headline's sub_results."""
+    keep = ("metric", "value", "unit", "n_gpus", "steps", "warmup", "ms_per_step", "scaling", "tok_per_s",
+            "hbm_frac_of_step", "parity", "roofline", "append", "comm", "e2e", "clocks", "per_rank", "config",
+            "gpu_launches", "cpu_baseline")
+    return {k: line[k] for k in keep if k in line}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="decode_c2")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default=None,
+                    help="one workload alone (default: decode_c2 headline with the other configs as sub_results)")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--pool-blocks", type=int, default=0,
@@ -1135,31 +1302,42 @@ def main():
         ap.error("--warmup must be >= 3")
     sys.path.insert(0, str(ROOT))
     world, rank, local = dist_setup(args)
-    prefill = args.workload.startswith("prefill")
     if args.impl == "reference":
-        if prefill:
-            if rank != 0:
-                return 0
-            wl = WORKLOADS[args.workload]
-            threads = os.cpu_count() or 1
-            cpu_baseline_prefill(wl, 0.0, threads, min_layers=max(1, args.warmup // 3))
-            r = cpu_baseline_prefill(wl, 0.0, threads, min_layers=args.steps)
-            print(json.dumps({"impl": "reference", "metric": "prefix prefill attention TFLOP/s", "value": r["value"],
-                              "unit": "TFLOP/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-                              "ms_per_step": r["ms_per_layer"] * wl.layers, "higher_is_better": True,
-                              "scaling": wl.scaling, "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-                              "config": {"workload": wl.describe, "parallelism": "host CPU"}, "cpu_baseline": r,
-                              "e2e": {"value": r["value"], "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
-                                      "d2h_bytes_per_step": 0}}), flush=True)
-            return 0
         return run_reference(args, world, rank)
-    if prefill:
-        return run_prefill_ours(args, world, rank, local)
-    if args.workload == "decode_c5":
-        return run_c5_ours(args, world, rank, local)
-    if args.workload == "kernels":
-        return run_kernels(args, world, rank, local)
-    return run_ours(args, world, rank, local)
+    cpu = world == 1 and not args.no_cpu_baseline
+    try:
+        if args.workload == "kernels":
+            return run_kernels(args, world, rank, local)
+        if args.workload == "decode_c5":
+            line = measure_c5(args, world, rank, local, args.gather)
+        elif args.workload == "prefill_c3":
+            line = measure_prefill(args, world, rank, local, args.cpu_seconds if cpu else 0.0)
+        elif args.workload is not None:
+            line = measure_decode(args, WORKLOADS[args.workload], world, rank, local, with_cpu=cpu)
+        else:
+            line = measure_decode(args, WORKLOADS["decode_c2"], world, rank, local, with_cpu=cpu)
+            subs = {}
+            free_device_memory()
+            if world == 1:
+                subs["prefill_c3"] = summarize(measure_prefill(args, world, rank, local,
+                                                               min(args.cpu_seconds, 4.0) if cpu else 0.0))
+                free_device_memory()
+            subs["decode_c4"] = summarize(measure_decode(args, WORKLOADS["decode_c4"], world, rank, local,
+                                                         with_cpu=False))
+            if world > 1 and KVH % world == 0:
+                free_device_memory()
+                subs["decode_c5"] = summarize(measure_c5(args, world, rank, local, "kernel"))
+            line["sub_results"] = subs
+        if rank == 0:
+            print(json.dumps(line), flush=True)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+
+            if dist.is_initialized():
+                dist.barrier()
+                dist.destroy_process_group()
+    return 0
 
 
 if __name__ == "__main__":
