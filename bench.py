@@ -8,7 +8,8 @@
 Without --workload (what the driver runs) one JSON line is printed whose
 headline is config 2 (decode_c2) and whose ``sub_results`` carry the other
 configs measured in the same run, one after another on the same GPUs:
-prefill_c3 and decode_c4 at N = 1; decode_c4 and decode_c5 at N > 1. Every
+prefill_c3, decode_c4 and step_c2 at N = 1; decode_c4, step_c2 and decode_c5
+at N > 1. Every
 workload first measures, then checks a sampled slice of its own output on the
 box against an fp32 torch-CPU reference (``parity``), so each number is
 backed by a parity verdict of the same run. --workload X prints X alone.
@@ -39,6 +40,12 @@ Workloads (seeded synthetic inputs with the configs' shapes; no model weights):
       into every rank's gathered [128, 32, 128] output (in-kernel all-gather
       over NVLink, --gather kernel) or, as the baseline, decode followed by an
       NCCL all_gather_into_tensor and a permuting copy (--gather nccl).
+  step_c2: config 2 through StepRunner (the reference's ModelRunner step
+      drivers): a Qwen3-0.6B-shaped model with seeded random weights, 32
+      sequences prefilled to context ~U[256, 2304], then greedy decode steps
+      from one CUDA graph (device metadata, 28 layers of fused q/k norm + RoPE
+      + append, paged decode, cuBLAS projections and MLP, LM head + argmax)
+      with the next tokens read back every step; value = decode tok/s.
   kernels: the path's other kernels timed one by one under CUDA graphs on
       config-sized inputs (prefill-sized append, decode- and prefill-sized
       q/k norm + RoPE + append, device decode metadata, LM head + greedy
@@ -651,6 +658,125 @@ def measure_decode(args, wl: Workload, world: int, rank: int, local: int, with_c
     if with_cpu and rank == 0:
         line["cpu_baseline"] = cpu_baseline_decode(wl, ctx, seconds=args.cpu_seconds, threads=os.cpu_count() or 1)
     return line
+
+
+# ---------------------------------------------------------- model step ----
+def _step_reference_logits(model, tokens: torch.Tensor) -> torch.Tensor:
+    """fp32-attention torch recompute of one sequence through the step's model
+    (same weights and dense ops): logits of its last position."""
+    import torch.nn.functional as F
+
+    from nano_vllm_ascend_b200.step_runner import _rms_norm
+
+    s = model.shape
+    ids = tokens.to(model.device)
+    n = ids.numel()
+    pos = torch.arange(n, device=model.device)
+    c = model.cos[pos].to(torch.bfloat16).float()[:, None]
+    sn = model.sin[pos].to(torch.bfloat16).float()[:, None]
+
+    def norm_rope(x, w):
+        xf = x.float()
+        y = (xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + s.rms_norm_eps) * w.float()).to(torch.bfloat16)
+        y = y.float()
+        half = y.shape[-1] // 2
+        return (y * c + torch.cat([-y[..., half:], y[..., :half]], dim=-1) * sn).to(torch.bfloat16)
+
+    g = s.num_heads // s.num_kv_heads
+    causal = torch.ones(n, n, dtype=torch.bool, device=model.device).tril()
+    x = model.embed[ids]
+    for layer in model.layers:
+        h = _rms_norm(x, layer.in_norm, s.rms_norm_eps)
+        qkv = F.linear(h, layer.qkv).view(n, -1, s.head_dim)
+        q = norm_rope(qkv[:, :s.num_heads], layer.q_norm)
+        k = norm_rope(qkv[:, s.num_heads:s.num_heads + s.num_kv_heads], layer.k_norm)
+        v = qkv[:, s.num_heads + s.num_kv_heads:]
+        sc = torch.einsum("tkgd,nkd->kgtn", q.float().view(n, s.num_kv_heads, g, -1), k.float()) * s.head_dim ** -0.5
+        p = torch.softmax(sc.masked_fill(~causal, float("-inf")), dim=-1)
+        x = x + F.linear(torch.einsum("kgtn,nkd->tkgd", p, v.float()).reshape(n, -1).to(torch.bfloat16), layer.o)
+        h = _rms_norm(x, layer.post_norm, s.rms_norm_eps)
+        gate, up = F.linear(h, layer.gate_up).chunk(2, dim=-1)
+        x = x + F.linear(F.silu(gate) * up, layer.down)
+    return _rms_norm(x, model.final_norm, s.rms_norm_eps)[-1].float() @ model.embed.float().T
+
+
+def measure_step(args, world: int, rank: int, local: int) -> dict:
+    """Config 2 through StepRunner (the reference's ModelRunner step drivers):
+    a Qwen3-0.6B-shaped model with seeded random weights, 32 sequences per
+    rank prefilled to context ~U[256, 2304] from random token ids (as the
+    reference's bench_compare.py draws its prompts), then greedy decode steps
+    at batch 32 from one CUDA graph: device-side metadata, the 28 layers
+    (fused q/k norm + RoPE + append, paged decode, cuBLAS projections and
+    MLP), LM head + argmax, and the next token ids read back every step."""
+    from nano_vllm_ascend_b200.step_runner import ModelShape, StepRunner, StepSequence
+
+    wl = WORKLOADS["decode_c2"]
+    device = torch.device("cuda", local)
+    ctx = rank_contexts(wl, world, rank)
+    b = len(ctx)
+    max_len = wl.ctx_hi + args.warmup + args.steps + 8
+    runner = StepRunner(ModelShape(), device, max_model_len=max_len, max_num_seqs=b, decode_graph_batch_sizes=[b],
+                        seed=100 + rank)
+    g = torch.Generator().manual_seed(2000 + rank)
+    seqs = [StepSequence(i, torch.randint(0, 10000, (n,), generator=g)) for i, n in enumerate(ctx)]
+    runner.prepare_sequences(seqs)
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    runner.prefill(seqs)  # reads the tokens back: synchronous
+    t_prefill = time.perf_counter() - t0
+    stream = torch.cuda.current_stream(device)
+    with ClockSampler(local) as clocks:
+        for _ in range(args.warmup):
+            runner.decode(seqs)
+        barrier_sync(world)
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        w0 = time.perf_counter()
+        start.record(stream)
+        for _ in range(args.steps):
+            runner.decode(seqs)
+        end.record(stream)
+        barrier_sync(world)
+        wall = (time.perf_counter() - w0) / args.steps
+        t_step = start.elapsed_time(end) / 1e3 / args.steps
+    clk = clocks.summary()
+    # parity: two sequences recomputed from scratch; each picked token must be
+    # a greedy choice of the recompute's logits (bf16 may reorder near-ties)
+    ok, worst = True, 0.0
+    for seq in (seqs[0], seqs[-1]):
+        logits = _step_reference_logits(runner.model, seq.token_ids())
+        gap = float(logits.max() - logits[seq.next_token_id])
+        ok, worst = ok and gap <= 5e-2, max(worst, gap)
+    parity = {"parity_ok": _reduce(1.0 if ok else 0.0, world, "min") > 0.5,
+              "max_logit_gap": max_over_ranks(worst, world), "sequences_checked": 2,
+              "tolerance": "each sequence's last greedy token within 0.05 of the max logit of a torch recompute "
+                           "(fp32 attention, same weights and dense ops) of its whole history"}
+    stats = runner.decode_graph_stats()
+    runner.release()
+    t_step_max = max_over_ranks(t_step, world)
+    seqs_all = sum_over_ranks(float(b), world)
+    ctx_now = [c + args.warmup + args.steps for c in ctx]
+    kv_step = kv_bytes_per_layer(ctx_now, wl.kv_heads) * wl.layers
+    return {
+        "metric": "decode tok/s (Qwen3-0.6B-shaped step, greedy, through StepRunner)",
+        "value": seqs_all / t_step_max, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": t_step_max * 1e3, "scaling": "weak",
+        "config": {"workload": "config[1] through the model step: Qwen3-0.6B shapes (28 layers, hidden 1024, "
+                               "MLP 3072, vocab 151936, tied LM head), random weights, 32 seqs per GPU, "
+                               "ctx~U[256,2304], CUDA graph bs 32",
+                   "batch_per_gpu": b, "global_batch": int(seqs_all)},
+        "parity": parity,
+        "e2e": {"value": seqs_all / max_over_ranks(wall, world), "unit": "tok/s",
+                "h2d_bytes_per_step": 2 * 8 * b, "d2h_bytes_per_step": 8 * b,
+                "ms_per_step_wall": wall * 1e3, "note": "every step crosses token ids + positions in and the "
+                                                        "next token ids out, and waits for them"},
+        "kv_gbs_of_step": kv_bytes_per_layer(ctx_now, wl.kv_heads) * wl.layers / t_step_max / 1e9 * world,
+        "prefill_tok_per_s": sum(ctx) / t_prefill,
+        "graph_stats": stats,
+        "clocks": clk,
+        "vs_reference_published": {"value": 1296.05, "unit": "output tok/s",
+                                   "what": "the reference on an Ascend 910B3, 32 x 256 in / 2048 out, whole run "
+                                           "(bench_outputs/nano_32x256_2048.json)"},
+    }
 
 
 # ------------------------------------------------------------- kernels ----
@@ -1288,7 +1414,7 @@ def main():
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=sorted(WORKLOADS), default=None,
+    ap.add_argument("--workload", choices=sorted(WORKLOADS) + ["step_c2"], default=None,
                     help="one workload alone (default: decode_c2 headline with the other configs as sub_results)")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -1310,6 +1436,8 @@ def main():
             return run_kernels(args, world, rank, local)
         if args.workload == "decode_c5":
             line = measure_c5(args, world, rank, local, args.gather)
+        elif args.workload == "step_c2":
+            line = measure_step(args, world, rank, local)
         elif args.workload == "prefill_c3":
             line = measure_prefill(args, world, rank, local, args.cpu_seconds if cpu else 0.0)
         elif args.workload is not None:
@@ -1324,6 +1452,8 @@ def main():
                 free_device_memory()
             subs["decode_c4"] = summarize(measure_decode(args, WORKLOADS["decode_c4"], world, rank, local,
                                                          with_cpu=False))
+            free_device_memory()
+            subs["step_c2"] = measure_step(args, world, rank, local)
             if world > 1 and KVH % world == 0:
                 free_device_memory()
                 subs["decode_c5"] = summarize(measure_c5(args, world, rank, local, "kernel"))

@@ -47,6 +47,7 @@ from typing import Any, Iterator
 import torch
 
 from . import device_errors
+from .block_manager import PagedKVCacheMetadata
 
 # The slot whose warm-up or capture is running (at most one at a time).
 _recording: "GraphSlot | None" = None
@@ -128,9 +129,11 @@ class GraphSlot:
             self.workspace = torch.zeros(max(nbytes, 1), dtype=torch.uint8, device=self.device)
         return self.workspace
 
-    def metadata(self, like):
-        """The step metadata as the graph sees it (the static buffers), in ``like``'s type."""
-        return type(like)(
+    def metadata(self, like=None):
+        """The step metadata as the graph sees it (the static buffers), in the type of
+        ``like`` (default PagedKVCacheMetadata). Metadata built on the device can be
+        written straight into it (DeviceBlockTables.prepare_decode_metadata(out=...))."""
+        return (PagedKVCacheMetadata if like is None else type(like))(
             block_tables=self.block_tables,
             context_lens=self.context_lens,
             slot_mapping=self.slot_mapping,

@@ -101,6 +101,11 @@ class DeviceErrorState:
         self._words.pop(name, None)
         self._dirty.discard(name)
 
+    def mark(self, *names: str) -> None:
+        """Records that launches wrote these words (default: the shared word) without
+        starting a read; the next ``launched`` or ``check`` reads them."""
+        self._dirty.update(names or (SHARED,))
+
     def launched(self, *names: str) -> None:
         """Marks words as written by launches just enqueued on the current stream
         (default: the shared word) and starts a non-blocking read if none is in flight."""

@@ -59,12 +59,18 @@ class DeviceBlockTables:
         return host, view, event
 
     def prepare_decode_metadata(self, slots: list[int], start_positions: list[int], q_len: int,
-                                width: int | None = None) -> PagedKVCacheMetadata:
+                                width: int | None = None, out=None) -> PagedKVCacheMetadata:
         """Same contract as BlockManager.prepare_decode_metadata; the tensors are built on the device.
 
         ``width`` pads the block tables to a fixed number of columns (e.g. the
         CUDA-graph runner's ceil(max_model_len / block_size)); default: the
         longest table of the batch, as the host path does.
+
+        ``out`` (a metadata object whose block_tables [batch, W] int32 with
+        unit column stride, context_lens int32 [batch] and slot_mapping int64
+        [batch * q_len] live on this device) receives the results in place --
+        a decode graph's static buffers, so that nothing is copied before its
+        replay; the tables are then padded to W columns and ``out`` is returned.
         """
         if len(slots) != len(start_positions):
             raise ValueError("slots and start_positions length mismatch")
@@ -122,6 +128,15 @@ class DeviceBlockTables:
                 ns.append(n)
         b, m = len(slots), len(idx)
         width = width or widest
+        if out is not None:
+            ot, oc, os_ = out.block_tables, out.context_lens, out.slot_mapping
+            if ot.dtype != torch.int32 or ot.dim() != 2 or ot.shape[0] != b or ot.stride(1) != 1 \
+                    or ot.shape[1] < widest or oc.dtype != torch.int32 or oc.numel() != b or not oc.is_contiguous() \
+                    or os_.dtype != torch.int64 or os_.numel() != b * q_len or not os_.is_contiguous() \
+                    or any(t.device != self.device for t in (ot, oc, os_)):
+                raise ValueError("prepare_decode_metadata: out buffers must be int32 [batch, >= widest table] / "
+                                 "int32 [batch] / int64 [batch * q_len] on the mirror's device")
+            width = ot.shape[1]
         # device buffer, int64 words: staged inputs int32 [slots | offsets | idx | blk | ctxs | ns]
         # (even length) and int64 starts; then the outputs: int32 tables [b, width], int32 context
         # lengths, int64 slots
@@ -134,21 +149,28 @@ class DeviceBlockTables:
         view.view(np.int32)[:n32] = list(slots) + offsets + idx + blk + ctxs + ns
         view[w_in32:w_in] = start_positions
         stream = torch.cuda.current_stream(self.device)
-        buf = torch.empty(w_in + w_tab + w_ctx + b * q_len, dtype=torch.int64, device=self.device)
+        words = w_in if out is not None else w_in + w_tab + w_ctx + b * q_len
+        buf = torch.empty(words, dtype=torch.int64, device=self.device)
         buf[:w_in].copy_(host[:w_in], non_blocking=True)
         event.record(stream)
-        out32 = buf[w_in:w_in + w_tab + w_ctx].view(torch.int32)
-        block_tables = out32[:b * width].view(b, width)
-        context_lens = out32[2 * w_tab:2 * w_tab + b]
-        slot_mapping = buf[w_in + w_tab + w_ctx:]
+        if out is not None:
+            block_tables, context_lens, slot_mapping = out.block_tables, out.context_lens, out.slot_mapping
+            tab_stride = block_tables.stride(0)
+        else:
+            out32 = buf[w_in:w_in + w_tab + w_ctx].view(torch.int32)
+            block_tables = out32[:b * width].view(b, width)
+            context_lens = out32[2 * w_tab:2 * w_tab + b]
+            slot_mapping = buf[w_in + w_tab + w_ctx:]
+            tab_stride = width
         base = buf.data_ptr()
         p_off = base + 4 * b
         p_idx = p_off + 4 * (b + 1)
         p_ctx = p_idx + 8 * m
-        p_tab = base + 8 * w_in
         _lib.check("nvk_decode_metadata", self._fn(
             self.mirror.data_ptr(), cols, rows, base, base + 8 * w_in32, p_ctx, p_ctx + 4 * b, b, q_len, bs,
-            p_off, p_idx, p_idx + 4 * m, p_tab, width, width, p_tab + 8 * w_tab, p_tab + 8 * (w_tab + w_ctx),
-            self.error_word.data_ptr(), stream.cuda_stream))
+            p_off, p_idx, p_idx + 4 * m, block_tables.data_ptr(), tab_stride, width, context_lens.data_ptr(),
+            slot_mapping.data_ptr(), self.error_word.data_ptr(), stream.cuda_stream))
         synced.update(sending)  # after the launch: a refused launch leaves the record as it was
+        if out is not None:
+            return out
         return PagedKVCacheMetadata(block_tables=block_tables, context_lens=context_lens, slot_mapping=slot_mapping)
