@@ -8,27 +8,33 @@
 // lengths. Masking is bottom-right aligned: query i of a sequence with Lq
 // queries and Lk keys sees key j iff j <= Lk - Lq + i.
 //
-// One CTA = 128 query rows of one sequence x one query head; two CTAs share
-// an SM (96 KB of shared memory and 256 TMEM columns each), so that one
-// CTA's softmax runs while the other's MMAs do.
-//   warp 4 (producer): TMA loads of the Q tile once, then 64-key K and V
-//     tiles (half a pool block each, 128-byte swizzle = the canonical UMMA
-//     operand layout): K into a 2-stage ring freed as soon as S has read it,
-//     V into a 2-stage ring freed by PV; K runs two tiles ahead of V, and
-//     the block ids come 32 at a time (one parallel load per warp).
-//   warp 5 (MMA): allocates 256 TMEM columns (S/P double buffered: 0-63,
-//     64-127; O: 128-255) and one lane issues S = Q K^T (8 x M128 N64 K16,
-//     both K-major) one key tile ahead of O += P V (4 x M128 N128 K16, P read
-//     from TMEM where the softmax wrote it over S(j), V MN-major from smem),
-//     so the tensor core computes S(j+1) while the softmax warps work on
-//     tile j; S(j+2) reuses the columns of P(j) and so waits for P V(j);
-//     tcgen05.commit signals the mbarriers.
-//   warps 0-3 (softmax): thread r owns query row r = TMEM lane r: loads its
-//     S row in two halves (tcgen05.ld), masks, base-2 online softmax with
-//     lazy rescaling of O in TMEM (only when the running max grows by more
-//     than 2^8), packed f32x2 exponent arguments and row sums, writes P as
-//     bf16 pairs into the first 32 columns of its S buffer (tcgen05.st),
-//     and at the end normalises its O row and stores it.
+// One CTA = 128 query rows of one sequence x TWO query heads of one GQA
+// group ("streams" 0 and 1; one stream when the group size is odd), one CTA
+// per SM. Both streams read the same 128-key K and V tiles (one pool block
+// each), so every K/V byte staged in shared memory feeds two heads.
+// Tensor memory (all 512 columns): S/P of stream s at columns s*128, its O
+// accumulator at 256 + s*128.
+//   warp 8 (producer): TMA loads of the two Q tiles once, then per key tile
+//     the K and the V tile (two 64-dim halves each, 128-byte swizzle = the
+//     canonical UMMA operand layout) into 2-stage rings; block ids 32 at a
+//     time (one parallel load per warp).
+//   warp 9 (MMA, one elected lane): S_s(0) = Q_s K(0)^T for both streams,
+//     then per tile j and stream s: wait for P_s(j), issue O_s += P_s(j) V(j)
+//     (P read from TMEM where the softmax wrote it over S_s, V MN-major from
+//     smem) and right behind it S_s(j+1) = Q_s K(j+1)^T into the same
+//     columns. tcgen05.mma executes in issue order, so S_s(j+1) overwrites
+//     P_s(j) only after the P V has read it, and the tensor pipe always has
+//     the other stream's work queued while one stream's softmax runs.
+//   warps 0-3 / 4-7 (softmax of stream 0 / 1): thread r owns query row r =
+//     TMEM lane r: takes the max of its 128-key S row (tcgen05.ld of two
+//     64-column halves), masks, base-2 online softmax with lazy rescaling of
+//     O (only when the running max grows by more than 2^8; S_s(j) having
+//     landed means P V(j-1) is done, so O may be rescaled at once), then per
+//     half again the exponentials, written as bf16 pairs into the first 64
+//     columns of its S (tcgen05.st), and at the end normalises its O row and
+//     stores it.
+// Ten warps put three on one SM sub-partition, whose register file holds
+// 3 x 32 x 168 registers: the kernel is held to 168 registers a thread.
 // Every mbarrier wait is bounded; on a timeout the CTA records the error,
 // drains its in-flight copies and MMAs, frees TMEM and exits.
 #include "host_common.h"
@@ -39,21 +45,17 @@ namespace nvk {
 namespace {
 
 constexpr int kD = 128;
-constexpr int kRows = 128;                   // query rows per CTA
-constexpr int kKeys = 64;                    // keys per K/V tile (half a 128-token pool block)
-constexpr int kQHalfBytes = kRows * 128;     // one 64-dim half of the Q tile
-constexpr int kQTileBytes = 2 * kQHalfBytes;
-constexpr int kKVHalfBytes = kKeys * 128;    // one 64-dim half of a K or V tile
-constexpr int kKVTileBytes = 2 * kKVHalfBytes;
-constexpr int kKStages = 2;
-constexpr int kVStages = 2;
-constexpr int kSoftmaxThreads = 128;
-constexpr int kProducerWarp = 4;
-constexpr int kMmaWarp = 5;
-constexpr int kThreads = 6 * 32;
-constexpr int kSBufs = 2;            // S/P buffers in TMEM
-constexpr uint32_t kTmemCols = 256;  // S0, S1 (64 columns each), O (128): two CTAs share an SM's 512
-constexpr int kCtasPerSm = 2;        // two softmax warpgroups per SM hide each other's latency
+constexpr int kRows = 128;                // query rows per CTA (UMMA M)
+constexpr int kKeys = 128;                // keys per K/V tile: one 128-token pool block
+constexpr int kHalfBytes = 128 * 128;     // one 64-dim half of a 128-row tile
+constexpr int kTileBytes = 2 * kHalfBytes;
+constexpr int kStages = 2;                // K and V ring depth
+constexpr int kStreams = 2;               // query heads per CTA
+constexpr int kStreamThreads = 128;       // softmax threads per stream
+constexpr int kProducerWarp = 8;
+constexpr int kMmaWarp = 9;
+constexpr int kThreads = 10 * 32;
+constexpr uint32_t kTmemCols = 512;       // S0 | S1 | O0 | O1, 128 columns each
 constexpr float kRescaleThreshold = 8.0f;
 
 struct PrefillArgs {
@@ -67,39 +69,40 @@ struct PrefillArgs {
   int num_blocks;
   int num_heads;
   int qpk;
+  int paired;  // two heads per CTA (qpk even)
   int paged;
   float scale_log2;
 };
 
 struct PrefillSmem {
-  alignas(1024) uint8_t q[kQTileBytes];
-  alignas(1024) uint8_t k[kKStages][kKVTileBytes];
-  alignas(1024) uint8_t v[kVStages][kKVTileBytes];
+  alignas(1024) uint8_t q[kStreams][kTileBytes];
+  alignas(1024) uint8_t k[kStages][kTileBytes];
+  alignas(1024) uint8_t v[kStages][kTileBytes];
   uint64_t bar_q;
-  uint64_t full_k[kKStages], k_empty[kKStages];
-  uint64_t full_v[kVStages], v_empty[kVStages];
-  uint64_t s_full[kSBufs];
-  uint64_t p_full[kSBufs];   // P(j) written into S buffer j % 2
-  uint64_t pv_done[kSBufs];  // PV(j) complete (S buffer j % 2 free again)
+  uint64_t full_k[kStages], k_empty[kStages];
+  uint64_t full_v[kStages], v_empty[kStages];
+  uint64_t s_full[kStreams];  // S_s(j) in TMEM (and, in issue order, P V_s(j-1) done)
+  uint64_t p_full[kStreams];  // P_s(j) written by the stream's 128 softmax threads
+  uint64_t o_done[kStreams];  // O_s += P_s(j) V(j) complete
   uint64_t fin;
   uint32_t tmem_base;
   volatile int abort;
 };
 
-static_assert(kCtasPerSm * (sizeof(PrefillSmem) + 1024 + 1024) <= 233472,
-              "prefill shared memory does not let two CTAs share an SM");
+static_assert(sizeof(PrefillSmem) + 1024 <= 232448, "prefill shared memory exceeds one SM's 227 KB");
 
 __device__ __forceinline__ void flag_error(const PrefillArgs& a, PrefillSmem& sm, int code) {
   if (a.err) atomicOr(a.err, code);
   sm.abort = 1;
 }
 
-__global__ void __launch_bounds__(kThreads, kCtasPerSm) prefill_kernel(const __grid_constant__ CUtensorMap qmap,
-                                                              const __grid_constant__ CUtensorMap kmap,
-                                                              const __grid_constant__ CUtensorMap vmap,
-                                                              const PrefillArgs a) {
+__global__ void __maxnreg__(168) prefill_kernel(const __grid_constant__ CUtensorMap qmap,
+                                                const __grid_constant__ CUtensorMap kmap,
+                                                const __grid_constant__ CUtensorMap vmap, const PrefillArgs a) {
   const int qt = gridDim.x - 1 - blockIdx.x;  // heaviest (last) query tiles first
-  const int h = blockIdx.y, b = blockIdx.z;
+  const int b = blockIdx.z;
+  const int nstreams = a.paired ? 2 : 1;
+  const int h0 = blockIdx.y * nstreams;  // query heads h0 .. h0 + nstreams - 1, one KV group
   pdl_launch_dependents();
   pdl_wait();
   const int q0 = a.cu_q[b];
@@ -107,15 +110,18 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) prefill_kernel(const __g
   if (qt * kRows >= lq) return;
   const int lk = a.paged ? a.kv_lens[b] : (a.cu_kv[b + 1] - a.cu_kv[b]);
   const int kv_row0 = a.paged ? 0 : a.cu_kv[b];
-  const int g = h / a.qpk;
+  const int g = h0 / a.qpk;
   const int i_last = min(qt * kRows + kRows - 1, lq - 1);
   const int lim_last = min(lk - lq + i_last, lk - 1);
-  const int n_kv = lim_last < 0 ? 0 : lim_last / kKeys + 1;  // 64-key tiles
+  const int n_kv = lim_last < 0 ? 0 : lim_last / kKeys + 1;  // 128-key tiles
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int stream = warp >> 2;                  // softmax warps 0-3 / 4-7
+  const int r = tid & (kStreamThreads - 1);      // query row within the tile = TMEM lane
+  const int i = qt * kRows + r;                  // query row within the sequence
   __nv_bfloat16* out_row = nullptr;
-  const int i = qt * kRows + tid;  // query row within the sequence (softmax threads)
-  if (tid < kSoftmaxThreads && i < lq) out_row = a.out + (static_cast<int64_t>(q0 + i) * a.num_heads + h) * kD;
+  if (warp < 8 && stream < nstreams && i < lq)
+    out_row = a.out + (static_cast<int64_t>(q0 + i) * a.num_heads + h0 + stream) * kD;
 
   if (n_kv == 0) {  // no visible key for any row of this tile: zeros
     if (out_row) {
@@ -130,18 +136,16 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) prefill_kernel(const __g
 
   if (tid == 0) {
     mbar_init(&sm.bar_q, 1);
-    for (int s = 0; s < kKStages; ++s) {
+    for (int s = 0; s < kStages; ++s) {
       mbar_init(&sm.full_k[s], 1);
       mbar_init(&sm.k_empty[s], 1);
-    }
-    for (int s = 0; s < kVStages; ++s) {
       mbar_init(&sm.full_v[s], 1);
       mbar_init(&sm.v_empty[s], 1);
     }
-    for (int i = 0; i < kSBufs; ++i) {
-      mbar_init(&sm.s_full[i], 1);
-      mbar_init(&sm.p_full[i], kSoftmaxThreads);
-      mbar_init(&sm.pv_done[i], 1);
+    for (int s = 0; s < kStreams; ++s) {
+      mbar_init(&sm.s_full[s], 1);
+      mbar_init(&sm.p_full[s], kStreamThreads);
+      mbar_init(&sm.o_done[s], 1);
     }
     mbar_init(&sm.fin, 1);
     sm.abort = 0;
@@ -155,193 +159,178 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) prefill_kernel(const __g
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = sm.tmem_base;
-  const uint32_t tmem_s = tmem;            // S(j), then P(j), in columns (j % 2) * 64
-  const uint32_t tmem_o = tmem + kSBufs * kKeys;
 
   if (warp == kProducerWarp) {
     // -------------------------------------------------------- producer ----
-    // The whole warp walks the tiles (block ids come 32 at a time, one per
-    // lane); lane 0 waits for ring slots and issues the copies.
     if (lane == 0) {
       tma_prefetch_desc(&qmap);
       tma_prefetch_desc(&kmap);
       tma_prefetch_desc(&vmap);
-      mbar_arrive_expect_tx(&sm.bar_q, kQTileBytes);
-      tma_load_3d(sm.q, &qmap, &sm.bar_q, 0, h, q0 + qt * kRows);
-      tma_load_3d(sm.q + kQHalfBytes, &qmap, &sm.bar_q, 64, h, q0 + qt * kRows);
+      mbar_arrive_expect_tx(&sm.bar_q, nstreams * kTileBytes);
+      for (int s = 0; s < nstreams; ++s) {
+        tma_load_3d(sm.q[s], &qmap, &sm.bar_q, 0, h0 + s, q0 + qt * kRows);
+        tma_load_3d(sm.q[s] + kHalfBytes, &qmap, &sm.bar_q, 64, h0 + s, q0 + qt * kRows);
+      }
     }
     const int32_t* bt = a.block_tables + static_cast<int64_t>(b) * a.bt_stride;
-    // First pool row of 64-key tile j (tile j is half j & 1 of block j / 2);
-    // `chunk` holds this lane's block id for tile j & ~31 + lane and is
-    // refreshed when j crosses a multiple of 32 (each caller passes its own
-    // register and consecutive j).
-    auto row_of = [&](int j, int& chunk) -> int {
-      if ((j & 31) == 0) {
+    int ids = 0, k_issued = 0, v_issued = 0;
+    bool ok = true;
+    for (int j = 0; j < n_kv; ++j) {
+      // warp-uniform stop decision (lane 0's view of the abort flag)
+      if (__shfl_sync(0xffffffffu, (ok ? 0 : 1) | sm.abort, 0)) break;
+      if ((j & 31) == 0 && a.paged) {  // block ids of tiles j .. j+31, one per lane
         const int jj = j + lane;
         int blk = 0;
-        if (a.paged && jj < n_kv) {
-          blk = bt[jj >> 1];
+        if (jj < n_kv) {
+          blk = bt[jj];
           if (blk < 0 || blk >= a.num_blocks) {
             if (a.err) atomicOr(a.err, kErrBadBlockId);
             blk = a.num_blocks;  // fully outside the tensor map: zero fill
           }
         }
-        chunk = blk;
+        ids = blk;
       }
-      const int blk = __shfl_sync(0xffffffffu, chunk, j & 31);
-      return a.paged ? blk * kRows + (j & 1) * kKeys : kv_row0 + j * kKeys;
-    };
-    int k_chunk = 0, v_chunk = 0, k_issued = 0, v_issued = 0;
-    bool ok = true;
-    auto load_k = [&](int j) {
-      const int row = row_of(j, k_chunk);
-      const int st = j % kKStages;
+      const int blk = __shfl_sync(0xffffffffu, ids, j & 31);
+      const int row = a.paged ? blk * kKeys : kv_row0 + j * kKeys;
+      const int st = j % kStages;
       if (lane == 0) {
-        if (j >= kKStages && !mbar_wait(&sm.k_empty[st], ((j / kKStages) - 1) & 1)) {
+        if (j >= kStages && !mbar_wait(&sm.k_empty[st], ((j / kStages) - 1) & 1)) {
           ok = false;
         } else {
-          mbar_arrive_expect_tx(&sm.full_k[st], kKVTileBytes);
+          mbar_arrive_expect_tx(&sm.full_k[st], kTileBytes);
           tma_load_3d(sm.k[st], &kmap, &sm.full_k[st], 0, g, row);
-          tma_load_3d(sm.k[st] + kKVHalfBytes, &kmap, &sm.full_k[st], 64, g, row);
+          tma_load_3d(sm.k[st] + kHalfBytes, &kmap, &sm.full_k[st], 64, g, row);
+          ++k_issued;
+          if (j >= kStages && !mbar_wait(&sm.v_empty[st], ((j / kStages) - 1) & 1)) {
+            ok = false;
+          } else {
+            mbar_arrive_expect_tx(&sm.full_v[st], kTileBytes);
+            tma_load_3d(sm.v[st], &vmap, &sm.full_v[st], 0, g, row);
+            tma_load_3d(sm.v[st] + kHalfBytes, &vmap, &sm.full_v[st], 64, g, row);
+            ++v_issued;
+          }
         }
       }
       ok = __shfl_sync(0xffffffffu, ok, 0);
-      k_issued += ok ? 1 : 0;
-    };
-    auto load_v = [&](int j) {
-      const int row = row_of(j, v_chunk);
-      const int st = j % kVStages;
-      if (lane == 0) {
-        if (j >= kVStages && !mbar_wait(&sm.v_empty[st], ((j / kVStages) - 1) & 1)) {
-          ok = false;
-        } else {
-          mbar_arrive_expect_tx(&sm.full_v[st], kKVTileBytes);
-          tma_load_3d(sm.v[st], &vmap, &sm.full_v[st], 0, g, row);
-          tma_load_3d(sm.v[st] + kKVHalfBytes, &vmap, &sm.full_v[st], 64, g, row);
-        }
-      }
-      ok = __shfl_sync(0xffffffffu, ok, 0);
-      v_issued += ok ? 1 : 0;
-    };
-    for (int j = 0; ok && j < 2 && j < n_kv; ++j) load_k(j);
-    for (int t = 0; ok && t < n_kv && !sm.abort; ++t) {
-      if (t + 2 < n_kv) load_k(t + 2);
-      if (ok) load_v(t);
     }
     if (lane == 0) {
       if (!ok) flag_error(a, sm, kErrWaitTimeout);
       // Drain every copy this CTA issued before it may exit.
       (void)mbar_wait(&sm.bar_q, 0);
-      for (int j = max(0, k_issued - kKStages); j < k_issued; ++j)
-        (void)mbar_wait(&sm.full_k[j % kKStages], (j / kKStages) & 1);
-      for (int j = max(0, v_issued - kVStages); j < v_issued; ++j)
-        (void)mbar_wait(&sm.full_v[j % kVStages], (j / kVStages) & 1);
+      for (int j = max(0, k_issued - kStages); j < k_issued; ++j)
+        (void)mbar_wait(&sm.full_k[j % kStages], (j / kStages) & 1);
+      for (int j = max(0, v_issued - kStages); j < v_issued; ++j)
+        (void)mbar_wait(&sm.full_v[j % kStages], (j / kStages) & 1);
     }
   } else if (warp == kMmaWarp) {
     // ------------------------------------------------------------- MMA ----
     if (lane == 0) {
       constexpr uint32_t idesc_qk = umma_idesc_bf16(kRows, kKeys, false);
       constexpr uint32_t idesc_pv = umma_idesc_bf16(kRows, kD, true);
-      const uint32_t q_addr = smem_u32(sm.q);
-      bool ok = mbar_wait(&sm.bar_q, 0);
-      if (!ok) flag_error(a, sm, kErrWaitTimeout);
-      // S(j) = Q K(j)^T into S buffer j % 2, once K(j) has landed and PV(j-2)
-      // has read P(j-2) out of that buffer.
-      auto issue_s = [&](int j) -> bool {
-        const int s = j % kSBufs, ks = j % kKStages;
-        if (!mbar_wait(&sm.full_k[ks], (j / kKStages) & 1)) return false;
-        if (j >= kSBufs && !mbar_wait(&sm.pv_done[s], ((j / kSBufs) - 1) & 1)) return false;
-        tc_fence_after();
-        const uint32_t k_addr = smem_u32(sm.k[ks]);
+      auto issue_s = [&](int s, int j) {  // S_s(j) = Q_s K(j)^T
+        const uint32_t q_addr = smem_u32(sm.q[s]);
+        const uint32_t k_addr = smem_u32(sm.k[j % kStages]);
 #pragma unroll
         for (int kk = 0; kk < kD / 16; ++kk) {
-          const uint32_t qoff = (kk >> 2) * kQHalfBytes + (kk & 3) * 32;
-          const uint32_t koff = (kk >> 2) * kKVHalfBytes + (kk & 3) * 32;
-          umma_f16_ss(tmem_s + s * kKeys, smem_desc_sw128(q_addr + qoff, 16, 1024),
-                      smem_desc_sw128(k_addr + koff, 16, 1024), idesc_qk, kk > 0);
+          const uint32_t off = (kk >> 2) * kHalfBytes + (kk & 3) * 32;
+          umma_f16_ss(tmem + s * kKeys, smem_desc_sw128(q_addr + off, 16, 1024),
+                      smem_desc_sw128(k_addr + off, 16, 1024), idesc_qk, kk > 0);
         }
         umma_commit(&sm.s_full[s]);
-        umma_commit(&sm.k_empty[ks]);  // K(j) slot free once S(j) has read it
-        return true;
       };
-      if (ok) ok = issue_s(0);
-      for (int j = 0; ok && j < n_kv; ++j) {
-        const int s = j % kSBufs;
-        if (j + 1 < n_kv && !issue_s(j + 1)) { ok = false; break; }
-        if (!mbar_wait(&sm.p_full[s], (j / kSBufs) & 1)) { ok = false; break; }
-        const int vs = j % kVStages;
-        if (!mbar_wait(&sm.full_v[vs], (j / kVStages) & 1)) { ok = false; break; }
-        tc_fence_after();
-        const uint32_t v_addr = smem_u32(sm.v[vs]);
+      auto issue_pv = [&](int s, int j) {  // O_s += P_s(j) V(j)
+        const uint32_t v_addr = smem_u32(sm.v[j % kStages]);
 #pragma unroll
         for (int kk = 0; kk < kKeys / 16; ++kk) {
-          const uint64_t vb = smem_desc_sw128(v_addr + kk * 16 * 128, kKVHalfBytes, 1024);
-          umma_f16_ts(tmem_o, tmem_s + s * kKeys + kk * 8, vb, idesc_pv, (j > 0 || kk > 0) ? 1u : 0u);
+          const uint64_t vb = smem_desc_sw128(v_addr + kk * 16 * 128, kHalfBytes, 1024);
+          umma_f16_ts(tmem + 256 + s * kD, tmem + s * kKeys + kk * 8, vb, idesc_pv, (j > 0 || kk > 0) ? 1u : 0u);
         }
-        umma_commit(&sm.v_empty[vs]);
-        umma_commit(&sm.pv_done[s]);
+        umma_commit(&sm.o_done[s]);
+      };
+      bool ok = mbar_wait(&sm.bar_q, 0) && mbar_wait(&sm.full_k[0], 0);
+      if (ok) {
+        tc_fence_after();
+        for (int s = 0; s < nstreams; ++s) issue_s(s, 0);
+        umma_commit(&sm.k_empty[0]);
+      }
+      for (int j = 0; ok && j < n_kv; ++j) {
+        const int st = j % kStages;
+        if (!mbar_wait(&sm.full_v[st], (j / kStages) & 1)) { ok = false; break; }
+        const bool more = j + 1 < n_kv;
+        for (int s = 0; ok && s < nstreams; ++s) {
+          if (!mbar_wait(&sm.p_full[s], j & 1)) { ok = false; break; }
+          if (s == 0 && more && !mbar_wait(&sm.full_k[(j + 1) % kStages], ((j + 1) / kStages) & 1)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          issue_pv(s, j);
+          if (s == nstreams - 1) umma_commit(&sm.v_empty[st]);
+          if (more) {
+            issue_s(s, j + 1);
+            if (s == nstreams - 1) umma_commit(&sm.k_empty[(j + 1) % kStages]);
+          }
+        }
       }
       if (!ok) flag_error(a, sm, kErrWaitTimeout);
       // All MMAs of this CTA complete before TMEM is released.
       umma_commit(&sm.fin);
       (void)mbar_wait(&sm.fin, 0);
     }
-  } else {
+  } else if (stream < nstreams) {
     // --------------------------------------------------------- softmax ----
     const int lim = (i < lq) ? (lk - lq + i) : (lk - 1);
-    const uint32_t t_lane = static_cast<uint32_t>(warp * 32) << 16;
+    const uint32_t t_lane = static_cast<uint32_t>((warp & 3) * 32) << 16;
+    const uint32_t tmem_s = tmem + stream * kKeys + t_lane;
+    const uint32_t tmem_o = tmem + 256 + stream * kD + t_lane;
     float m = -INFINITY, l = 0.f;
     bool ok = true;
     for (int j = 0; j < n_kv; ++j) {
       // warp-uniform outcome: the tcgen05.ld/st below need a converged warp
-      const int sb = j % kSBufs;
-      if (!__all_sync(0xffffffffu, mbar_wait(&sm.s_full[sb], (j / kSBufs) & 1))) { ok = false; break; }
+      if (!__all_sync(0xffffffffu, mbar_wait(&sm.s_full[stream], j & 1))) { ok = false; break; }
       tc_fence_after();
-      // S row in two 32-column halves: the second half loads while the
-      // first half's maximum is taken.
-      uint32_t sr[2][32];
-      tmem_ld32(tmem_s + sb * kKeys + t_lane, sr[0]);
-      tmem_ld_wait();
-      tmem_ld32(tmem_s + sb * kKeys + t_lane + 32, sr[1]);
       const int kbase = j * kKeys;
       const bool need_mask = kbase + kKeys - 1 > lim;
+      // Max pass over the row in two 64-column halves (64 registers live).
       // The max is taken over raw scores (scale > 0), the scale folded into
       // the exponent's FMA below; max is exact, so its order is free.
       float mx0 = -INFINITY, mx1 = -INFINITY;
 #pragma unroll
-      for (int c = 0; c < 2; ++c) {
-        if (c == 1) tmem_ld_wait();
-        if (need_mask) {
+      for (int hh = 0; hh < 2; ++hh) {
+        uint32_t sr[2][32];
+        tmem_ld32(tmem_s + hh * 64, sr[0]);
+        tmem_ld32(tmem_s + hh * 64 + 32, sr[1]);
+        tmem_ld_wait();
 #pragma unroll
-          for (int e = 0; e < 32; ++e)
-            if (kbase + c * 32 + e > lim) sr[c][e] = __float_as_uint(-INFINITY);
-        }
+        for (int c = 0; c < 2; ++c) {
+          if (need_mask) {
 #pragma unroll
-        for (int e = 0; e < 32; e += 4) {
-          mx0 = fmax3(mx0, __uint_as_float(sr[c][e]), __uint_as_float(sr[c][e + 1]));
-          mx1 = fmax3(mx1, __uint_as_float(sr[c][e + 2]), __uint_as_float(sr[c][e + 3]));
+            for (int e = 0; e < 32; ++e)
+              if (kbase + hh * 64 + c * 32 + e > lim) sr[c][e] = __float_as_uint(-INFINITY);
+          }
+#pragma unroll
+          for (int e = 0; e < 32; e += 4) {
+            mx0 = fmax3(mx0, __uint_as_float(sr[c][e]), __uint_as_float(sr[c][e + 1]));
+            mx1 = fmax3(mx1, __uint_as_float(sr[c][e + 2]), __uint_as_float(sr[c][e + 3]));
+          }
         }
       }
-      const float mraw = fmaxf(mx0, mx1);
-      const float mt = mraw * a.scale_log2;
+      const float mt = fmaxf(mx0, mx1) * a.scale_log2;
       const float m_new = fmaxf(m, mt);
       const bool resc = m_new > m + kRescaleThreshold;
       const float alpha = resc ? fast_exp2(m - m_new) : 1.f;
-      // O rows change only when one of this warp's rows rescales; then
-      // PV(j-1) must be complete first.
+      // S_s(j) has landed, so P V(j-1) -- issued before it -- is complete:
+      // O may be rescaled now (rows of this warp, when one of them needs it).
       if (j > 0 && __any_sync(0xffffffffu, resc)) {
-        if (!__all_sync(0xffffffffu, mbar_wait(&sm.pv_done[(j - 1) % kSBufs], ((j - 1) / kSBufs) & 1))) { ok = false; break; }
-        tc_fence_after();
 #pragma unroll 1
         for (int c = 0; c < 4; ++c) {
           uint32_t o[32];
-          tmem_ld32(tmem_o + t_lane + c * 32, o);
+          tmem_ld32(tmem_o + c * 32, o);
           tmem_ld_wait();
 #pragma unroll
           for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
-          tmem_st32(tmem_o + t_lane + c * 32, o);
+          tmem_st32(tmem_o + c * 32, o);
         }
-        tmem_st_wait();
       }
       if (resc) {
         l *= alpha;
@@ -351,31 +340,45 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) prefill_kernel(const __g
       const uint64_t sc2 = f32x2_pack(a.scale_log2, a.scale_log2);
       const uint64_t nm2 = f32x2_pack(neg_mu, neg_mu);
       uint64_t sum2[2] = {f32x2_pack(0.f, 0.f), f32x2_pack(0.f, 0.f)};  // two add chains
-      // P over the first 32 columns of the S buffer (S is in registers now):
-      // column k holds keys 2k and 2k+1 of this row as a bf16 pair.
+      // Exponent pass, again per 64-column half: P goes over the first 64
+      // columns of the S buffer, column k holding keys 2k and 2k+1 as a bf16
+      // pair. Half hh's P lands in columns 32hh .. 32hh+31, which hold S
+      // values of half 0 -- all read before they are overwritten.
 #pragma unroll
-      for (int c = 0; c < 2; ++c) {  // 32 keys -> 16 columns at a time
-        uint32_t w[16];
+      for (int hh = 0; hh < 2; ++hh) {
+        uint32_t sr[2][32];
+        tmem_ld32(tmem_s + hh * 64, sr[0]);
+        tmem_ld32(tmem_s + hh * 64 + 32, sr[1]);
+        tmem_ld_wait();
 #pragma unroll
-        for (int e = 0; e < 16; ++e) {
-          const uint64_t x2 = f32x2_fma(
-              f32x2_pack(__uint_as_float(sr[c][2 * e]), __uint_as_float(sr[c][2 * e + 1])), sc2, nm2);
-          float x0, x1;
-          f32x2_unpack(x2, x0, x1);
-          const float p0 = fast_exp2(x0), p1 = fast_exp2(x1);
-          sum2[e & 1] = f32x2_add(sum2[e & 1], f32x2_pack(p0, p1));
-          w[e] = pack_bf16x2(p0, p1);
+        for (int c = 0; c < 2; ++c) {  // 32 keys -> 16 columns at a time
+          if (need_mask) {
+#pragma unroll
+            for (int e = 0; e < 32; ++e)
+              if (kbase + hh * 64 + c * 32 + e > lim) sr[c][e] = __float_as_uint(-INFINITY);
+          }
+          uint32_t w[16];
+#pragma unroll
+          for (int e = 0; e < 16; ++e) {
+            const uint64_t x2 = f32x2_fma(
+                f32x2_pack(__uint_as_float(sr[c][2 * e]), __uint_as_float(sr[c][2 * e + 1])), sc2, nm2);
+            float x0, x1;
+            f32x2_unpack(x2, x0, x1);
+            const float p0 = fast_exp2(x0), p1 = fast_exp2(x1);
+            sum2[e & 1] = f32x2_add(sum2[e & 1], f32x2_pack(p0, p1));
+            w[e] = pack_bf16x2(p0, p1);
+          }
+          tmem_st16(tmem_s + hh * 32 + c * 16, w);
         }
-        tmem_st16(tmem_s + sb * kKeys + c * 16 + t_lane, w);
       }
       float s_lo, s_hi;
       f32x2_unpack(f32x2_add(sum2[0], sum2[1]), s_lo, s_hi);
       l += s_lo + s_hi;
       tmem_st_wait();
       tc_fence_before();
-      mbar_arrive(&sm.p_full[sb]);
+      mbar_arrive(&sm.p_full[stream]);
     }
-    if (ok && !__all_sync(0xffffffffu, mbar_wait(&sm.pv_done[(n_kv - 1) % kSBufs], ((n_kv - 1) / kSBufs) & 1))) ok = false;
+    if (ok && !__all_sync(0xffffffffu, mbar_wait(&sm.o_done[stream], (n_kv - 1) & 1))) ok = false;
     if (!ok) {
       flag_error(a, sm, kErrWaitTimeout);
     } else {
@@ -384,7 +387,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) prefill_kernel(const __g
 #pragma unroll 1
       for (int c = 0; c < 4; ++c) {
         uint32_t o[32];
-        tmem_ld32(tmem_o + t_lane + c * 32, o);
+        tmem_ld32(tmem_o + c * 32, o);
         tmem_ld_wait();
         if (out_row) {
 #pragma unroll
@@ -415,7 +418,8 @@ int launch_prefill(const CUtensorMap& qm, const CUtensorMap& km, const CUtensorM
   const size_t smem = sizeof(PrefillSmem) + 1024;
   int rc = ensure_dynamic_smem(reinterpret_cast<const void*>(&prefill_kernel), smem);
   if (rc != NVK_OK) return rc;
-  const dim3 grid((max_q_len + kRows - 1) / kRows, a.num_heads, batch);
+  const int groups = a.paired ? a.num_heads / 2 : a.num_heads;
+  const dim3 grid((max_q_len + kRows - 1) / kRows, groups, batch);
   return check_cuda(launch_pdl(prefill_kernel, grid, dim3(kThreads), smem, stream, qm, km, vm, a), "prefill launch");
 }
 
@@ -469,6 +473,7 @@ extern "C" int nvk_paged_prefill(void* out, const void* query, const void* key_c
   a.num_blocks = num_blocks;
   a.num_heads = num_heads;
   a.qpk = num_heads / num_kv_heads;
+  a.paired = a.qpk % 2 == 0;
   a.paged = 1;
   a.scale_log2 = scale * 1.4426950408889634f;
   return launch_prefill(qm, km, vm, a, batch, max_q_len, reinterpret_cast<cudaStream_t>(stream));
@@ -499,6 +504,7 @@ extern "C" int nvk_dense_prefill(void* out, const void* query, const void* key, 
   a.num_blocks = 0;
   a.num_heads = num_heads;
   a.qpk = num_heads / num_kv_heads;
+  a.paired = a.qpk % 2 == 0;
   a.paged = 0;
   a.scale_log2 = scale * 1.4426950408889634f;
   return launch_prefill(qm, km, vm, a, batch, max_q_len, reinterpret_cast<cudaStream_t>(stream));
