@@ -11,6 +11,10 @@
  *   num_kv_heads, head_dim], contiguous. Token slot s = block_id * block_size
  *   + offset addresses row s of the flattened [num_blocks * block_size,
  *   num_kv_heads, head_dim] view.
+ *   The attention kernels stage whole tiles of a block, so the rows of a
+ *   sequence's last block past its context are read and weighted by 0: they
+ *   must hold finite values (zero-fill the pool once when it is allocated;
+ *   appends only ever write real rows).
  *
  * Reference interfaces replaced (paths inside Pla-Yer/nano_vllm_ascend):
  *   nvk_kv_append      <- PagedKVCache.write, src/nanovllm_ascend/npu/paged_kv_cache.py:44-69

@@ -59,8 +59,12 @@ class PagedKVCache:
         self.dtype = dtype
         self.device = torch.device(device)
         shape = (num_layers, num_blocks, block_size, num_kv_heads, head_dim)
-        self.key_cache = torch.empty(shape, dtype=dtype, device=self.device)
-        self.value_cache = torch.empty(shape, dtype=dtype, device=self.device)
+        # Zero-filled (the reference allocates with torch.empty): the attention
+        # kernels stage whole tiles, so rows of a block past a sequence's end are
+        # read with probability 0, and 0 * V must stay 0 -- a never-written row
+        # holding a NaN bit pattern would make it NaN.
+        self.key_cache = torch.zeros(shape, dtype=dtype, device=self.device)
+        self.value_cache = torch.zeros(shape, dtype=dtype, device=self.device)
         self._deferring = False
         self._pending: dict[int, tuple[torch.Tensor, torch.Tensor, torch.Tensor]] = {}
 
