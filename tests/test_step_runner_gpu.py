@@ -14,8 +14,10 @@ forcing), and checks that
   (its logit within 0.05 of the maximum: the kernels' bf16 rounding may
   reorder near-ties),
 * every K/V row the runner wrote into the pool (layer 0 and the last layer,
-  through the block manager's tables) matches the reference's within the
-  attention tolerance.
+  through the block manager's tables) matches the reference's: layer 0's
+  within the attention tolerance; the last layer's, which inherit one layer
+  of bf16 rounding differences through attention, projections and MLP,
+  within two bf16 ulps at magnitude 8 (0.125) plus 2e-2 relative.
 """
 
 from types import SimpleNamespace
@@ -31,6 +33,7 @@ pytestmark = pytest.mark.gpu
 SHAPE = ModelShape(num_layers=2, hidden_size=256, num_heads=16, num_kv_heads=8, head_dim=128,
                    intermediate_size=512, vocab_size=512, max_position=4096)
 ATOL, RTOL, LOGIT_TOL = 2e-2, 1e-2, 5e-2
+DEEP_ATOL, DEEP_RTOL = 0.125, 2e-2  # rows of layers behind at least one attention layer
 
 
 def Seq(seq_id, prompt):
@@ -98,9 +101,10 @@ def check_sequences(runner, seqs, what):
             kc, vc = runner.kv_cache.get_physical_cache(layer)
             k_got = kc.reshape(-1, *kc.shape[2:])[slots].float()
             v_got = vc.reshape(-1, *vc.shape[2:])[slots].float()
+            atol, rtol = (ATOL, RTOL) if layer == 0 else (DEEP_ATOL, DEEP_RTOL)
             for got, want, name in ((k_got, k_ref.float(), "K"), (v_got, v_ref.float(), "V")):
                 err = (got - want).abs()
-                assert bool((err <= ATOL + RTOL * want.abs()).all()), \
+                assert bool((err <= atol + rtol * want.abs()).all()), \
                     f"{what}: seq {seq.seq_id} layer {layer} {name} rows off by up to {float(err.max())}"
 
 
