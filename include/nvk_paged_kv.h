@@ -238,9 +238,7 @@ NVK_API int nvk_dense_prefill(void* out, const void* query, const void* key, con
  * [max_position, head_dim] cast to bf16), and PagedKVCache.write of the
  * rotated k and of v at slot_mapping. query/key/value: bf16 rows of
  * num_heads / num_kv_heads heads, query_stride etc. ELEMENTS between tokens
- * (slices of a fused QKV output work; rows 8-byte aligned: pointers 8-byte
- * aligned, strides multiples of 4), cos/sin tables 16-byte aligned;
- * query_out: bf16 [num_tokens,
+ * (slices of a fused QKV output work); query_out: bf16 [num_tokens,
  * num_heads, head_dim] contiguous (may alias query when its stride is
  * num_heads * head_dim). Arithmetic in fp32, the norm's output rounded to
  * bf16 before the rotation (as the separate ops do). A bad slot skips that

@@ -7,12 +7,11 @@
 // then PagedKVCache.write of the rotated k and of v. One read of q, k, v;
 // the rotated q goes to q_out, k and v go to the pool rows of their slots.
 //
-// Half a warp per head row: lane l of a half holds dims {4l .. 4l+3} and
-// {64+4l .. 64+4l+3} (two 8-byte words), so each rotation pair (i, i+64) is
-// in one lane and a row is two coalesced 128-byte loads. A warp works on a
-// group of rows of one token (its position, slot and cos/sin loaded once)
-// and keeps kPairs row pairs (2 * kPairs rows) of loads in flight before
-// their reductions: a 16-lane reduction for the mean square, then
+// One warp per 8 head rows of a token, four rows at a time (cos/sin loaded
+// once per warp).
+// Lane l holds dims {2l, 2l+1} and {64+2l, 64+2l+1} of a row, so each
+// rotation pair (i, i+64) is in one lane: a warp reduction for the mean
+// square, then
 //   y  = bf16(x * rsqrt(mean(x^2) + eps) * w)                (fp32 arithmetic)
 //   out = bf16(y * cos + rotate_half(y) * sin),  rotate_half(y) = (-y[64:], y[:64])
 // HBM-bound elementwise work: per token (H + KVH) * 256 B read and written for
@@ -25,8 +24,8 @@ namespace {
 
 constexpr int kD = 128;
 constexpr int kWarps = 8;
-constexpr int kPairs = 8;  // row pairs in flight per warp
 
+__device__ __forceinline__ float2 bf16x2_to_f32(uint32_t w) { return make_float2(bf16lo_to_f32(w), bf16hi_to_f32(w)); }
 __device__ __forceinline__ float round_bf16(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
 
 struct NormRopeArgs {
@@ -46,73 +45,43 @@ struct NormRopeArgs {
   __nv_bfloat16* value_cache;
   int64_t num_tokens, num_slots;
   int num_heads, num_kv_heads;
-  int group_rows;  // head rows per warp, even
+  int group_rows;  // head rows per warp, a multiple of 4
   float eps;
   int* err;
 };
 
-__device__ __forceinline__ void unpack4(uint2 w, float (&x)[4]) {
-  x[0] = bf16lo_to_f32(w.x);
-  x[1] = bf16hi_to_f32(w.x);
-  x[2] = bf16lo_to_f32(w.y);
-  x[3] = bf16hi_to_f32(w.y);
-}
-
-__device__ __forceinline__ uint2 load8(const __nv_bfloat16* p) { return *reinterpret_cast<const uint2*>(p); }
-
-// Normalises and rotates one 128-dim head row held by a half warp as this
-// lane's dims {4l .. 4l+3} (w_lo) and {64+4l .. 64+4l+3} (w_hi); g_*, c_*, s_*
-// are this lane's weights and bf16-rounded cos/sin values as bf16 pairs.
-// Every lane of the warp must call it (the reduction shuffles stay inside
-// each half).
-__device__ __forceinline__ void norm_rope_row(uint2 w_lo, uint2 w_hi, uint2 g_lo, uint2 g_hi, uint2 c_lo, uint2 c_hi,
-                                              uint2 s_lo, uint2 s_hi, float eps, uint2& o_lo, uint2& o_hi) {
-  float x0[4], x1[4];
-  unpack4(w_lo, x0);
-  unpack4(w_hi, x1);
-  float ss = 0.f;
+// Normalises and rotates one 128-dim head row held as lane dims {2l, 2l+1}
+// (w_lo) and {64+2l, 65+2l} (w_hi); the cos/sin pairs are this lane's.
+__device__ __forceinline__ void norm_rope_row(uint32_t w_lo, uint32_t w_hi, float2 g0, float2 g1, float2 c0,
+                                              float2 c1, float2 s0, float2 s1, float eps, uint32_t& o_lo,
+                                              uint32_t& o_hi) {
+  const float2 x0 = bf16x2_to_f32(w_lo), x1 = bf16x2_to_f32(w_hi);
+  float ss = x0.x * x0.x + x0.y * x0.y + x1.x * x1.x + x1.y * x1.y;
 #pragma unroll
-  for (int k = 0; k < 4; ++k) ss += x0[k] * x0[k] + x1[k] * x1[k];
-#pragma unroll
-  for (int off = 8; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+  for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
   const float rinv = rsqrtf(ss * (1.f / kD) + eps);
-  float g0[4], g1[4], y0[4], y1[4], r0[4], r1[4];
-  unpack4(g_lo, g0);
-  unpack4(g_hi, g1);
-#pragma unroll
-  for (int k = 0; k < 4; ++k) {  // normalised row, rounded to bf16 as the norm's output is
-    y0[k] = round_bf16(x0[k] * rinv * g0[k]);
-    y1[k] = round_bf16(x1[k] * rinv * g1[k]);
-  }
-  float c0[4], c1[4], s0[4], s1[4];
-  unpack4(c_lo, c0);
-  unpack4(c_hi, c1);
-  unpack4(s_lo, s0);
-  unpack4(s_hi, s1);
+  // normalised row, rounded to bf16 as the norm's output is
+  const float y0 = round_bf16(x0.x * rinv * g0.x), y1 = round_bf16(x0.y * rinv * g0.y);
+  const float y2 = round_bf16(x1.x * rinv * g1.x), y3 = round_bf16(x1.y * rinv * g1.y);
   // out[i] = y[i] cos[i] - y[i+64] sin[i];  out[i+64] = y[i+64] cos[i+64] + y[i] sin[i+64]
-#pragma unroll
-  for (int k = 0; k < 4; ++k) {
-    r0[k] = y0[k] * c0[k] - y1[k] * s0[k];
-    r1[k] = y1[k] * c1[k] + y0[k] * s1[k];
-  }
-  o_lo = make_uint2(pack_bf16x2(r0[0], r0[1]), pack_bf16x2(r0[2], r0[3]));
-  o_hi = make_uint2(pack_bf16x2(r1[0], r1[1]), pack_bf16x2(r1[2], r1[3]));
+  o_lo = pack_bf16x2(y0 * c0.x - y2 * s0.x, y1 * c0.y - y3 * s0.y);
+  o_hi = pack_bf16x2(y2 * c1.x + y0 * s1.x, y3 * c1.y + y1 * s1.y);
 }
 
-// bf16 rounding of four fp32 table values, packed as two bf16 pairs.
-__device__ __forceinline__ uint2 table4(const float* p) {
-  const float4 v = *reinterpret_cast<const float4*>(p);
-  return make_uint2(pack_bf16x2(v.x, v.y), pack_bf16x2(v.z, v.w));
-}
+// One warp per group of group_rows head rows of one token (rows: the q heads,
+// then the k heads, then the v heads): the token's position, slot and
+// cos/sin pairs are loaded once per group, and the group's rows go kBatch at
+// a time (loads of kBatch rows in flight before their reductions).
+constexpr int kBatch = 8;
 
-__global__ void __launch_bounds__(kWarps * 32, 2) qk_norm_rope_append_kernel(const NormRopeArgs a) {
+__global__ void __launch_bounds__(kWarps * 32) qk_norm_rope_append_kernel(const NormRopeArgs a) {
   pdl_launch_dependents();
   pdl_wait();
   const int lane = threadIdx.x & 31;
-  const int half = lane >> 4, hl = lane & 15;
-  const int d_lo = 4 * hl, d_hi = 64 + 4 * hl;
-  const uint2 gq_lo = load8(a.q_weight + d_lo), gq_hi = load8(a.q_weight + d_hi);
-  const uint2 gk_lo = load8(a.k_weight + d_lo), gk_hi = load8(a.k_weight + d_hi);
+  const float2 gq0 = bf16x2_to_f32(*reinterpret_cast<const uint32_t*>(a.q_weight + 2 * lane));
+  const float2 gq1 = bf16x2_to_f32(*reinterpret_cast<const uint32_t*>(a.q_weight + 64 + 2 * lane));
+  const float2 gk0 = bf16x2_to_f32(*reinterpret_cast<const uint32_t*>(a.k_weight + 2 * lane));
+  const float2 gk1 = bf16x2_to_f32(*reinterpret_cast<const uint32_t*>(a.k_weight + 64 + 2 * lane));
   const int nrows = a.num_heads + 2 * a.num_kv_heads;
   const int nqk = a.num_heads + a.num_kv_heads;
   const int groups = (nrows + a.group_rows - 1) / a.group_rows;
@@ -125,57 +94,49 @@ __global__ void __launch_bounds__(kWarps * 32, 2) qk_norm_rope_append_kernel(con
     const int64_t slot = a.slots[t];
     const bool slot_ok = slot >= 0 && slot < a.num_slots;
     if (!slot_ok && lane == 0 && r_lo == 0 && a.err) atomicOr(a.err, kErrBadSlot);
-    uint2 c_lo = make_uint2(0u, 0u), c_hi = c_lo, s_lo = c_lo, s_hi = c_lo;
+    float2 c0 = make_float2(0.f, 0.f), c1 = c0, s0 = c0, s1 = c0;
     if (r_lo < nqk) {
       int64_t p = a.positions[t];
       if (p < 0 || p >= a.max_pos) {
         if (lane == 0 && r_lo == 0 && a.err) atomicOr(a.err, kErrContextTooLong);
         p = p < 0 ? 0 : a.max_pos - 1;
       }
+      const float* cr = a.cos_table + p * kD;
+      const float* sr = a.sin_table + p * kD;
       // cos/sin rows cast to bf16 (apply_rotary_pos_emb_tnd casts them to q's dtype)
-      c_lo = table4(a.cos_table + p * kD + d_lo);
-      c_hi = table4(a.cos_table + p * kD + d_hi);
-      s_lo = table4(a.sin_table + p * kD + d_lo);
-      s_hi = table4(a.sin_table + p * kD + d_hi);
+      c0 = make_float2(round_bf16(cr[2 * lane]), round_bf16(cr[2 * lane + 1]));
+      c1 = make_float2(round_bf16(cr[64 + 2 * lane]), round_bf16(cr[65 + 2 * lane]));
+      s0 = make_float2(round_bf16(sr[2 * lane]), round_bf16(sr[2 * lane + 1]));
+      s1 = make_float2(round_bf16(sr[64 + 2 * lane]), round_bf16(sr[65 + 2 * lane]));
     }
-    for (int r0 = r_lo; r0 < r_hi; r0 += 2 * kPairs) {
-      uint2 lo[kPairs], hi[kPairs];
+    for (int r0 = r_lo; r0 < r_hi; r0 += kBatch) {
+      uint32_t lo[kBatch], hi[kBatch];
 #pragma unroll
-      for (int u = 0; u < kPairs; ++u) {
-        const int r = r0 + 2 * u + half;
+      for (int u = 0; u < kBatch; ++u) {
+        const int r = r0 + u;
         const __nv_bfloat16* src = r < a.num_heads ? a.q + t * a.q_stride + r * kD
                                  : r < nqk       ? a.k + t * a.k_stride + (r - a.num_heads) * kD
                                                  : a.v + t * a.v_stride + (r - nqk) * kD;
-        const bool in = r < r_hi;
-        lo[u] = in ? load8(src + d_lo) : make_uint2(0u, 0u);
-        hi[u] = in ? load8(src + d_hi) : make_uint2(0u, 0u);
+        lo[u] = r < r_hi ? *reinterpret_cast<const uint32_t*>(src + 2 * lane) : 0u;
+        hi[u] = r < r_hi ? *reinterpret_cast<const uint32_t*>(src + 64 + 2 * lane) : 0u;
       }
 #pragma unroll
-      for (int u = 0; u < kPairs; ++u) {
-        if (r0 + 2 * u >= r_hi) break;  // warp-uniform: both halves are past the group's end
-        const int r = r0 + 2 * u + half;
-        const bool is_q = r < a.num_heads;
-        uint2 o_lo = lo[u], o_hi = hi[u];
-        if (r0 + 2 * u < nqk) {  // at least one half holds a q or k row: the whole warp reduces
-          uint2 n_lo, n_hi;
-          norm_rope_row(lo[u], hi[u], is_q ? gq_lo : gk_lo, is_q ? gq_hi : gk_hi, c_lo, c_hi, s_lo, s_hi, a.eps,
-                        n_lo, n_hi);
-          if (r < nqk) {
-            o_lo = n_lo;
-            o_hi = n_hi;
-          }
-        }
-        if (r >= r_hi) continue;
+      for (int u = 0; u < kBatch; ++u) {
+        const int r = r0 + u;
+        if (r >= r_hi) break;
         __nv_bfloat16* dst;
-        if (is_q) {
-          dst = a.q_out + (t * a.num_heads + r) * kD;
-        } else {
+        uint32_t o_lo = lo[u], o_hi = hi[u];
+        if (r < nqk) {
+          const bool is_q = r < a.num_heads;
+          norm_rope_row(lo[u], hi[u], is_q ? gq0 : gk0, is_q ? gq1 : gk1, c0, c1, s0, s1, a.eps, o_lo, o_hi);
+          if (!is_q && !slot_ok) continue;
+          dst = is_q ? a.q_out + (t * a.num_heads + r) * kD : a.key_cache + (slot * a.num_kv_heads + r - a.num_heads) * kD;
+        } else {  // v: a raw copy
           if (!slot_ok) continue;
-          dst = r < nqk ? a.key_cache + (slot * a.num_kv_heads + r - a.num_heads) * kD
-                        : a.value_cache + (slot * a.num_kv_heads + r - nqk) * kD;
+          dst = a.value_cache + (slot * a.num_kv_heads + r - nqk) * kD;
         }
-        *reinterpret_cast<uint2*>(dst + d_lo) = o_lo;
-        *reinterpret_cast<uint2*>(dst + d_hi) = o_hi;
+        *reinterpret_cast<uint32_t*>(dst + 2 * lane) = o_lo;
+        *reinterpret_cast<uint32_t*>(dst + 64 + 2 * lane) = o_hi;
       }
     }
   }
@@ -202,14 +163,11 @@ extern "C" int nvk_qk_norm_rope_append(const void* query, const void* key, const
   if (!query || !key || !value || !q_weight || !k_weight || !cos_table || !sin_table || !positions || !query_out ||
       !key_cache || !value_cache || !slot_mapping)
     return fail(NVK_ERR_INVALID_ARGUMENT, "qk_norm_rope_append: null pointer");
-  auto al8 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 7u) == 0; };
-  if (!al8(query) || !al8(key) || !al8(value) || !al8(q_weight) || !al8(k_weight) || !al8(query_out) ||
-      query_stride % 4 || key_stride % 4 || value_stride % 4 || query_stride < int64_t(num_heads) * kD ||
+  auto al4 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 3u) == 0; };
+  if (!al4(query) || !al4(key) || !al4(value) || !al4(q_weight) || !al4(k_weight) || !al4(query_out) ||
+      query_stride % 2 || key_stride % 2 || value_stride % 2 || query_stride < int64_t(num_heads) * kD ||
       key_stride < int64_t(num_kv_heads) * kD || value_stride < int64_t(num_kv_heads) * kD)
-    return fail(NVK_ERR_INVALID_ARGUMENT,
-                "qk_norm_rope_append: rows must be 8-byte aligned (strides multiples of 4) and strides cover a row");
-  if (!aligned16(cos_table) || !aligned16(sin_table))
-    return fail(NVK_ERR_INVALID_ARGUMENT, "qk_norm_rope_append: cos/sin tables must be 16-byte aligned");
+    return fail(NVK_ERR_INVALID_ARGUMENT, "qk_norm_rope_append: rows must be 4-byte aligned and strides cover a row");
   NormRopeArgs a;
   a.q = static_cast<const __nv_bfloat16*>(query);
   a.k = static_cast<const __nv_bfloat16*>(key);
@@ -238,7 +196,7 @@ extern "C" int nvk_qk_norm_rope_append(const void* query, const void* key, const
   // A whole token per warp (cos/sin loaded once per token) when the tokens
   // alone give every SM 16 warps; else four rows per warp, for parallelism.
   const int nrows = num_heads + 2 * num_kv_heads;
-  const int group_rows = num_tokens >= int64_t(sms) * 16 ? (nrows + 1) / 2 * 2 : 4;  // even: rows go in pairs
+  const int group_rows = num_tokens >= int64_t(sms) * 16 ? (nrows + 3) / 4 * 4 : 4;
   a.group_rows = group_rows;
   const int64_t groups = (nrows + group_rows - 1) / group_rows;
   const int64_t want = (num_tokens * groups + kWarps - 1) / kWarps;

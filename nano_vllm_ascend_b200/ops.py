@@ -124,10 +124,6 @@ def qk_norm_rope_append(
         raise ValueError("qk_norm_rope_append: positions and slot_mapping must be int64 [tokens]")
     if not (key_cache.is_contiguous() and value_cache.is_contiguous()):
         raise ValueError("qk_norm_rope_append: caches must be contiguous")
-    # the kernel reads rows as 8-byte words: rows whose token stride or start is
-    # not 8-byte aligned are packed first
-    query, key, value = (t if t.stride(0) % 4 == 0 and t.data_ptr() % 8 == 0 else t.contiguous()
-                         for t in (query, key, value))
     if query_out is None:
         query_out = torch.empty(tokens, num_heads, head_dim, dtype=_BF16, device=dev)
     elif query_out.shape != (tokens, num_heads, head_dim) or not query_out.is_contiguous() or query_out.dtype != _BF16:
