@@ -26,13 +26,12 @@
 //     P_s(j) only after the P V has read it, and the tensor pipe always has
 //     the other stream's work queued while one stream's softmax runs.
 //   warps 0-3 / 4-7 (softmax of stream 0 / 1): thread r owns query row r =
-//     TMEM lane r: takes the max of its 128-key S row (tcgen05.ld of two
-//     64-column halves), masks, base-2 online softmax with lazy rescaling of
-//     O (only when the running max grows by more than 2^8; S_s(j) having
-//     landed means P V(j-1) is done, so O may be rescaled at once), then per
-//     half again the exponentials, written as bf16 pairs into the first 64
-//     columns of its S (tcgen05.st), and at the end normalises its O row and
-//     stores it.
+//     TMEM lane r: loads its 128-key S row (one round of tcgen05.ld), masks,
+//     base-2 online softmax, P written as bf16 pairs into the first 64
+//     columns of its S (tcgen05.st), lazy rescaling of O (only when the
+//     running max grew by more than 2^8; S_s(j) having landed means P V(j-1)
+//     is done, so O may be rescaled before P_s(j) is signalled), and at the
+//     end normalises its O row and stores it.
 // Ten warps put three on one SM sub-partition, whose register file holds
 // 3 x 32 x 168 registers: the kernel is held to 168 registers a thread.
 // Every mbarrier wait is bounded; on a timeout the CTA records the error,
@@ -90,6 +89,30 @@ struct PrefillSmem {
 };
 
 static_assert(sizeof(PrefillSmem) + 1024 <= 232448, "prefill shared memory exceeds one SM's 227 KB");
+
+// The first 16 of 32 registers into 16 consecutive 32-bit TMEM columns of
+// this thread's lane (warp-collective).
+__device__ __forceinline__ void tmem_st16_first(uint32_t taddr, const uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+      "{%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),
+      "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+      : "memory");
+}
+
+// O row of this thread (four 32-column chunks) times alpha, in TMEM.
+__device__ __forceinline__ void rescale_o(uint32_t tmem_o, float alpha) {
+#pragma unroll 1
+  for (int c = 0; c < 4; ++c) {
+    uint32_t o[32];
+    tmem_ld32(tmem_o + c * 32, o);
+    tmem_ld_wait();
+#pragma unroll
+    for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
+    tmem_st32(tmem_o + c * 32, o);
+  }
+}
 
 __device__ __forceinline__ void flag_error(const PrefillArgs& a, PrefillSmem& sm, int code) {
   if (a.err) atomicOr(a.err, code);
@@ -290,90 +313,59 @@ __global__ void __maxnreg__(168) prefill_kernel(const __grid_constant__ CUtensor
       if (!__all_sync(0xffffffffu, mbar_wait(&sm.s_full[stream], j & 1))) { ok = false; break; }
       tc_fence_after();
       const int kbase = j * kKeys;
-      const bool need_mask = kbase + kKeys - 1 > lim;
-      // Max pass over the row in two 64-column halves (64 registers live).
+      // The whole 128-key S row in one round of TMEM loads.
+      uint32_t sr[4][32];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) tmem_ld32(tmem_s + c * 32, sr[c]);
+      tmem_ld_wait();
+      if (kbase + kKeys - 1 > lim) {
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+#pragma unroll
+          for (int e = 0; e < 32; ++e)
+            if (kbase + c * 32 + e > lim) sr[c][e] = __float_as_uint(-INFINITY);
+      }
       // The max is taken over raw scores (scale > 0), the scale folded into
       // the exponent's FMA below; max is exact, so its order is free.
       float mx0 = -INFINITY, mx1 = -INFINITY;
 #pragma unroll
-      for (int hh = 0; hh < 2; ++hh) {
-        uint32_t sr[2][32];
-        tmem_ld32(tmem_s + hh * 64, sr[0]);
-        tmem_ld32(tmem_s + hh * 64 + 32, sr[1]);
-        tmem_ld_wait();
+      for (int c = 0; c < 4; ++c)
 #pragma unroll
-        for (int c = 0; c < 2; ++c) {
-          if (need_mask) {
-#pragma unroll
-            for (int e = 0; e < 32; ++e)
-              if (kbase + hh * 64 + c * 32 + e > lim) sr[c][e] = __float_as_uint(-INFINITY);
-          }
-#pragma unroll
-          for (int e = 0; e < 32; e += 4) {
-            mx0 = fmax3(mx0, __uint_as_float(sr[c][e]), __uint_as_float(sr[c][e + 1]));
-            mx1 = fmax3(mx1, __uint_as_float(sr[c][e + 2]), __uint_as_float(sr[c][e + 3]));
-          }
+        for (int e = 0; e < 32; e += 4) {
+          mx0 = fmax3(mx0, __uint_as_float(sr[c][e]), __uint_as_float(sr[c][e + 1]));
+          mx1 = fmax3(mx1, __uint_as_float(sr[c][e + 2]), __uint_as_float(sr[c][e + 3]));
         }
-      }
       const float mt = fmaxf(mx0, mx1) * a.scale_log2;
       const float m_new = fmaxf(m, mt);
       const bool resc = m_new > m + kRescaleThreshold;
       const float alpha = resc ? fast_exp2(m - m_new) : 1.f;
-      // S_s(j) has landed, so P V(j-1) -- issued before it -- is complete:
-      // O may be rescaled now (rows of this warp, when one of them needs it).
-      if (j > 0 && __any_sync(0xffffffffu, resc)) {
-#pragma unroll 1
-        for (int c = 0; c < 4; ++c) {
-          uint32_t o[32];
-          tmem_ld32(tmem_o + c * 32, o);
-          tmem_ld_wait();
-#pragma unroll
-          for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
-          tmem_st32(tmem_o + c * 32, o);
-        }
-      }
       if (resc) {
         l *= alpha;
         m = m_new;
       }
       const float neg_mu = (m == -INFINITY) ? 0.f : -m;
-      const uint64_t sc2 = f32x2_pack(a.scale_log2, a.scale_log2);
-      const uint64_t nm2 = f32x2_pack(neg_mu, neg_mu);
-      uint64_t sum2[2] = {f32x2_pack(0.f, 0.f), f32x2_pack(0.f, 0.f)};  // two add chains
-      // Exponent pass, again per 64-column half: P goes over the first 64
-      // columns of the S buffer, column k holding keys 2k and 2k+1 as a bf16
-      // pair. Half hh's P lands in columns 32hh .. 32hh+31, which hold S
-      // values of half 0 -- all read before they are overwritten.
+      const float sc = a.scale_log2;
+      float sum[4] = {0.f, 0.f, 0.f, 0.f};  // independent add chains
+      // P over the first 64 columns of the S buffer (S is in registers now):
+      // column k holds keys 2k and 2k+1 of this row as a bf16 pair.
 #pragma unroll
-      for (int hh = 0; hh < 2; ++hh) {
-        uint32_t sr[2][32];
-        tmem_ld32(tmem_s + hh * 64, sr[0]);
-        tmem_ld32(tmem_s + hh * 64 + 32, sr[1]);
-        tmem_ld_wait();
+      for (int c = 0; c < 4; ++c) {  // 32 keys -> 16 columns at a time
+        // word e of P overwrites score e, already read at pair e / 2 <= e
 #pragma unroll
-        for (int c = 0; c < 2; ++c) {  // 32 keys -> 16 columns at a time
-          if (need_mask) {
-#pragma unroll
-            for (int e = 0; e < 32; ++e)
-              if (kbase + hh * 64 + c * 32 + e > lim) sr[c][e] = __float_as_uint(-INFINITY);
-          }
-          uint32_t w[16];
-#pragma unroll
-          for (int e = 0; e < 16; ++e) {
-            const uint64_t x2 = f32x2_fma(
-                f32x2_pack(__uint_as_float(sr[c][2 * e]), __uint_as_float(sr[c][2 * e + 1])), sc2, nm2);
-            float x0, x1;
-            f32x2_unpack(x2, x0, x1);
-            const float p0 = fast_exp2(x0), p1 = fast_exp2(x1);
-            sum2[e & 1] = f32x2_add(sum2[e & 1], f32x2_pack(p0, p1));
-            w[e] = pack_bf16x2(p0, p1);
-          }
-          tmem_st16(tmem_s + hh * 32 + c * 16, w);
+        for (int e = 0; e < 16; ++e) {
+          const float p0 = fast_exp2(fmaf(__uint_as_float(sr[c][2 * e]), sc, neg_mu));
+          const float p1 = fast_exp2(fmaf(__uint_as_float(sr[c][2 * e + 1]), sc, neg_mu));
+          sum[(2 * e) & 3] += p0;
+          sum[(2 * e + 1) & 3] += p1;
+          sr[c][e] = pack_bf16x2(p0, p1);
         }
+        tmem_st16_first(tmem_s + c * 16, sr[c]);
       }
-      float s_lo, s_hi;
-      f32x2_unpack(f32x2_add(sum2[0], sum2[1]), s_lo, s_hi);
-      l += s_lo + s_hi;
+      l += (sum[0] + sum[1]) + (sum[2] + sum[3]);
+      // S_s(j) has landed, so P V(j-1) -- issued before it -- is complete: O
+      // may be rescaled now (rows of this warp, when one of them needs it),
+      // before this tile's P is signalled and P V(j) issued.
+      if (j > 0 && __any_sync(0xffffffffu, resc)) rescale_o(tmem_o, alpha);
       tmem_st_wait();
       tc_fence_before();
       mbar_arrive(&sm.p_full[stream]);
