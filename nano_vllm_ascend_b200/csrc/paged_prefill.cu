@@ -8,32 +8,32 @@
 // lengths. Masking is bottom-right aligned: query i of a sequence with Lq
 // queries and Lk keys sees key j iff j <= Lk - Lq + i.
 //
-// One CTA = 128 query rows of one sequence x TWO query heads of one GQA
-// group ("streams" 0 and 1; one stream when the group size is odd), one CTA
-// per SM. Both streams read the same 128-key K and V tiles (one pool block
-// each), so every K/V byte staged in shared memory feeds two heads.
-// Tensor memory (all 512 columns): S/P of stream s at columns s*128, its O
-// accumulator at 256 + s*128.
-//   warp 8 (producer): TMA loads of the two Q tiles once, then per key tile
-//     the K and the V tile (two 64-dim halves each, 128-byte swizzle = the
-//     canonical UMMA operand layout) into 2-stage rings; block ids 32 at a
-//     time (one parallel load per warp).
-//   warp 9 (MMA, one elected lane): S_s(0) = Q_s K(0)^T for both streams,
-//     then per tile j and stream s: wait for P_s(j), issue O_s += P_s(j) V(j)
-//     (P read from TMEM where the softmax wrote it over S_s, V MN-major from
-//     smem) and right behind it S_s(j+1) = Q_s K(j+1)^T into the same
-//     columns. tcgen05.mma executes in issue order, so S_s(j+1) overwrites
-//     P_s(j) only after the P V has read it, and the tensor pipe always has
-//     the other stream's work queued while one stream's softmax runs.
-//   warps 0-3 / 4-7 (softmax of stream 0 / 1): thread r owns query row r =
-//     TMEM lane r: loads its 128-key S row (one round of tcgen05.ld), masks,
-//     base-2 online softmax, P written as bf16 pairs into the first 64
-//     columns of its S (tcgen05.st), lazy rescaling of O (only when the
-//     running max grew by more than 2^8; S_s(j) having landed means P V(j-1)
-//     is done, so O may be rescaled before P_s(j) is signalled), and at the
-//     end normalises its O row and stores it.
-// Ten warps put three on one SM sub-partition, whose register file holds
-// 3 x 32 x 168 registers: the kernel is held to 168 registers a thread.
+// Work item = 128 query rows of one sequence x one query head. The grid is
+// persistent (one CTA per SM); CTA c takes items c, c + C, c + 2C, ... in an
+// order that puts the heaviest query tiles first. Per item the 128-key K and
+// V tiles (one pool block each) stream through shared memory.
+// Tensor memory (512 columns): S/P double buffered at 0 and 128, O at 256,
+// the item's Q as the A operand of S = Q K^T at 384 / 448 (double buffered
+// across items), so an S UMMA reads only K from shared memory.
+//   warp 4 (producer): per item a TMA load of the Q tile into one of two
+//     staging buffers, then per key tile the K and V tiles (two 64-dim halves
+//     each, 128-byte swizzle = the canonical UMMA operand layout) into
+//     2-stage rings; block ids 32 at a time (one parallel load per warp).
+//   warp 5 (MMA, one elected lane): S(j) = Q K(j)^T (A from TMEM) into S
+//     buffer j % 2, two tiles ahead of O += P(j) V(j) (P from TMEM where the
+//     softmax wrote it over S(j), V MN-major from smem); S(j+2) is issued
+//     right behind P V(j) (tcgen05.mma executes in issue order, so it
+//     overwrites P(j) only after the P V has read it). An item's first two S
+//     tiles are issued behind the previous item's last P V, while the
+//     softmax warps still write that item's output.
+//   warps 0-3 (softmax): thread r owns query row r = TMEM lane r: per item
+//     the copy of its Q row from the staging buffer into TMEM; per tile the
+//     128-key S row in one round of tcgen05.ld, mask, base-2 online softmax,
+//     P written as bf16 pairs into the first 64 columns of its S buffer
+//     (tcgen05.st), lazy rescaling of O (only when the running max grew by
+//     more than 2^8, after P V(j-1) completed); per item the next item's Q
+//     copy, then the normalised O rows staged in the item's own Q staging
+//     buffer (O released) and stored two whole rows per warp instruction.
 // Every mbarrier wait is bounded; on a timeout the CTA records the error,
 // drains its in-flight copies and MMAs, frees TMEM and exits.
 #include "host_common.h"
@@ -44,17 +44,18 @@ namespace nvk {
 namespace {
 
 constexpr int kD = 128;
-constexpr int kRows = 128;                // query rows per CTA (UMMA M)
+constexpr int kRows = 128;                // query rows per item (UMMA M)
 constexpr int kKeys = 128;                // keys per K/V tile: one 128-token pool block
 constexpr int kHalfBytes = 128 * 128;     // one 64-dim half of a 128-row tile
 constexpr int kTileBytes = 2 * kHalfBytes;
-constexpr int kStages = 2;                // K and V ring depth
-constexpr int kStreams = 2;               // query heads per CTA
-constexpr int kStreamThreads = 128;       // softmax threads per stream
-constexpr int kProducerWarp = 8;
-constexpr int kMmaWarp = 9;
-constexpr int kThreads = 10 * 32;
-constexpr uint32_t kTmemCols = 512;       // S0 | S1 | O0 | O1, 128 columns each
+constexpr int kStages = 2;                // K, V and Q ring depth
+constexpr int kSoftmaxThreads = 128;
+constexpr int kProducerWarp = 4;
+constexpr int kMmaWarp = 5;
+constexpr int kThreads = 6 * 32;
+constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kColO = 256;           // O accumulator
+constexpr uint32_t kColQ = 384;           // Q(item) at kColQ + (item % 2) * 64
 constexpr float kRescaleThreshold = 8.0f;
 
 struct PrefillArgs {
@@ -68,27 +69,69 @@ struct PrefillArgs {
   int num_blocks;
   int num_heads;
   int qpk;
-  int paired;  // two heads per CTA (qpk even)
   int paged;
+  int batch;
+  int qtiles;  // query tiles of the longest sequence
   float scale_log2;
 };
 
 struct PrefillSmem {
-  alignas(1024) uint8_t q[kStreams][kTileBytes];
+  alignas(1024) uint8_t q[kStages][kTileBytes];
   alignas(1024) uint8_t k[kStages][kTileBytes];
   alignas(1024) uint8_t v[kStages][kTileBytes];
-  uint64_t bar_q;
+  uint64_t q_full[kStages], q_empty[kStages], q_tmem[kStages];
   uint64_t full_k[kStages], k_empty[kStages];
   uint64_t full_v[kStages], v_empty[kStages];
-  uint64_t s_full[kStreams];  // S_s(j) in TMEM (and, in issue order, P V_s(j-1) done)
-  uint64_t p_full[kStreams];  // P_s(j) written by the stream's 128 softmax threads
-  uint64_t o_done[kStreams];  // O_s += P_s(j) V(j) complete
+  uint64_t s_full[2];   // S(j) in buffer j % 2
+  uint64_t p_full[2];   // P(j) written over it by the 128 softmax threads
+  uint64_t pv_done[2];  // O += P V(j) complete, barrier j % 2 (one phase per two tiles, so a
+                        // wait is never two phases behind its barrier)
+  uint64_t o_free;      // one phase per item: its O has been read out
   uint64_t fin;
   uint32_t tmem_base;
   volatile int abort;
 };
 
 static_assert(sizeof(PrefillSmem) + 1024 <= 232448, "prefill shared memory exceeds one SM's 227 KB");
+
+// One work item: query tile qt of head h of sequence b. Every role walks the
+// same list; `next` skips items without rows and reports their key tiles.
+struct Item {
+  int w, qt, h, b, q0, lq, lk, kv_row0, n_kv;
+};
+
+__device__ __forceinline__ bool load_item(const PrefillArgs& a, int w, Item& it) {
+  const int per_tile = a.num_heads * a.batch;
+  it.w = w;
+  it.qt = a.qtiles - 1 - w / per_tile;  // heaviest (last) query tiles first
+  const int rem = w - (a.qtiles - 1 - it.qt) * per_tile;
+  it.h = rem % a.num_heads;
+  it.b = rem / a.num_heads;
+  it.q0 = a.cu_q[it.b];
+  it.lq = a.cu_q[it.b + 1] - it.q0;
+  if (it.qt * kRows >= it.lq) return false;
+  it.lk = a.paged ? a.kv_lens[it.b] : (a.cu_kv[it.b + 1] - a.cu_kv[it.b]);
+  it.kv_row0 = a.paged ? 0 : a.cu_kv[it.b];
+  const int i_last = min(it.qt * kRows + kRows - 1, it.lq - 1);
+  const int lim_last = min(it.lk - it.lq + i_last, it.lk - 1);
+  it.n_kv = lim_last < 0 ? 0 : lim_last / kKeys + 1;
+  return true;
+}
+
+// Next item of this CTA at or after list position w that has key tiles
+// (items with rows but no visible key are handed to `zero_rows`).
+template <typename ZeroRows>
+__device__ __forceinline__ bool next_item(const PrefillArgs& a, int& w, int total, Item& it, ZeroRows&& zero_rows) {
+  for (; w < total; w += gridDim.x) {
+    if (!load_item(a, w, it)) continue;
+    if (it.n_kv == 0) {
+      zero_rows(it);
+      continue;
+    }
+    return true;
+  }
+  return false;
+}
 
 // The first 16 of 32 registers into 16 consecutive 32-bit TMEM columns of
 // this thread's lane (warp-collective).
@@ -99,6 +142,11 @@ __device__ __forceinline__ void tmem_st16_first(uint32_t taddr, const uint32_t (
       "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),
       "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
       : "memory");
+}
+
+// Barrier `id` (not 0, which __syncthreads uses) among `count` threads.
+__device__ __forceinline__ void named_barrier_sync(int id, int count) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
 }
 
 // O row of this thread (four 32-column chunks) times alpha, in TMEM.
@@ -119,57 +167,35 @@ __device__ __forceinline__ void flag_error(const PrefillArgs& a, PrefillSmem& sm
   sm.abort = 1;
 }
 
-__global__ void __maxnreg__(168) prefill_kernel(const __grid_constant__ CUtensorMap qmap,
-                                                const __grid_constant__ CUtensorMap kmap,
-                                                const __grid_constant__ CUtensorMap vmap, const PrefillArgs a) {
-  const int qt = gridDim.x - 1 - blockIdx.x;  // heaviest (last) query tiles first
-  const int b = blockIdx.z;
-  const int nstreams = a.paired ? 2 : 1;
-  const int h0 = blockIdx.y * nstreams;  // query heads h0 .. h0 + nstreams - 1, one KV group
+__global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_constant__ CUtensorMap qmap,
+                                                              const __grid_constant__ CUtensorMap kmap,
+                                                              const __grid_constant__ CUtensorMap vmap,
+                                                              const PrefillArgs a) {
   pdl_launch_dependents();
   pdl_wait();
-  const int q0 = a.cu_q[b];
-  const int lq = a.cu_q[b + 1] - q0;
-  if (qt * kRows >= lq) return;
-  const int lk = a.paged ? a.kv_lens[b] : (a.cu_kv[b + 1] - a.cu_kv[b]);
-  const int kv_row0 = a.paged ? 0 : a.cu_kv[b];
-  const int g = h0 / a.qpk;
-  const int i_last = min(qt * kRows + kRows - 1, lq - 1);
-  const int lim_last = min(lk - lq + i_last, lk - 1);
-  const int n_kv = lim_last < 0 ? 0 : lim_last / kKeys + 1;  // 128-key tiles
-
+  const int total = a.qtiles * a.num_heads * a.batch;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int stream = warp >> 2;                  // softmax warps 0-3 / 4-7
-  const int r = tid & (kStreamThreads - 1);      // query row within the tile = TMEM lane
-  const int i = qt * kRows + r;                  // query row within the sequence
-  __nv_bfloat16* out_row = nullptr;
-  if (warp < 8 && stream < nstreams && i < lq)
-    out_row = a.out + (static_cast<int64_t>(q0 + i) * a.num_heads + h0 + stream) * kD;
-
-  if (n_kv == 0) {  // no visible key for any row of this tile: zeros
-    if (out_row) {
-      for (int c = 0; c < kD; c += 8) *reinterpret_cast<uint4*>(out_row + c) = make_uint4(0, 0, 0, 0);
-    }
-    return;
-  }
 
   extern __shared__ uint8_t smem_raw[];
   PrefillSmem& sm =
       *reinterpret_cast<PrefillSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-
   if (tid == 0) {
-    mbar_init(&sm.bar_q, 1);
     for (int s = 0; s < kStages; ++s) {
+      mbar_init(&sm.q_full[s], 1);
+      mbar_init(&sm.q_empty[s], kSoftmaxThreads);
+      mbar_init(&sm.q_tmem[s], kSoftmaxThreads);
       mbar_init(&sm.full_k[s], 1);
       mbar_init(&sm.k_empty[s], 1);
       mbar_init(&sm.full_v[s], 1);
       mbar_init(&sm.v_empty[s], 1);
     }
-    for (int s = 0; s < kStreams; ++s) {
+    for (int s = 0; s < 2; ++s) {
       mbar_init(&sm.s_full[s], 1);
-      mbar_init(&sm.p_full[s], kStreamThreads);
-      mbar_init(&sm.o_done[s], 1);
+      mbar_init(&sm.p_full[s], kSoftmaxThreads);
     }
+    mbar_init(&sm.pv_done[0], 1);
+    mbar_init(&sm.pv_done[1], 1);
+    mbar_init(&sm.o_free, kSoftmaxThreads);
     mbar_init(&sm.fin, 1);
     sm.abort = 0;
     fence_mbar_init();
@@ -182,6 +208,7 @@ __global__ void __maxnreg__(168) prefill_kernel(const __grid_constant__ CUtensor
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = sm.tmem_base;
+  auto no_zero = [](const Item&) {};
 
   if (warp == kProducerWarp) {
     // -------------------------------------------------------- producer ----
@@ -189,57 +216,71 @@ __global__ void __maxnreg__(168) prefill_kernel(const __grid_constant__ CUtensor
       tma_prefetch_desc(&qmap);
       tma_prefetch_desc(&kmap);
       tma_prefetch_desc(&vmap);
-      mbar_arrive_expect_tx(&sm.bar_q, nstreams * kTileBytes);
-      for (int s = 0; s < nstreams; ++s) {
-        tma_load_3d(sm.q[s], &qmap, &sm.bar_q, 0, h0 + s, q0 + qt * kRows);
-        tma_load_3d(sm.q[s] + kHalfBytes, &qmap, &sm.bar_q, 64, h0 + s, q0 + qt * kRows);
-      }
     }
-    const int32_t* bt = a.block_tables + static_cast<int64_t>(b) * a.bt_stride;
-    int ids = 0, k_issued = 0, v_issued = 0;
+    int w = blockIdx.x, qi = 0, g = 0, q_issued = 0, k_issued = 0, v_issued = 0;
     bool ok = true;
-    for (int j = 0; j < n_kv; ++j) {
-      // warp-uniform stop decision (lane 0's view of the abort flag)
-      if (__shfl_sync(0xffffffffu, (ok ? 0 : 1) | sm.abort, 0)) break;
-      if ((j & 31) == 0 && a.paged) {  // block ids of tiles j .. j+31, one per lane
-        const int jj = j + lane;
-        int blk = 0;
-        if (jj < n_kv) {
-          blk = bt[jj];
-          if (blk < 0 || blk >= a.num_blocks) {
-            if (a.err) atomicOr(a.err, kErrBadBlockId);
-            blk = a.num_blocks;  // fully outside the tensor map: zero fill
-          }
-        }
-        ids = blk;
-      }
-      const int blk = __shfl_sync(0xffffffffu, ids, j & 31);
-      const int row = a.paged ? blk * kKeys : kv_row0 + j * kKeys;
-      const int st = j % kStages;
+    Item it;
+    while (ok && next_item(a, w, total, it, no_zero)) {
+      const int qs = qi % kStages;
       if (lane == 0) {
-        if (j >= kStages && !mbar_wait(&sm.k_empty[st], ((j / kStages) - 1) & 1)) {
+        if (qi >= kStages && !mbar_wait(&sm.q_empty[qs], ((qi / kStages) - 1) & 1)) {
           ok = false;
         } else {
-          mbar_arrive_expect_tx(&sm.full_k[st], kTileBytes);
-          tma_load_3d(sm.k[st], &kmap, &sm.full_k[st], 0, g, row);
-          tma_load_3d(sm.k[st] + kHalfBytes, &kmap, &sm.full_k[st], 64, g, row);
-          ++k_issued;
-          if (j >= kStages && !mbar_wait(&sm.v_empty[st], ((j / kStages) - 1) & 1)) {
-            ok = false;
-          } else {
-            mbar_arrive_expect_tx(&sm.full_v[st], kTileBytes);
-            tma_load_3d(sm.v[st], &vmap, &sm.full_v[st], 0, g, row);
-            tma_load_3d(sm.v[st] + kHalfBytes, &vmap, &sm.full_v[st], 64, g, row);
-            ++v_issued;
-          }
+          mbar_arrive_expect_tx(&sm.q_full[qs], kTileBytes);
+          tma_load_3d(sm.q[qs], &qmap, &sm.q_full[qs], 0, it.h, it.q0 + it.qt * kRows);
+          tma_load_3d(sm.q[qs] + kHalfBytes, &qmap, &sm.q_full[qs], 64, it.h, it.q0 + it.qt * kRows);
+          ++q_issued;
         }
       }
       ok = __shfl_sync(0xffffffffu, ok, 0);
+      const int kvh = it.h / a.qpk;
+      const int32_t* bt = a.block_tables + static_cast<int64_t>(it.b) * a.bt_stride;
+      int ids = 0;
+      for (int j = 0; ok && j < it.n_kv; ++j, ++g) {
+        if (__shfl_sync(0xffffffffu, sm.abort, 0)) { ok = false; break; }
+        if ((j & 31) == 0 && a.paged) {  // block ids of tiles j .. j+31, one per lane
+          const int jj = j + lane;
+          int blk = 0;
+          if (jj < it.n_kv) {
+            blk = bt[jj];
+            if (blk < 0 || blk >= a.num_blocks) {
+              if (a.err) atomicOr(a.err, kErrBadBlockId);
+              blk = a.num_blocks;  // fully outside the tensor map: zero fill
+            }
+          }
+          ids = blk;
+        }
+        const int blk = __shfl_sync(0xffffffffu, ids, j & 31);
+        const int row = a.paged ? blk * kKeys : it.kv_row0 + j * kKeys;
+        const int st = g % kStages;
+        if (lane == 0) {
+          if (g >= kStages && !mbar_wait(&sm.k_empty[st], ((g / kStages) - 1) & 1)) {
+            ok = false;
+          } else {
+            mbar_arrive_expect_tx(&sm.full_k[st], kTileBytes);
+            tma_load_3d(sm.k[st], &kmap, &sm.full_k[st], 0, kvh, row);
+            tma_load_3d(sm.k[st] + kHalfBytes, &kmap, &sm.full_k[st], 64, kvh, row);
+            ++k_issued;
+            if (g >= kStages && !mbar_wait(&sm.v_empty[st], ((g / kStages) - 1) & 1)) {
+              ok = false;
+            } else {
+              mbar_arrive_expect_tx(&sm.full_v[st], kTileBytes);
+              tma_load_3d(sm.v[st], &vmap, &sm.full_v[st], 0, kvh, row);
+              tma_load_3d(sm.v[st] + kHalfBytes, &vmap, &sm.full_v[st], 64, kvh, row);
+              ++v_issued;
+            }
+          }
+        }
+        ok = __shfl_sync(0xffffffffu, ok, 0);
+      }
+      ++qi;
+      w += gridDim.x;
     }
     if (lane == 0) {
       if (!ok) flag_error(a, sm, kErrWaitTimeout);
       // Drain every copy this CTA issued before it may exit.
-      (void)mbar_wait(&sm.bar_q, 0);
+      for (int j = max(0, q_issued - kStages); j < q_issued; ++j)
+        (void)mbar_wait(&sm.q_full[j % kStages], (j / kStages) & 1);
       for (int j = max(0, k_issued - kStages); j < k_issued; ++j)
         (void)mbar_wait(&sm.full_k[j % kStages], (j / kStages) & 1);
       for (int j = max(0, v_issued - kStages); j < v_issued; ++j)
@@ -250,150 +291,250 @@ __global__ void __maxnreg__(168) prefill_kernel(const __grid_constant__ CUtensor
     if (lane == 0) {
       constexpr uint32_t idesc_qk = umma_idesc_bf16(kRows, kKeys, false);
       constexpr uint32_t idesc_pv = umma_idesc_bf16(kRows, kD, true);
-      auto issue_s = [&](int s, int j) {  // S_s(j) = Q_s K(j)^T
-        const uint32_t q_addr = smem_u32(sm.q[s]);
-        const uint32_t k_addr = smem_u32(sm.k[j % kStages]);
+      bool ok = true;
+      // S(g) = Q(item qi) K(g)^T into S buffer g % 2 (A from TMEM, B from smem)
+      auto issue_s = [&](int g, int qi) -> bool {
+        const int st = g % kStages;
+        if (!mbar_wait(&sm.full_k[st], (g / kStages) & 1)) return false;
+        tc_fence_after();
+        const uint32_t k_addr = smem_u32(sm.k[st]);
+        const uint32_t q_col = tmem + kColQ + (qi % 2) * 64;
 #pragma unroll
         for (int kk = 0; kk < kD / 16; ++kk) {
           const uint32_t off = (kk >> 2) * kHalfBytes + (kk & 3) * 32;
-          umma_f16_ss(tmem + s * kKeys, smem_desc_sw128(q_addr + off, 16, 1024),
-                      smem_desc_sw128(k_addr + off, 16, 1024), idesc_qk, kk > 0);
+          umma_f16_ts(tmem + (g % 2) * kKeys, q_col + kk * 8, smem_desc_sw128(k_addr + off, 16, 1024), idesc_qk,
+                      kk > 0);
         }
-        umma_commit(&sm.s_full[s]);
+        umma_commit(&sm.s_full[g % 2]);
+        umma_commit(&sm.k_empty[st]);
+        return true;
       };
-      auto issue_pv = [&](int s, int j) {  // O_s += P_s(j) V(j)
-        const uint32_t v_addr = smem_u32(sm.v[j % kStages]);
-#pragma unroll
-        for (int kk = 0; kk < kKeys / 16; ++kk) {
-          const uint64_t vb = smem_desc_sw128(v_addr + kk * 16 * 128, kHalfBytes, 1024);
-          umma_f16_ts(tmem + 256 + s * kD, tmem + s * kKeys + kk * 8, vb, idesc_pv, (j > 0 || kk > 0) ? 1u : 0u);
-        }
-        umma_commit(&sm.o_done[s]);
-      };
-      bool ok = mbar_wait(&sm.bar_q, 0) && mbar_wait(&sm.full_k[0], 0);
-      if (ok) {
+      // S of an item's first two tiles, once its Q is in TMEM
+      auto start_item = [&](const Item& it, int g0, int qi) -> bool {
+        if (!mbar_wait(&sm.q_tmem[qi % 2], (qi / 2) & 1)) return false;
         tc_fence_after();
-        for (int s = 0; s < nstreams; ++s) issue_s(s, 0);
-        umma_commit(&sm.k_empty[0]);
-      }
-      for (int j = 0; ok && j < n_kv; ++j) {
-        const int st = j % kStages;
-        if (!mbar_wait(&sm.full_v[st], (j / kStages) & 1)) { ok = false; break; }
-        const bool more = j + 1 < n_kv;
-        for (int s = 0; ok && s < nstreams; ++s) {
-          if (!mbar_wait(&sm.p_full[s], j & 1)) { ok = false; break; }
-          if (s == 0 && more && !mbar_wait(&sm.full_k[(j + 1) % kStages], ((j + 1) / kStages) & 1)) {
+        for (int j = 0; j < 2 && j < it.n_kv; ++j)
+          if (!issue_s(g0 + j, qi)) return false;
+        return true;
+      };
+      int w = blockIdx.x, qi = 0, g = 0;
+      Item it;
+      bool have = next_item(a, w, total, it, no_zero);
+      if (have) ok = start_item(it, 0, 0);
+      while (ok && have) {
+        for (int j = 0; j < it.n_kv; ++j, ++g) {
+          const int b2 = g % 2, st = g % kStages;
+          if (!mbar_wait(&sm.p_full[b2], (g / 2) & 1) || !mbar_wait(&sm.full_v[st], (g / kStages) & 1) ||
+              (j == 0 && qi > 0 && !mbar_wait(&sm.o_free, (qi - 1) & 1))) {
             ok = false;
             break;
           }
           tc_fence_after();
-          issue_pv(s, j);
-          if (s == nstreams - 1) umma_commit(&sm.v_empty[st]);
-          if (more) {
-            issue_s(s, j + 1);
-            if (s == nstreams - 1) umma_commit(&sm.k_empty[(j + 1) % kStages]);
+          const uint32_t v_addr = smem_u32(sm.v[st]);
+#pragma unroll
+          for (int kk = 0; kk < kKeys / 16; ++kk) {
+            const uint64_t vb = smem_desc_sw128(v_addr + kk * 16 * 128, kHalfBytes, 1024);
+            umma_f16_ts(tmem + kColO, tmem + b2 * kKeys + kk * 8, vb, idesc_pv, (j > 0 || kk > 0) ? 1u : 0u);
+          }
+          umma_commit(&sm.v_empty[st]);
+          umma_commit(&sm.pv_done[b2]);
+          if (j + 2 < it.n_kv && !issue_s(g + 2, qi)) {
+            ok = false;
+            break;
           }
         }
+        if (!ok) break;
+        ++qi;
+        w += gridDim.x;
+        have = next_item(a, w, total, it, no_zero);
+        if (have) ok = start_item(it, g, qi);
       }
       if (!ok) flag_error(a, sm, kErrWaitTimeout);
       // All MMAs of this CTA complete before TMEM is released.
       umma_commit(&sm.fin);
       (void)mbar_wait(&sm.fin, 0);
     }
-  } else if (stream < nstreams) {
+  } else {
     // --------------------------------------------------------- softmax ----
-    const int lim = (i < lq) ? (lk - lq + i) : (lk - 1);
-    const uint32_t t_lane = static_cast<uint32_t>((warp & 3) * 32) << 16;
-    const uint32_t tmem_s = tmem + stream * kKeys + t_lane;
-    const uint32_t tmem_o = tmem + 256 + stream * kD + t_lane;
-    float m = -INFINITY, l = 0.f;
-    bool ok = true;
-    for (int j = 0; j < n_kv; ++j) {
-      // warp-uniform outcome: the tcgen05.ld/st below need a converged warp
-      if (!__all_sync(0xffffffffu, mbar_wait(&sm.s_full[stream], j & 1))) { ok = false; break; }
-      tc_fence_after();
-      const int kbase = j * kKeys;
-      // The whole 128-key S row in one round of TMEM loads.
-      uint32_t sr[4][32];
+    const int r = tid;  // query row within the tile = TMEM lane
+    const uint32_t t_lane = static_cast<uint32_t>(warp * 32) << 16;
+    const uint32_t tmem_o = tmem + kColO + t_lane;
+    // Rows of an item that sees no key: zeros (no tile work).
+    auto zero_rows = [&](const Item& z) {
+      const int i = z.qt * kRows + r;
+      if (i < z.lq) {
+        __nv_bfloat16* row = a.out + (static_cast<int64_t>(z.q0 + i) * a.num_heads + z.h) * kD;
+        for (int c = 0; c < kD; c += 8) *reinterpret_cast<uint4*>(row + c) = make_uint4(0, 0, 0, 0);
+      }
+    };
+    // Q row r of item qi from its staging buffer into TMEM (the A operand of S).
+    auto copy_q = [&](int qi) -> bool {
+      const int qs = qi % kStages;
+      if (!__all_sync(0xffffffffu, mbar_wait(&sm.q_full[qs], (qi / kStages) & 1))) return false;
+      uint32_t words[2][32];
 #pragma unroll
-      for (int c = 0; c < 4; ++c) tmem_ld32(tmem_s + c * 32, sr[c]);
-      tmem_ld_wait();
-      if (kbase + kKeys - 1 > lim) {
+      for (int hf = 0; hf < 2; ++hf) {
+        const uint8_t* base = sm.q[qs] + hf * kHalfBytes + r * 128;
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {  // 16-byte chunk c of the row sits at chunk c ^ (r % 8) (128-byte swizzle)
+          const uint4 v4 = *reinterpret_cast<const uint4*>(base + ((c ^ (r & 7)) << 4));
+          words[hf][4 * c + 0] = v4.x;
+          words[hf][4 * c + 1] = v4.y;
+          words[hf][4 * c + 2] = v4.z;
+          words[hf][4 * c + 3] = v4.w;
+        }
+      }
+      // (the stage is released after this item's epilogue, which uses it as scratch)
+      const uint32_t q_col = tmem + kColQ + (qi % 2) * 64 + t_lane;
+      tmem_st32(q_col, words[0]);
+      tmem_st32(q_col + 32, words[1]);
+      tmem_st_wait();
+      tc_fence_before();
+      mbar_arrive(&sm.q_tmem[qi % 2]);
+      return true;
+    };
+    int w = blockIdx.x, qi = 0, g = 0;
+    bool ok = true;
+    Item it;
+    bool have = next_item(a, w, total, it, zero_rows);
+    if (have) ok = copy_q(0);
+    while (ok && have) {
+      const int i = it.qt * kRows + r;
+      const int lim = (i < it.lq) ? (it.lk - it.lq + i) : (it.lk - 1);
+      float m = -INFINITY, l = 0.f;
+      for (int j = 0; j < it.n_kv; ++j, ++g) {
+        const int b2 = g % 2;
+        const uint32_t tmem_s = tmem + b2 * kKeys + t_lane;
+        // warp-uniform outcome: the tcgen05.ld/st below need a converged warp
+        if (!__all_sync(0xffffffffu, mbar_wait(&sm.s_full[b2], (g / 2) & 1))) { ok = false; break; }
+        tc_fence_after();
+        const int kbase = j * kKeys;
+        uint32_t sr[4][32];
+#pragma unroll
+        for (int c = 0; c < 4; ++c) tmem_ld32(tmem_s + c * 32, sr[c]);
+        tmem_ld_wait();
+        if (kbase + kKeys - 1 > lim) {
+#pragma unroll
+          for (int c = 0; c < 4; ++c)
+#pragma unroll
+            for (int e = 0; e < 32; ++e)
+              if (kbase + c * 32 + e > lim) sr[c][e] = __float_as_uint(-INFINITY);
+        }
+        // The max is taken over raw scores (scale > 0), the scale folded into
+        // the exponent's FMA below; max is exact, so its order is free.
+        float mx0 = -INFINITY, mx1 = -INFINITY;
 #pragma unroll
         for (int c = 0; c < 4; ++c)
 #pragma unroll
-          for (int e = 0; e < 32; ++e)
-            if (kbase + c * 32 + e > lim) sr[c][e] = __float_as_uint(-INFINITY);
-      }
-      // The max is taken over raw scores (scale > 0), the scale folded into
-      // the exponent's FMA below; max is exact, so its order is free.
-      float mx0 = -INFINITY, mx1 = -INFINITY;
-#pragma unroll
-      for (int c = 0; c < 4; ++c)
-#pragma unroll
-        for (int e = 0; e < 32; e += 4) {
-          mx0 = fmax3(mx0, __uint_as_float(sr[c][e]), __uint_as_float(sr[c][e + 1]));
-          mx1 = fmax3(mx1, __uint_as_float(sr[c][e + 2]), __uint_as_float(sr[c][e + 3]));
+          for (int e = 0; e < 32; e += 4) {
+            mx0 = fmax3(mx0, __uint_as_float(sr[c][e]), __uint_as_float(sr[c][e + 1]));
+            mx1 = fmax3(mx1, __uint_as_float(sr[c][e + 2]), __uint_as_float(sr[c][e + 3]));
+          }
+        const float mt = fmaxf(mx0, mx1) * a.scale_log2;
+        const float m_new = fmaxf(m, mt);
+        const bool resc = m_new > m + kRescaleThreshold;
+        const float alpha = resc ? fast_exp2(m - m_new) : 1.f;
+        if (resc) {
+          l *= alpha;
+          m = m_new;
         }
-      const float mt = fmaxf(mx0, mx1) * a.scale_log2;
-      const float m_new = fmaxf(m, mt);
-      const bool resc = m_new > m + kRescaleThreshold;
-      const float alpha = resc ? fast_exp2(m - m_new) : 1.f;
-      if (resc) {
-        l *= alpha;
-        m = m_new;
-      }
-      const float neg_mu = (m == -INFINITY) ? 0.f : -m;
-      const float sc = a.scale_log2;
-      float sum[4] = {0.f, 0.f, 0.f, 0.f};  // independent add chains
-      // P over the first 64 columns of the S buffer (S is in registers now):
-      // column k holds keys 2k and 2k+1 of this row as a bf16 pair.
+        const float neg_mu = (m == -INFINITY) ? 0.f : -m;
+        const float sc = a.scale_log2;
+        float sum[4] = {0.f, 0.f, 0.f, 0.f};  // independent add chains
+        // P over the first 64 columns of the S buffer: column k holds keys 2k
+        // and 2k+1 of this row as a bf16 pair; word e of P overwrites score
+        // e, already read at pair e / 2 <= e.
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {  // 32 keys -> 16 columns at a time
-        // word e of P overwrites score e, already read at pair e / 2 <= e
+        for (int c = 0; c < 4; ++c) {
 #pragma unroll
-        for (int e = 0; e < 16; ++e) {
-          const float p0 = fast_exp2(fmaf(__uint_as_float(sr[c][2 * e]), sc, neg_mu));
-          const float p1 = fast_exp2(fmaf(__uint_as_float(sr[c][2 * e + 1]), sc, neg_mu));
-          sum[(2 * e) & 3] += p0;
-          sum[(2 * e + 1) & 3] += p1;
-          sr[c][e] = pack_bf16x2(p0, p1);
+          for (int e = 0; e < 16; ++e) {
+            const float p0 = fast_exp2(fmaf(__uint_as_float(sr[c][2 * e]), sc, neg_mu));
+            const float p1 = fast_exp2(fmaf(__uint_as_float(sr[c][2 * e + 1]), sc, neg_mu));
+            sum[(2 * e) & 3] += p0;
+            sum[(2 * e + 1) & 3] += p1;
+            sr[c][e] = pack_bf16x2(p0, p1);
+          }
+          tmem_st16_first(tmem_s + c * 16, sr[c]);
         }
-        tmem_st16_first(tmem_s + c * 16, sr[c]);
+        l += (sum[0] + sum[1]) + (sum[2] + sum[3]);
+        // O rows of this warp rescale (rarely) once P V(j-1) is complete,
+        // before this tile's P is signalled and P V(j) issued.
+        if (j > 0 && __any_sync(0xffffffffu, resc)) {
+          if (!__all_sync(0xffffffffu, mbar_wait(&sm.pv_done[(g - 1) % 2], ((g - 1) / 2) & 1))) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          rescale_o(tmem_o, alpha);
+        }
+        tmem_st_wait();
+        tc_fence_before();
+        mbar_arrive(&sm.p_full[b2]);
       }
-      l += (sum[0] + sum[1]) + (sum[2] + sum[3]);
-      // S_s(j) has landed, so P V(j-1) -- issued before it -- is complete: O
-      // may be rescaled now (rows of this warp, when one of them needs it),
-      // before this tile's P is signalled and P V(j) issued.
-      if (j > 0 && __any_sync(0xffffffffu, resc)) rescale_o(tmem_o, alpha);
-      tmem_st_wait();
-      tc_fence_before();
-      mbar_arrive(&sm.p_full[stream]);
-    }
-    if (ok && !__all_sync(0xffffffffu, mbar_wait(&sm.o_done[stream], (n_kv - 1) & 1))) ok = false;
-    if (!ok) {
-      flag_error(a, sm, kErrWaitTimeout);
-    } else {
+      if (!ok) break;
+      // The next item's Q goes into TMEM now, so that its first S tiles are
+      // computed while this item's output is written.
+      const int g_last = g - 1;
+      int w_next = w + gridDim.x;
+      Item nx;
+      const bool have_next = next_item(a, w_next, total, nx, zero_rows);
+      if (have_next && !copy_q(qi + 1)) { ok = false; break; }
+      // P V completes in issue order: the last tile's implies the item's.
+      if (!__all_sync(0xffffffffu, mbar_wait(&sm.pv_done[g_last % 2], (g_last / 2) & 1))) {
+        ok = false;
+        break;
+      }
       tc_fence_after();
+      // Output through the item's Q staging buffer (free since its copy into
+      // TMEM): thread r writes its normalised row there (16-byte chunk c of row
+      // r at chunk c ^ (r % 16): conflict-free), then every warp stores two
+      // whole rows per instruction, so the global writes are coalesced.
       const float inv = l > 0.f ? 1.f / l : 0.f;
+      uint8_t* scratch = sm.q[qi % kStages];
 #pragma unroll 1
       for (int c = 0; c < 4; ++c) {
         uint32_t o[32];
         tmem_ld32(tmem_o + c * 32, o);
         tmem_ld_wait();
-        if (out_row) {
 #pragma unroll
-          for (int q4 = 0; q4 < 4; ++q4) {
-            uint4 wv;
-            wv.x = pack_bf16x2(__uint_as_float(o[q4 * 8 + 0]) * inv, __uint_as_float(o[q4 * 8 + 1]) * inv);
-            wv.y = pack_bf16x2(__uint_as_float(o[q4 * 8 + 2]) * inv, __uint_as_float(o[q4 * 8 + 3]) * inv);
-            wv.z = pack_bf16x2(__uint_as_float(o[q4 * 8 + 4]) * inv, __uint_as_float(o[q4 * 8 + 5]) * inv);
-            wv.w = pack_bf16x2(__uint_as_float(o[q4 * 8 + 6]) * inv, __uint_as_float(o[q4 * 8 + 7]) * inv);
-            *reinterpret_cast<uint4*>(out_row + c * 32 + q4 * 8) = wv;
+        for (int q4 = 0; q4 < 4; ++q4) {
+          uint4 wv;
+          wv.x = pack_bf16x2(__uint_as_float(o[q4 * 8 + 0]) * inv, __uint_as_float(o[q4 * 8 + 1]) * inv);
+          wv.y = pack_bf16x2(__uint_as_float(o[q4 * 8 + 2]) * inv, __uint_as_float(o[q4 * 8 + 3]) * inv);
+          wv.z = pack_bf16x2(__uint_as_float(o[q4 * 8 + 4]) * inv, __uint_as_float(o[q4 * 8 + 5]) * inv);
+          wv.w = pack_bf16x2(__uint_as_float(o[q4 * 8 + 6]) * inv, __uint_as_float(o[q4 * 8 + 7]) * inv);
+          const int chunk = c * 4 + q4;
+          *reinterpret_cast<uint4*>(scratch + r * 256 + ((chunk ^ (r & 15)) << 4)) = wv;
+        }
+      }
+      // O is read out: the next item's first P V may overwrite it.
+      tc_fence_before();
+      mbar_arrive(&sm.o_free);
+      named_barrier_sync(1, kSoftmaxThreads);
+      {
+        const int c = lane & 15;
+        const int lq_rows = it.lq - it.qt * kRows;  // valid rows of this tile
+#pragma unroll 4
+        for (int k = 0; k < 16; ++k) {
+          const int row = warp * 32 + k * 2 + (lane >> 4);
+          if (row < lq_rows) {
+            const uint4 v4 = *reinterpret_cast<const uint4*>(scratch + row * 256 + ((c ^ (row & 15)) << 4));
+            __nv_bfloat16* dst =
+                a.out + (static_cast<int64_t>(it.q0 + it.qt * kRows + row) * a.num_heads + it.h) * kD + c * 8;
+            *reinterpret_cast<uint4*>(dst) = v4;
           }
         }
       }
+      // The scratch reads are done: the stage may take the Q tile of the
+      // item after next (an async-proxy write).
+      fence_proxy_async_smem();
+      mbar_arrive(&sm.q_empty[qi % kStages]);
+      ++qi;
+      w = w_next;
+      it = nx;
+      have = have_next;
     }
+    if (!ok) flag_error(a, sm, kErrWaitTimeout);
   }
 
   tc_fence_before();
@@ -405,14 +546,20 @@ __global__ void __maxnreg__(168) prefill_kernel(const __grid_constant__ CUtensor
   }
 }
 
-int launch_prefill(const CUtensorMap& qm, const CUtensorMap& km, const CUtensorMap& vm, const PrefillArgs& a,
-                   int batch, int max_q_len, cudaStream_t stream) {
+int launch_prefill(const CUtensorMap& qm, const CUtensorMap& km, const CUtensorMap& vm, PrefillArgs a,
+                   int max_q_len, cudaStream_t stream) {
   const size_t smem = sizeof(PrefillSmem) + 1024;
   int rc = ensure_dynamic_smem(reinterpret_cast<const void*>(&prefill_kernel), smem);
   if (rc != NVK_OK) return rc;
-  const int groups = a.paired ? a.num_heads / 2 : a.num_heads;
-  const dim3 grid((max_q_len + kRows - 1) / kRows, groups, batch);
-  return check_cuda(launch_pdl(prefill_kernel, grid, dim3(kThreads), smem, stream, qm, km, vm, a), "prefill launch");
+  int dev = 0, sms = 148;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  a.qtiles = (max_q_len + kRows - 1) / kRows;
+  const int64_t items = static_cast<int64_t>(a.qtiles) * a.num_heads * a.batch;
+  if (items > (int64_t(1) << 30))
+    return fail(NVK_ERR_UNSUPPORTED, "prefill: %lld work items above the kernel's range", (long long)items);
+  const int grid = static_cast<int>(items < sms ? items : sms);
+  return check_cuda(launch_pdl(prefill_kernel, dim3(grid), dim3(kThreads), smem, stream, qm, km, vm, a),
+                    "prefill launch");
 }
 
 int check_common(const void* out, const void* query, int batch, int total_q, int max_q_len, int num_heads,
@@ -465,10 +612,10 @@ extern "C" int nvk_paged_prefill(void* out, const void* query, const void* key_c
   a.num_blocks = num_blocks;
   a.num_heads = num_heads;
   a.qpk = num_heads / num_kv_heads;
-  a.paired = a.qpk % 2 == 0;
   a.paged = 1;
+  a.batch = batch;
   a.scale_log2 = scale * 1.4426950408889634f;
-  return launch_prefill(qm, km, vm, a, batch, max_q_len, reinterpret_cast<cudaStream_t>(stream));
+  return launch_prefill(qm, km, vm, a, max_q_len, reinterpret_cast<cudaStream_t>(stream));
 }
 
 extern "C" int nvk_dense_prefill(void* out, const void* query, const void* key, const void* value,
@@ -496,8 +643,8 @@ extern "C" int nvk_dense_prefill(void* out, const void* query, const void* key, 
   a.num_blocks = 0;
   a.num_heads = num_heads;
   a.qpk = num_heads / num_kv_heads;
-  a.paired = a.qpk % 2 == 0;
   a.paged = 0;
+  a.batch = batch;
   a.scale_log2 = scale * 1.4426950408889634f;
-  return launch_prefill(qm, km, vm, a, batch, max_q_len, reinterpret_cast<cudaStream_t>(stream));
+  return launch_prefill(qm, km, vm, a, max_q_len, reinterpret_cast<cudaStream_t>(stream));
 }
