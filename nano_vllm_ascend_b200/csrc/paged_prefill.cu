@@ -15,25 +15,31 @@
 // Tensor memory (512 columns): S/P double buffered at 0 and 128, O at 256,
 // the item's Q as the A operand of S = Q K^T at 384 / 448 (double buffered
 // across items), so an S UMMA reads only K from shared memory.
-//   warp 4 (producer): per item a TMA load of the Q tile into one of two
+//   warp 8 (producer): per item a TMA load of the Q tile into one of two
 //     staging buffers, then per key tile the K and V tiles (two 64-dim halves
 //     each, 128-byte swizzle = the canonical UMMA operand layout) into
 //     2-stage rings; block ids 32 at a time (one parallel load per warp).
-//   warp 5 (MMA, one elected lane): S(j) = Q K(j)^T (A from TMEM) into S
+//   warp 9 (MMA, one elected lane): S(j) = Q K(j)^T (A from TMEM) into S
 //     buffer j % 2, two tiles ahead of O += P(j) V(j) (P from TMEM where the
 //     softmax wrote it over S(j), V MN-major from smem); S(j+2) is issued
 //     right behind P V(j) (tcgen05.mma executes in issue order, so it
 //     overwrites P(j) only after the P V has read it). An item's first two S
 //     tiles are issued behind the previous item's last P V, while the
 //     softmax warps still write that item's output.
-//   warps 0-3 (softmax): thread r owns query row r = TMEM lane r: per item
-//     the copy of its Q row from the staging buffer into TMEM; per tile the
-//     128-key S row in one round of tcgen05.ld, mask, base-2 online softmax,
-//     P written as bf16 pairs into the first 64 columns of its S buffer
-//     (tcgen05.st), lazy rescaling of O (only when the running max grew by
-//     more than 2^8, after P V(j-1) completed); per item the next item's Q
-//     copy, then the normalised O rows staged in the item's own Q staging
+//   warps 0-7 (softmax, two warpgroups): query row r = TMEM lane r belongs
+//     to thread r of both warpgroups; warpgroup wg handles keys wg*64 ..
+//     wg*64+63 of every tile and dims wg*64 .. wg*64+63 of Q and O, so that
+//     each sub-partition's exponentials spread over two warps. Per item the
+//     copy of the Q row halves from the staging buffer into TMEM; per tile 64
+//     scores in one round of tcgen05.ld, mask, the row max exchanged through
+//     shared memory, base-2 online softmax, P written as bf16 pairs into the
+//     warpgroup's 32 columns of its S buffer (tcgen05.st), lazy rescaling of
+//     its half of O (only when the running max grew by more than 2^8, after
+//     P V(j-1) completed); per item the next item's Q copy, the row sums
+//     exchanged, the normalised O rows staged in the item's own Q staging
 //     buffer (O released) and stored two whole rows per warp instruction.
+// Ten warps put three on one SM sub-partition, whose register file holds
+// 3 x 32 x 168 registers: the kernel is held to 168 registers a thread.
 // Every mbarrier wait is bounded; on a timeout the CTA records the error,
 // drains its in-flight copies and MMAs, frees TMEM and exits.
 #include "host_common.h"
@@ -49,10 +55,10 @@ constexpr int kKeys = 128;                // keys per K/V tile: one 128-token po
 constexpr int kHalfBytes = 128 * 128;     // one 64-dim half of a 128-row tile
 constexpr int kTileBytes = 2 * kHalfBytes;
 constexpr int kStages = 2;                // K, V and Q ring depth
-constexpr int kSoftmaxThreads = 128;
-constexpr int kProducerWarp = 4;
-constexpr int kMmaWarp = 5;
-constexpr int kThreads = 6 * 32;
+constexpr int kSoftmaxThreads = 128;      // per warpgroup; two warpgroups share every row
+constexpr int kProducerWarp = 8;
+constexpr int kMmaWarp = 9;
+constexpr int kThreads = 10 * 32;
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kColO = 256;           // O accumulator
 constexpr uint32_t kColQ = 384;           // Q(item) at kColQ + (item % 2) * 64
@@ -83,11 +89,16 @@ struct PrefillSmem {
   uint64_t full_k[kStages], k_empty[kStages];
   uint64_t full_v[kStages], v_empty[kStages];
   uint64_t s_full[2];   // S(j) in buffer j % 2
-  uint64_t p_full[2];   // P(j) written over it by the 128 softmax threads
+  uint64_t p_full[2];   // P(j) written over it by the 256 softmax threads
   uint64_t pv_done[2];  // O += P V(j) complete, barrier j % 2 (one phase per two tiles, so a
                         // wait is never two phases behind its barrier)
   uint64_t o_free;      // one phase per item: its O has been read out
   uint64_t fin;
+  uint64_t max_ready[2];    // both halves' row maxima of tile j written (barrier j % 2)
+  uint64_t sum_ready;       // both halves' row sums of an item written
+  uint64_t staged;          // an item's normalised rows are in the staging buffer
+  float rowmax[2][2][kRows];  // [tile parity][warpgroup][row]: per-half row maxima
+  float rowsum[2][kRows];     // [warpgroup][row]: per-half row sums of an item
   uint32_t tmem_base;
   volatile int abort;
 };
@@ -144,15 +155,10 @@ __device__ __forceinline__ void tmem_st16_first(uint32_t taddr, const uint32_t (
       : "memory");
 }
 
-// Barrier `id` (not 0, which __syncthreads uses) among `count` threads.
-__device__ __forceinline__ void named_barrier_sync(int id, int count) {
-  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
-}
-
-// O row of this thread (four 32-column chunks) times alpha, in TMEM.
-__device__ __forceinline__ void rescale_o(uint32_t tmem_o, float alpha) {
+// Half (64 columns) of this thread's O row times alpha, in TMEM.
+__device__ __forceinline__ void rescale_o_half(uint32_t tmem_o, float alpha) {
 #pragma unroll 1
-  for (int c = 0; c < 4; ++c) {
+  for (int c = 0; c < 2; ++c) {
     uint32_t o[32];
     tmem_ld32(tmem_o + c * 32, o);
     tmem_ld_wait();
@@ -167,7 +173,7 @@ __device__ __forceinline__ void flag_error(const PrefillArgs& a, PrefillSmem& sm
   sm.abort = 1;
 }
 
-__global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_constant__ CUtensorMap qmap,
+__global__ void __maxnreg__(168) prefill_kernel(const __grid_constant__ CUtensorMap qmap,
                                                               const __grid_constant__ CUtensorMap kmap,
                                                               const __grid_constant__ CUtensorMap vmap,
                                                               const PrefillArgs a) {
@@ -182,8 +188,8 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
   if (tid == 0) {
     for (int s = 0; s < kStages; ++s) {
       mbar_init(&sm.q_full[s], 1);
-      mbar_init(&sm.q_empty[s], kSoftmaxThreads);
-      mbar_init(&sm.q_tmem[s], kSoftmaxThreads);
+      mbar_init(&sm.q_empty[s], 2 * kSoftmaxThreads);
+      mbar_init(&sm.q_tmem[s], 2 * kSoftmaxThreads);
       mbar_init(&sm.full_k[s], 1);
       mbar_init(&sm.k_empty[s], 1);
       mbar_init(&sm.full_v[s], 1);
@@ -191,11 +197,15 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
     }
     for (int s = 0; s < 2; ++s) {
       mbar_init(&sm.s_full[s], 1);
-      mbar_init(&sm.p_full[s], kSoftmaxThreads);
+      mbar_init(&sm.p_full[s], 2 * kSoftmaxThreads);
     }
     mbar_init(&sm.pv_done[0], 1);
     mbar_init(&sm.pv_done[1], 1);
-    mbar_init(&sm.o_free, kSoftmaxThreads);
+    mbar_init(&sm.o_free, 2 * kSoftmaxThreads);
+    mbar_init(&sm.max_ready[0], 2 * kSoftmaxThreads);
+    mbar_init(&sm.max_ready[1], 2 * kSoftmaxThreads);
+    mbar_init(&sm.sum_ready, 2 * kSoftmaxThreads);
+    mbar_init(&sm.staged, 2 * kSoftmaxThreads);
     mbar_init(&sm.fin, 1);
     sm.abort = 0;
     fence_mbar_init();
@@ -356,38 +366,38 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
     }
   } else {
     // --------------------------------------------------------- softmax ----
-    const int r = tid;  // query row within the tile = TMEM lane
-    const uint32_t t_lane = static_cast<uint32_t>(warp * 32) << 16;
-    const uint32_t tmem_o = tmem + kColO + t_lane;
-    // Rows of an item that sees no key: zeros (no tile work).
+    // Two warpgroups share every row: warpgroup wg takes keys wg*64 .. wg*64+63
+    // of each tile (and dims wg*64 .. of Q and O); both track the same running
+    // max, exchanged once per tile, and their own row sums.
+    const int wg = warp >> 2;               // 0 or 1
+    const int r = tid & (kRows - 1);        // query row within the tile = TMEM lane
+    const uint32_t t_lane = static_cast<uint32_t>((warp & 3) * 32) << 16;
+    const uint32_t tmem_o = tmem + kColO + wg * 64 + t_lane;
+    // Rows of an item that sees no key: zeros (each warpgroup its half of the dims).
     auto zero_rows = [&](const Item& z) {
       const int i = z.qt * kRows + r;
       if (i < z.lq) {
-        __nv_bfloat16* row = a.out + (static_cast<int64_t>(z.q0 + i) * a.num_heads + z.h) * kD;
-        for (int c = 0; c < kD; c += 8) *reinterpret_cast<uint4*>(row + c) = make_uint4(0, 0, 0, 0);
+        __nv_bfloat16* row = a.out + (static_cast<int64_t>(z.q0 + i) * a.num_heads + z.h) * kD + wg * 64;
+        for (int c = 0; c < 64; c += 8) *reinterpret_cast<uint4*>(row + c) = make_uint4(0, 0, 0, 0);
       }
     };
-    // Q row r of item qi from its staging buffer into TMEM (the A operand of S).
+    // This warpgroup's half (64 dims) of Q row r of item qi from the staging
+    // buffer into TMEM (the A operand of S).
     auto copy_q = [&](int qi) -> bool {
       const int qs = qi % kStages;
       if (!__all_sync(0xffffffffu, mbar_wait(&sm.q_full[qs], (qi / kStages) & 1))) return false;
-      uint32_t words[2][32];
+      uint32_t words[32];
+      const uint8_t* base = sm.q[qs] + wg * kHalfBytes + r * 128;
 #pragma unroll
-      for (int hf = 0; hf < 2; ++hf) {
-        const uint8_t* base = sm.q[qs] + hf * kHalfBytes + r * 128;
-#pragma unroll
-        for (int c = 0; c < 8; ++c) {  // 16-byte chunk c of the row sits at chunk c ^ (r % 8) (128-byte swizzle)
-          const uint4 v4 = *reinterpret_cast<const uint4*>(base + ((c ^ (r & 7)) << 4));
-          words[hf][4 * c + 0] = v4.x;
-          words[hf][4 * c + 1] = v4.y;
-          words[hf][4 * c + 2] = v4.z;
-          words[hf][4 * c + 3] = v4.w;
-        }
+      for (int c = 0; c < 8; ++c) {  // 16-byte chunk c of the row sits at chunk c ^ (r % 8) (128-byte swizzle)
+        const uint4 v4 = *reinterpret_cast<const uint4*>(base + ((c ^ (r & 7)) << 4));
+        words[4 * c + 0] = v4.x;
+        words[4 * c + 1] = v4.y;
+        words[4 * c + 2] = v4.z;
+        words[4 * c + 3] = v4.w;
       }
       // (the stage is released after this item's epilogue, which uses it as scratch)
-      const uint32_t q_col = tmem + kColQ + (qi % 2) * 64 + t_lane;
-      tmem_st32(q_col, words[0]);
-      tmem_st32(q_col + 32, words[1]);
+      tmem_st32(tmem + kColQ + (qi % 2) * 64 + wg * 32 + t_lane, words);
       tmem_st_wait();
       tc_fence_before();
       mbar_arrive(&sm.q_tmem[qi % 2]);
@@ -408,14 +418,14 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
         // warp-uniform outcome: the tcgen05.ld/st below need a converged warp
         if (!__all_sync(0xffffffffu, mbar_wait(&sm.s_full[b2], (g / 2) & 1))) { ok = false; break; }
         tc_fence_after();
-        const int kbase = j * kKeys;
-        uint32_t sr[4][32];
-#pragma unroll
-        for (int c = 0; c < 4; ++c) tmem_ld32(tmem_s + c * 32, sr[c]);
+        const int kbase = j * kKeys + wg * 64;
+        uint32_t sr[2][32];
+        tmem_ld32(tmem_s + wg * 64, sr[0]);
+        tmem_ld32(tmem_s + wg * 64 + 32, sr[1]);
         tmem_ld_wait();
-        if (kbase + kKeys - 1 > lim) {
+        if (kbase + 63 > lim) {
 #pragma unroll
-          for (int c = 0; c < 4; ++c)
+          for (int c = 0; c < 2; ++c)
 #pragma unroll
             for (int e = 0; e < 32; ++e)
               if (kbase + c * 32 + e > lim) sr[c][e] = __float_as_uint(-INFINITY);
@@ -424,13 +434,21 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
         // the exponent's FMA below; max is exact, so its order is free.
         float mx0 = -INFINITY, mx1 = -INFINITY;
 #pragma unroll
-        for (int c = 0; c < 4; ++c)
+        for (int c = 0; c < 2; ++c)
 #pragma unroll
           for (int e = 0; e < 32; e += 4) {
             mx0 = fmax3(mx0, __uint_as_float(sr[c][e]), __uint_as_float(sr[c][e + 1]));
             mx1 = fmax3(mx1, __uint_as_float(sr[c][e + 2]), __uint_as_float(sr[c][e + 3]));
           }
-        const float mt = fmaxf(mx0, mx1) * a.scale_log2;
+        // Row max over both halves: exchanged through shared memory (one slot
+        // per tile parity, so the next tile's writes cannot race these reads).
+        // (it also orders both warpgroups' score reads before the P writes below)
+        sm.rowmax[b2][wg][r] = fmaxf(mx0, mx1);
+        tc_fence_before();
+        mbar_arrive(&sm.max_ready[b2]);
+        if (!__all_sync(0xffffffffu, mbar_wait(&sm.max_ready[b2], (g / 2) & 1))) { ok = false; break; }
+        tc_fence_after();
+        const float mt = fmaxf(sm.rowmax[b2][0][r], sm.rowmax[b2][1][r]) * a.scale_log2;
         const float m_new = fmaxf(m, mt);
         const bool resc = m_new > m + kRescaleThreshold;
         const float alpha = resc ? fast_exp2(m - m_new) : 1.f;
@@ -441,31 +459,31 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
         const float neg_mu = (m == -INFINITY) ? 0.f : -m;
         const float sc = a.scale_log2;
         float sum[4] = {0.f, 0.f, 0.f, 0.f};  // independent add chains
-        // P over the first 64 columns of the S buffer: column k holds keys 2k
-        // and 2k+1 of this row as a bf16 pair; word e of P overwrites score
-        // e, already read at pair e / 2 <= e.
+        // P of keys wg*64 .. wg*64+63 into columns wg*32 .. wg*32+31 of the S
+        // buffer (column k holds keys 2k and 2k+1 as a bf16 pair): columns
+        // whose scores both warpgroups read before the exchange above.
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
+        for (int c = 0; c < 2; ++c) {
 #pragma unroll
-          for (int e = 0; e < 16; ++e) {
+          for (int e = 0; e < 16; ++e) {  // word e of P overwrites score e, already read
             const float p0 = fast_exp2(fmaf(__uint_as_float(sr[c][2 * e]), sc, neg_mu));
             const float p1 = fast_exp2(fmaf(__uint_as_float(sr[c][2 * e + 1]), sc, neg_mu));
             sum[(2 * e) & 3] += p0;
             sum[(2 * e + 1) & 3] += p1;
             sr[c][e] = pack_bf16x2(p0, p1);
           }
-          tmem_st16_first(tmem_s + c * 16, sr[c]);
+          tmem_st16_first(tmem_s + wg * 32 + c * 16, sr[c]);
         }
         l += (sum[0] + sum[1]) + (sum[2] + sum[3]);
-        // O rows of this warp rescale (rarely) once P V(j-1) is complete,
-        // before this tile's P is signalled and P V(j) issued.
+        // This warpgroup's half of the O rows rescales (rarely) once P V(j-1)
+        // is complete, before this tile's P is signalled and P V(j) issued.
         if (j > 0 && __any_sync(0xffffffffu, resc)) {
           if (!__all_sync(0xffffffffu, mbar_wait(&sm.pv_done[(g - 1) % 2], ((g - 1) / 2) & 1))) {
             ok = false;
             break;
           }
           tc_fence_after();
-          rescale_o(tmem_o, alpha);
+          rescale_o_half(tmem_o, alpha);
         }
         tmem_st_wait();
         tc_fence_before();
@@ -479,20 +497,28 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
       Item nx;
       const bool have_next = next_item(a, w_next, total, nx, zero_rows);
       if (have_next && !copy_q(qi + 1)) { ok = false; break; }
+      sm.rowsum[wg][r] = l;
+      mbar_arrive(&sm.sum_ready);
       // P V completes in issue order: the last tile's implies the item's.
       if (!__all_sync(0xffffffffu, mbar_wait(&sm.pv_done[g_last % 2], (g_last / 2) & 1))) {
         ok = false;
         break;
       }
+      if (!__all_sync(0xffffffffu, mbar_wait(&sm.sum_ready, qi & 1))) {  // both row sums written
+        ok = false;
+        break;
+      }
       tc_fence_after();
       // Output through the item's Q staging buffer (free since its copy into
-      // TMEM): thread r writes its normalised row there (16-byte chunk c of row
-      // r at chunk c ^ (r % 16): conflict-free), then every warp stores two
-      // whole rows per instruction, so the global writes are coalesced.
-      const float inv = l > 0.f ? 1.f / l : 0.f;
+      // TMEM): thread r writes its half of the normalised row there (16-byte
+      // chunk c of row r at chunk c ^ (r % 16): conflict-free), then every
+      // warp stores two whole rows per instruction, so the global writes are
+      // coalesced.
+      const float lt = sm.rowsum[0][r] + sm.rowsum[1][r];
+      const float inv = lt > 0.f ? 1.f / lt : 0.f;
       uint8_t* scratch = sm.q[qi % kStages];
 #pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
+      for (int c = 0; c < 2; ++c) {
         uint32_t o[32];
         tmem_ld32(tmem_o + c * 32, o);
         tmem_ld_wait();
@@ -503,20 +529,24 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
           wv.y = pack_bf16x2(__uint_as_float(o[q4 * 8 + 2]) * inv, __uint_as_float(o[q4 * 8 + 3]) * inv);
           wv.z = pack_bf16x2(__uint_as_float(o[q4 * 8 + 4]) * inv, __uint_as_float(o[q4 * 8 + 5]) * inv);
           wv.w = pack_bf16x2(__uint_as_float(o[q4 * 8 + 6]) * inv, __uint_as_float(o[q4 * 8 + 7]) * inv);
-          const int chunk = c * 4 + q4;
+          const int chunk = wg * 8 + c * 4 + q4;
           *reinterpret_cast<uint4*>(scratch + r * 256 + ((chunk ^ (r & 15)) << 4)) = wv;
         }
       }
       // O is read out: the next item's first P V may overwrite it.
       tc_fence_before();
       mbar_arrive(&sm.o_free);
-      named_barrier_sync(1, kSoftmaxThreads);
+      mbar_arrive(&sm.staged);
+      if (!__all_sync(0xffffffffu, mbar_wait(&sm.staged, qi & 1))) {  // the staged rows are complete
+        ok = false;
+        break;
+      }
       {
         const int c = lane & 15;
         const int lq_rows = it.lq - it.qt * kRows;  // valid rows of this tile
 #pragma unroll 4
-        for (int k = 0; k < 16; ++k) {
-          const int row = warp * 32 + k * 2 + (lane >> 4);
+        for (int k = 0; k < 8; ++k) {
+          const int row = warp * 16 + k * 2 + (lane >> 4);
           if (row < lq_rows) {
             const uint4 v4 = *reinterpret_cast<const uint4*>(scratch + row * 256 + ((c ^ (row & 15)) << 4));
             __nv_bfloat16* dst =
