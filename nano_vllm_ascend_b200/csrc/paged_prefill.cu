@@ -8,36 +8,35 @@
 // lengths. Masking is bottom-right aligned: query i of a sequence with Lq
 // queries and Lk keys sees key j iff j <= Lk - Lq + i.
 //
-// Work item = 128 query rows of one sequence x one query head. The grid is
-// persistent (one CTA per SM); CTA c takes items c, c + C, c + 2C, ... in an
-// order that puts the heaviest query tiles first. Per item the 128-key K and
-// V tiles (one pool block each) stream through shared memory.
-// Tensor memory (512 columns): S/P double buffered at 0 and 128, O at 256,
-// the item's Q as the A operand of S = Q K^T at 384 / 448 (double buffered
-// across items), so an S UMMA reads only K from shared memory.
-//   warp 8 (producer): per item a TMA load of the Q tile into one of two
-//     staging buffers, then per key tile the K and V tiles (two 64-dim halves
-//     each, 128-byte swizzle = the canonical UMMA operand layout) into
-//     2-stage rings; block ids 32 at a time (one parallel load per warp).
-//   warp 9 (MMA, one elected lane): S(j) = Q K(j)^T (A from TMEM) into S
-//     buffer j % 2, two tiles ahead of O += P(j) V(j) (P from TMEM where the
-//     softmax wrote it over S(j), V MN-major from smem); S(j+2) is issued
-//     right behind P V(j) (tcgen05.mma executes in issue order, so it
-//     overwrites P(j) only after the P V has read it). An item's first two S
-//     tiles are issued behind the previous item's last P V, while the
-//     softmax warps still write that item's output.
-//   warps 0-7 (softmax, two warpgroups): query row r = TMEM lane r belongs
-//     to thread r of both warpgroups; warpgroup wg handles keys wg*64 ..
-//     wg*64+63 of every tile and dims wg*64 .. wg*64+63 of Q and O, so that
-//     each sub-partition's exponentials spread over two warps. Per item the
-//     copy of the Q row halves from the staging buffer into TMEM; per tile 64
-//     scores in one round of tcgen05.ld, mask, the row max exchanged through
-//     shared memory, base-2 online softmax, P written as bf16 pairs into the
-//     warpgroup's 32 columns of its S buffer (tcgen05.st), lazy rescaling of
-//     its half of O (only when the running max grew by more than 2^8, after
-//     P V(j-1) completed); per item the next item's Q copy, the row sums
-//     exchanged, the normalised O rows staged in the item's own Q staging
-//     buffer (O released) and stored two whole rows per warp instruction.
+// Work item = 128 query rows of one sequence x two query heads of one GQA
+// group ("streams" 0 and 1; one stream when the group size is odd). Both
+// streams read the same 128-key K and V tiles (one pool block each), so each
+// K/V byte staged in shared memory feeds two heads. The grid is persistent
+// (one CTA per SM); CTA c takes items c, c + C, c + 2C, ... in an order that
+// puts the heaviest query tiles first.
+// Tensor memory (512 columns): S/P of stream s at s * 128, its O accumulator
+// at 256 + s * 128.
+//   warp 8 (producer): per item the TMA loads of the streams' Q tiles (each
+//     as soon as the previous item's last S of that stream has read its
+//     buffer), then per key tile the K and V tiles (two 64-dim halves each,
+//     128-byte swizzle = the canonical UMMA operand layout) into 2-stage
+//     rings; block ids 32 at a time (one parallel load per warp).
+//   warp 9 (MMA; the whole warp runs the loop, an elected lane issues):
+//     per tile j and stream s, once P_s(j) is written, O_s += P_s(j) V(j)
+//     (P read from TMEM where the softmax wrote it over S_s, V MN-major from
+//     smem) and right behind it S_s(j+1) = Q_s K(j+1)^T into the same
+//     columns. tcgen05.mma executes in issue order, so S_s(j+1) overwrites
+//     P_s(j) only after the P V has read it, and the tensor pipe has the
+//     other stream's work queued while one stream's softmax runs. An item's
+//     first S tiles are issued behind the previous item's last P V.
+//   warps 0-3 / 4-7 (softmax of stream 0 / 1): thread r owns query row r =
+//     TMEM lane r. Per tile the 128 scores of its row in one round of
+//     tcgen05.ld, the mask, base-2 online softmax, P written as bf16 pairs
+//     over the first 64 columns of S_s (tcgen05.st), lazy rescaling of O_s
+//     (only when the running max grew by more than 2^8; S_s(j) having landed
+//     means P V_s(j-1), issued before it, is complete). Per item the
+//     normalised O_s row is stored once the item's last P V_s completed,
+//     which releases O_s to the next item.
 // Ten warps put three on one SM sub-partition, whose register file holds
 // 3 x 32 x 168 registers: the kernel is held to 168 registers a thread.
 // Every mbarrier wait is bounded; on a timeout the CTA records the error,
@@ -54,15 +53,16 @@ constexpr int kRows = 128;                // query rows per item (UMMA M)
 constexpr int kKeys = 128;                // keys per K/V tile: one 128-token pool block
 constexpr int kHalfBytes = 128 * 128;     // one 64-dim half of a 128-row tile
 constexpr int kTileBytes = 2 * kHalfBytes;
-constexpr int kStages = 2;                // K, V and Q ring depth
-constexpr int kSoftmaxThreads = 128;      // per warpgroup; two warpgroups share every row
+constexpr int kStages = 2;                // K and V ring depth
+constexpr int kStreams = 2;               // query heads per item
+constexpr int kStreamThreads = 128;       // softmax threads per stream
 constexpr int kProducerWarp = 8;
 constexpr int kMmaWarp = 9;
 constexpr int kThreads = 10 * 32;
-constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kColO = 256;           // O accumulator
-constexpr uint32_t kColQ = 384;           // Q(item) at kColQ + (item % 2) * 64
+constexpr uint32_t kTmemCols = 512;       // S_0 | S_1 | O_0 | O_1, 128 columns each
+constexpr uint32_t kColO = 256;
 constexpr float kRescaleThreshold = 8.0f;
+constexpr int kItemRing = 4;              // item descriptors published ahead by the producer
 
 struct PrefillArgs {
   __nv_bfloat16* out;
@@ -75,49 +75,56 @@ struct PrefillArgs {
   int num_blocks;
   int num_heads;
   int qpk;
+  int paired;  // two heads per item (GQA group size even)
   int paged;
   int batch;
   int qtiles;  // query tiles of the longest sequence
   float scale_log2;
 };
 
+// One work item: query tile qt of heads h0 .. h0 + streams - 1 of sequence b
+// (n_kv < 0: no further item).
+struct Item {
+  int qt, h0, kvh, b, q0, lq, lk, kv_row0, n_kv;
+};
+
 struct PrefillSmem {
-  alignas(1024) uint8_t q[kStages][kTileBytes];
+  alignas(1024) uint8_t q[kStreams][kTileBytes];
   alignas(1024) uint8_t k[kStages][kTileBytes];
   alignas(1024) uint8_t v[kStages][kTileBytes];
-  uint64_t q_full[kStages], q_empty[kStages], q_tmem[kStages];
+  alignas(1024) uint8_t stage[kStreams][kHalfBytes];  // epilogue: 64 dims of 128 output rows per stream
+  Item items[kItemRing];
+  uint64_t item_full[kItemRing];                 // items[i % ring] written (one phase per use)
+  uint64_t q_full[kStreams], q_empty[kStreams];  // one phase per item
   uint64_t full_k[kStages], k_empty[kStages];
   uint64_t full_v[kStages], v_empty[kStages];
-  uint64_t s_full[2];   // S(j) in buffer j % 2
-  uint64_t p_full[2];   // P(j) written over it by the 256 softmax threads
-  uint64_t pv_done[2];  // O += P V(j) complete, barrier j % 2 (one phase per two tiles, so a
-                        // wait is never two phases behind its barrier)
-  uint64_t o_free;      // one phase per item: its O has been read out
+  uint64_t s_full[kStreams];   // S_s(j) in TMEM (and, in issue order, P V_s(j-1) done)
+  uint64_t p_full[kStreams];   // P_s(j) written by the stream's 128 softmax threads
+  uint64_t o_ready[kStreams];  // an item's last P V_s complete (one phase per item)
+  uint64_t o_free[kStreams];   // an item's O_s read out (one phase per item)
+  uint64_t staged[kStreams];   // a 64-dim half of an item's rows is in stage[s] (two phases per item)
+  uint64_t drained[kStreams];  // stage[s] copied out to global memory (two phases per item)
   uint64_t fin;
-  uint64_t max_ready[2];    // both halves' row maxima of tile j written (barrier j % 2)
-  uint64_t sum_ready;       // both halves' row sums of an item written
-  uint64_t staged;          // an item's normalised rows are in the staging buffer
-  float rowmax[2][2][kRows];  // [tile parity][warpgroup][row]: per-half row maxima
-  float rowsum[2][kRows];     // [warpgroup][row]: per-half row sums of an item
   uint32_t tmem_base;
   volatile int abort;
 };
 
 static_assert(sizeof(PrefillSmem) + 1024 <= 232448, "prefill shared memory exceeds one SM's 227 KB");
 
-// One work item: query tile qt of head h of sequence b. Every role walks the
-// same list; `next` skips items without rows and reports their key tiles.
-struct Item {
-  int w, qt, h, b, q0, lq, lk, kv_row0, n_kv;
-};
+// The producer walks the item list; `next_item` skips items without rows and
+// hands the ones whose rows see no key to `zero_rows`.
+__device__ __forceinline__ int item_streams(const PrefillArgs& a) { return a.paired ? kStreams : 1; }
 
 __device__ __forceinline__ bool load_item(const PrefillArgs& a, int w, Item& it) {
-  const int per_tile = a.num_heads * a.batch;
-  it.w = w;
-  it.qt = a.qtiles - 1 - w / per_tile;  // heaviest (last) query tiles first
-  const int rem = w - (a.qtiles - 1 - it.qt) * per_tile;
-  it.h = rem % a.num_heads;
-  it.b = rem / a.num_heads;
+  const int ns = item_streams(a);
+  const int groups = a.num_heads / ns;  // head groups per sequence
+  const int per_tile = groups * a.batch;
+  const int t = w / per_tile;
+  it.qt = a.qtiles - 1 - t;  // heaviest (last) query tiles first
+  const int rem = w - t * per_tile;
+  it.h0 = (rem % groups) * ns;
+  it.kvh = it.h0 / a.qpk;  // both heads of a pair share it: h0 even, group size even
+  it.b = rem / groups;
   it.q0 = a.cu_q[it.b];
   it.lq = a.cu_q[it.b + 1] - it.q0;
   if (it.qt * kRows >= it.lq) return false;
@@ -129,8 +136,6 @@ __device__ __forceinline__ bool load_item(const PrefillArgs& a, int w, Item& it)
   return true;
 }
 
-// Next item of this CTA at or after list position w that has key tiles
-// (items with rows but no visible key are handed to `zero_rows`).
 template <typename ZeroRows>
 __device__ __forceinline__ bool next_item(const PrefillArgs& a, int& w, int total, Item& it, ZeroRows&& zero_rows) {
   for (; w < total; w += gridDim.x) {
@@ -155,31 +160,18 @@ __device__ __forceinline__ void tmem_st16_first(uint32_t taddr, const uint32_t (
       : "memory");
 }
 
-// Half (64 columns) of this thread's O row times alpha, in TMEM.
-__device__ __forceinline__ void rescale_o_half(uint32_t tmem_o, float alpha) {
-#pragma unroll 1
-  for (int c = 0; c < 2; ++c) {
-    uint32_t o[32];
-    tmem_ld32(tmem_o + c * 32, o);
-    tmem_ld_wait();
-#pragma unroll
-    for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
-    tmem_st32(tmem_o + c * 32, o);
-  }
-}
-
 __device__ __forceinline__ void flag_error(const PrefillArgs& a, PrefillSmem& sm, int code) {
   if (a.err) atomicOr(a.err, code);
   sm.abort = 1;
 }
 
 __global__ void __maxnreg__(168) prefill_kernel(const __grid_constant__ CUtensorMap qmap,
-                                                              const __grid_constant__ CUtensorMap kmap,
-                                                              const __grid_constant__ CUtensorMap vmap,
-                                                              const PrefillArgs a) {
+                                                const __grid_constant__ CUtensorMap kmap,
+                                                const __grid_constant__ CUtensorMap vmap, const PrefillArgs a) {
   pdl_launch_dependents();
   pdl_wait();
-  const int total = a.qtiles * a.num_heads * a.batch;
+  const int ns = item_streams(a);
+  const int total = a.qtiles * (a.num_heads / ns) * a.batch;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
 
   extern __shared__ uint8_t smem_raw[];
@@ -187,25 +179,22 @@ __global__ void __maxnreg__(168) prefill_kernel(const __grid_constant__ CUtensor
       *reinterpret_cast<PrefillSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   if (tid == 0) {
     for (int s = 0; s < kStages; ++s) {
-      mbar_init(&sm.q_full[s], 1);
-      mbar_init(&sm.q_empty[s], 2 * kSoftmaxThreads);
-      mbar_init(&sm.q_tmem[s], 2 * kSoftmaxThreads);
       mbar_init(&sm.full_k[s], 1);
       mbar_init(&sm.k_empty[s], 1);
       mbar_init(&sm.full_v[s], 1);
       mbar_init(&sm.v_empty[s], 1);
     }
-    for (int s = 0; s < 2; ++s) {
+    for (int s = 0; s < kStreams; ++s) {
+      mbar_init(&sm.q_full[s], 1);
+      mbar_init(&sm.q_empty[s], 1);
       mbar_init(&sm.s_full[s], 1);
-      mbar_init(&sm.p_full[s], 2 * kSoftmaxThreads);
+      mbar_init(&sm.p_full[s], kStreamThreads);
+      mbar_init(&sm.o_ready[s], 1);
+      mbar_init(&sm.o_free[s], kStreamThreads);
+      mbar_init(&sm.staged[s], kStreamThreads);
+      mbar_init(&sm.drained[s], kStreamThreads);
     }
-    mbar_init(&sm.pv_done[0], 1);
-    mbar_init(&sm.pv_done[1], 1);
-    mbar_init(&sm.o_free, 2 * kSoftmaxThreads);
-    mbar_init(&sm.max_ready[0], 2 * kSoftmaxThreads);
-    mbar_init(&sm.max_ready[1], 2 * kSoftmaxThreads);
-    mbar_init(&sm.sum_ready, 2 * kSoftmaxThreads);
-    mbar_init(&sm.staged, 2 * kSoftmaxThreads);
+    for (int i = 0; i < kItemRing; ++i) mbar_init(&sm.item_full[i], 1);
     mbar_init(&sm.fin, 1);
     sm.abort = 0;
     fence_mbar_init();
@@ -218,7 +207,6 @@ __global__ void __maxnreg__(168) prefill_kernel(const __grid_constant__ CUtensor
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = sm.tmem_base;
-  auto no_zero = [](const Item&) {};
 
   if (warp == kProducerWarp) {
     // -------------------------------------------------------- producer ----
@@ -227,23 +215,40 @@ __global__ void __maxnreg__(168) prefill_kernel(const __grid_constant__ CUtensor
       tma_prefetch_desc(&kmap);
       tma_prefetch_desc(&vmap);
     }
-    int w = blockIdx.x, qi = 0, g = 0, q_issued = 0, k_issued = 0, v_issued = 0;
+    // Rows of an item that sees no key: zeros (two rows per warp instruction).
+    auto zero_rows = [&](const Item& z) {
+      const int rows = min(kRows, z.lq - z.qt * kRows);
+      for (int s = 0; s < ns; ++s)
+        for (int rr = lane >> 4; rr < rows; rr += 2) {
+          __nv_bfloat16* row = a.out + (static_cast<int64_t>(z.q0 + z.qt * kRows + rr) * a.num_heads + z.h0 + s) * kD;
+          *reinterpret_cast<uint4*>(row + (lane & 15) * 8) = make_uint4(0, 0, 0, 0);
+        }
+    };
+    int w = blockIdx.x, qi = 0, g = 0, k_issued = 0, v_issued = 0;
     bool ok = true;
-    Item it;
-    while (ok && next_item(a, w, total, it, no_zero)) {
-      const int qs = qi % kStages;
+    while (true) {
+      Item it;
+      const bool have = next_item(a, w, total, it, zero_rows);
       if (lane == 0) {
-        if (qi >= kStages && !mbar_wait(&sm.q_empty[qs], ((qi / kStages) - 1) & 1)) {
-          ok = false;
-        } else {
-          mbar_arrive_expect_tx(&sm.q_full[qs], kTileBytes);
-          tma_load_3d(sm.q[qs], &qmap, &sm.q_full[qs], 0, it.h, it.q0 + it.qt * kRows);
-          tma_load_3d(sm.q[qs] + kHalfBytes, &qmap, &sm.q_full[qs], 64, it.h, it.q0 + it.qt * kRows);
-          ++q_issued;
+        // The Q buffers, and with them the ring slot (read by every role
+        // before the previous item's last S), are free once the previous
+        // item's last S of each stream has completed.
+        for (int s = 0; s < ns && ok && qi > 0; ++s)
+          if (!mbar_wait(&sm.q_empty[s], (qi - 1) & 1)) ok = false;
+        Item& slot = sm.items[qi % kItemRing];
+        slot = it;
+        if (!have || !ok) slot.n_kv = -1;
+        mbar_arrive(&sm.item_full[qi % kItemRing]);
+        if (have && ok) {
+          for (int s = 0; s < ns; ++s) {
+            mbar_arrive_expect_tx(&sm.q_full[s], kTileBytes);
+            tma_load_3d(sm.q[s], &qmap, &sm.q_full[s], 0, it.h0 + s, it.q0 + it.qt * kRows);
+            tma_load_3d(sm.q[s] + kHalfBytes, &qmap, &sm.q_full[s], 64, it.h0 + s, it.q0 + it.qt * kRows);
+          }
         }
       }
       ok = __shfl_sync(0xffffffffu, ok, 0);
-      const int kvh = it.h / a.qpk;
+      if (!have || !ok) break;
       const int32_t* bt = a.block_tables + static_cast<int64_t>(it.b) * a.bt_stride;
       int ids = 0;
       for (int j = 0; ok && j < it.n_kv; ++j, ++g) {
@@ -268,15 +273,15 @@ __global__ void __maxnreg__(168) prefill_kernel(const __grid_constant__ CUtensor
             ok = false;
           } else {
             mbar_arrive_expect_tx(&sm.full_k[st], kTileBytes);
-            tma_load_3d(sm.k[st], &kmap, &sm.full_k[st], 0, kvh, row);
-            tma_load_3d(sm.k[st] + kHalfBytes, &kmap, &sm.full_k[st], 64, kvh, row);
+            tma_load_3d(sm.k[st], &kmap, &sm.full_k[st], 0, it.kvh, row);
+            tma_load_3d(sm.k[st] + kHalfBytes, &kmap, &sm.full_k[st], 64, it.kvh, row);
             ++k_issued;
             if (g >= kStages && !mbar_wait(&sm.v_empty[st], ((g / kStages) - 1) & 1)) {
               ok = false;
             } else {
               mbar_arrive_expect_tx(&sm.full_v[st], kTileBytes);
-              tma_load_3d(sm.v[st], &vmap, &sm.full_v[st], 0, kvh, row);
-              tma_load_3d(sm.v[st] + kHalfBytes, &vmap, &sm.full_v[st], 64, kvh, row);
+              tma_load_3d(sm.v[st], &vmap, &sm.full_v[st], 0, it.kvh, row);
+              tma_load_3d(sm.v[st] + kHalfBytes, &vmap, &sm.full_v[st], 64, it.kvh, row);
               ++v_issued;
             }
           }
@@ -285,12 +290,15 @@ __global__ void __maxnreg__(168) prefill_kernel(const __grid_constant__ CUtensor
       }
       ++qi;
       w += gridDim.x;
+      if (!ok) break;
     }
     if (lane == 0) {
       if (!ok) flag_error(a, sm, kErrWaitTimeout);
-      // Drain every copy this CTA issued before it may exit.
-      for (int j = max(0, q_issued - kStages); j < q_issued; ++j)
-        (void)mbar_wait(&sm.q_full[j % kStages], (j / kStages) & 1);
+      // Drain every copy this CTA issued before it may exit (a Q buffer is
+      // reloaded only after its previous load was consumed, so only the last
+      // load of each stream can be in flight).
+      for (int s = 0; s < ns; ++s)
+        if (qi > 0) (void)mbar_wait(&sm.q_full[s], (qi - 1) & 1);
       for (int j = max(0, k_issued - kStages); j < k_issued; ++j)
         (void)mbar_wait(&sm.full_k[j % kStages], (j / kStages) & 1);
       for (int j = max(0, v_issued - kStages); j < v_issued; ++j)
@@ -298,157 +306,133 @@ __global__ void __maxnreg__(168) prefill_kernel(const __grid_constant__ CUtensor
     }
   } else if (warp == kMmaWarp) {
     // ------------------------------------------------------------- MMA ----
-    if (lane == 0) {
-      constexpr uint32_t idesc_qk = umma_idesc_bf16(kRows, kKeys, false);
-      constexpr uint32_t idesc_pv = umma_idesc_bf16(kRows, kD, true);
-      bool ok = true;
-      // S(g) = Q(item qi) K(g)^T into S buffer g % 2 (A from TMEM, B from smem)
-      auto issue_s = [&](int g, int qi) -> bool {
-        const int st = g % kStages;
-        if (!mbar_wait(&sm.full_k[st], (g / kStages) & 1)) return false;
-        tc_fence_after();
-        const uint32_t k_addr = smem_u32(sm.k[st]);
-        const uint32_t q_col = tmem + kColQ + (qi % 2) * 64;
+    constexpr uint32_t idesc_qk = umma_idesc_bf16(kRows, kKeys, false);
+    constexpr uint32_t idesc_pv = umma_idesc_bf16(kRows, kD, true);
+    bool ok = true;
+    auto wait_all = [](uint64_t* bar, uint32_t parity) { return __all_sync(0xffffffffu, mbar_wait(bar, parity)); };
+    auto commit = [](uint64_t* bar) {
+      if (elect_one_sync()) umma_commit(bar);
+      __syncwarp();
+    };
+    auto issue_s = [&](int s, int st) {  // S_s = Q_s K(stage st)^T
+      const uint32_t q_addr = smem_u32(sm.q[s]);
+      const uint32_t k_addr = smem_u32(sm.k[st]);
 #pragma unroll
-        for (int kk = 0; kk < kD / 16; ++kk) {
-          const uint32_t off = (kk >> 2) * kHalfBytes + (kk & 3) * 32;
-          umma_f16_ts(tmem + (g % 2) * kKeys, q_col + kk * 8, smem_desc_sw128(k_addr + off, 16, 1024), idesc_qk,
-                      kk > 0);
+      for (int kk = 0; kk < kD / 16; ++kk) {
+        const uint32_t off = (kk >> 2) * kHalfBytes + (kk & 3) * 32;
+        const uint64_t qa = smem_desc_sw128(q_addr + off, 16, 1024);
+        const uint64_t kb = smem_desc_sw128(k_addr + off, 16, 1024);
+        if (elect_one_sync()) umma_f16_ss(tmem + s * kKeys, qa, kb, idesc_qk, kk > 0);
+        __syncwarp();
+      }
+      commit(&sm.s_full[s]);
+    };
+    auto issue_pv = [&](int s, int st, bool first) {  // O_s (+)= P_s V(stage st)
+      const uint32_t v_addr = smem_u32(sm.v[st]);
+#pragma unroll
+      for (int kk = 0; kk < kKeys / 16; ++kk) {
+        const uint64_t vb = smem_desc_sw128(v_addr + kk * 16 * 128, kHalfBytes, 1024);
+        if (elect_one_sync())
+          umma_f16_ts(tmem + kColO + s * kD, tmem + s * kKeys + kk * 8, vb, idesc_pv, (!first || kk > 0) ? 1u : 0u);
+        __syncwarp();
+      }
+    };
+    int qi = 0, g = 0;
+    while (ok) {
+      if (!wait_all(&sm.item_full[qi % kItemRing], (qi / kItemRing) & 1)) { ok = false; break; }
+      const Item it = sm.items[qi % kItemRing];
+      if (it.n_kv < 0) break;
+      // First S tiles of the item: behind the previous item's last P V in
+      // issue order, so they overwrite its P only after it was read.
+      {
+        const int st = g % kStages;
+        if (!wait_all(&sm.full_k[st], (g / kStages) & 1)) { ok = false; break; }
+        for (int s = 0; s < ns && ok; ++s) {
+          if (!wait_all(&sm.q_full[s], qi & 1)) { ok = false; break; }
+          tc_fence_after();
+          issue_s(s, st);
+          if (it.n_kv == 1) commit(&sm.q_empty[s]);
         }
-        umma_commit(&sm.s_full[g % 2]);
-        umma_commit(&sm.k_empty[st]);
-        return true;
-      };
-      // S of an item's first two tiles, once its Q is in TMEM
-      auto start_item = [&](const Item& it, int g0, int qi) -> bool {
-        if (!mbar_wait(&sm.q_tmem[qi % 2], (qi / 2) & 1)) return false;
-        tc_fence_after();
-        for (int j = 0; j < 2 && j < it.n_kv; ++j)
-          if (!issue_s(g0 + j, qi)) return false;
-        return true;
-      };
-      int w = blockIdx.x, qi = 0, g = 0;
-      Item it;
-      bool have = next_item(a, w, total, it, no_zero);
-      if (have) ok = start_item(it, 0, 0);
-      while (ok && have) {
-        for (int j = 0; j < it.n_kv; ++j, ++g) {
-          const int b2 = g % 2, st = g % kStages;
-          if (!mbar_wait(&sm.p_full[b2], (g / 2) & 1) || !mbar_wait(&sm.full_v[st], (g / kStages) & 1) ||
-              (j == 0 && qi > 0 && !mbar_wait(&sm.o_free, (qi - 1) & 1))) {
+        if (!ok) break;
+        commit(&sm.k_empty[st]);
+      }
+      for (int j = 0; j < it.n_kv && ok; ++j, ++g) {
+        const int st = g % kStages, st1 = (g + 1) % kStages;
+        const bool more = j + 1 < it.n_kv;
+        if (!wait_all(&sm.full_v[st], (g / kStages) & 1) ||
+            (more && !wait_all(&sm.full_k[st1], ((g + 1) / kStages) & 1))) {
+          ok = false;
+          break;
+        }
+        for (int s = 0; s < ns; ++s) {
+          if (!wait_all(&sm.p_full[s], g & 1) || (j == 0 && qi > 0 && !wait_all(&sm.o_free[s], (qi - 1) & 1))) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t v_addr = smem_u32(sm.v[st]);
-#pragma unroll
-          for (int kk = 0; kk < kKeys / 16; ++kk) {
-            const uint64_t vb = smem_desc_sw128(v_addr + kk * 16 * 128, kHalfBytes, 1024);
-            umma_f16_ts(tmem + kColO, tmem + b2 * kKeys + kk * 8, vb, idesc_pv, (j > 0 || kk > 0) ? 1u : 0u);
-          }
-          umma_commit(&sm.v_empty[st]);
-          umma_commit(&sm.pv_done[b2]);
-          if (j + 2 < it.n_kv && !issue_s(g + 2, qi)) {
-            ok = false;
-            break;
+          issue_pv(s, st, j == 0);
+          if (more) {
+            issue_s(s, st1);
+            if (j + 2 == it.n_kv) commit(&sm.q_empty[s]);  // the item's last S_s
+          } else {
+            commit(&sm.o_ready[s]);
           }
         }
         if (!ok) break;
-        ++qi;
-        w += gridDim.x;
-        have = next_item(a, w, total, it, no_zero);
-        if (have) ok = start_item(it, g, qi);
+        commit(&sm.v_empty[st]);
+        if (more) commit(&sm.k_empty[st1]);
       }
-      if (!ok) flag_error(a, sm, kErrWaitTimeout);
-      // All MMAs of this CTA complete before TMEM is released.
-      umma_commit(&sm.fin);
-      (void)mbar_wait(&sm.fin, 0);
+      ++qi;
     }
-  } else {
+    if (!ok && lane == 0) flag_error(a, sm, kErrWaitTimeout);
+    // All MMAs of this CTA complete before TMEM is released.
+    commit(&sm.fin);
+    (void)mbar_wait(&sm.fin, 0);
+  } else if ((warp >> 2) < ns) {
     // --------------------------------------------------------- softmax ----
-    // Two warpgroups share every row: warpgroup wg takes keys wg*64 .. wg*64+63
-    // of each tile (and dims wg*64 .. of Q and O); both track the same running
-    // max, exchanged once per tile, and their own row sums.
-    const int wg = warp >> 2;               // 0 or 1
-    const int r = tid & (kRows - 1);        // query row within the tile = TMEM lane
+    const int s = warp >> 2;
+    const int r = tid & (kStreamThreads - 1);  // query row within the tile = TMEM lane
     const uint32_t t_lane = static_cast<uint32_t>((warp & 3) * 32) << 16;
-    const uint32_t tmem_o = tmem + kColO + wg * 64 + t_lane;
-    // Rows of an item that sees no key: zeros (each warpgroup its half of the dims).
-    auto zero_rows = [&](const Item& z) {
-      const int i = z.qt * kRows + r;
-      if (i < z.lq) {
-        __nv_bfloat16* row = a.out + (static_cast<int64_t>(z.q0 + i) * a.num_heads + z.h) * kD + wg * 64;
-        for (int c = 0; c < 64; c += 8) *reinterpret_cast<uint4*>(row + c) = make_uint4(0, 0, 0, 0);
-      }
-    };
-    // This warpgroup's half (64 dims) of Q row r of item qi from the staging
-    // buffer into TMEM (the A operand of S).
-    auto copy_q = [&](int qi) -> bool {
-      const int qs = qi % kStages;
-      if (!__all_sync(0xffffffffu, mbar_wait(&sm.q_full[qs], (qi / kStages) & 1))) return false;
-      uint32_t words[32];
-      const uint8_t* base = sm.q[qs] + wg * kHalfBytes + r * 128;
-#pragma unroll
-      for (int c = 0; c < 8; ++c) {  // 16-byte chunk c of the row sits at chunk c ^ (r % 8) (128-byte swizzle)
-        const uint4 v4 = *reinterpret_cast<const uint4*>(base + ((c ^ (r & 7)) << 4));
-        words[4 * c + 0] = v4.x;
-        words[4 * c + 1] = v4.y;
-        words[4 * c + 2] = v4.z;
-        words[4 * c + 3] = v4.w;
-      }
-      // (the stage is released after this item's epilogue, which uses it as scratch)
-      tmem_st32(tmem + kColQ + (qi % 2) * 64 + wg * 32 + t_lane, words);
-      tmem_st_wait();
-      tc_fence_before();
-      mbar_arrive(&sm.q_tmem[qi % 2]);
-      return true;
-    };
-    int w = blockIdx.x, qi = 0, g = 0;
+    const uint32_t tmem_s = tmem + s * kKeys + t_lane;
+    const uint32_t tmem_o = tmem + kColO + s * kD + t_lane;
+    const float sc = a.scale_log2;
+    uint8_t* stage = sm.stage[s];
+    int qi = 0, g = 0;
     bool ok = true;
-    Item it;
-    bool have = next_item(a, w, total, it, zero_rows);
-    if (have) ok = copy_q(0);
-    while (ok && have) {
+    while (ok) {
+      if (!__all_sync(0xffffffffu, mbar_wait(&sm.item_full[qi % kItemRing], (qi / kItemRing) & 1))) {
+        ok = false;
+        break;
+      }
+      const Item it = sm.items[qi % kItemRing];
+      if (it.n_kv < 0) break;
       const int i = it.qt * kRows + r;
       const int lim = (i < it.lq) ? (it.lk - it.lq + i) : (it.lk - 1);
       float m = -INFINITY, l = 0.f;
       for (int j = 0; j < it.n_kv; ++j, ++g) {
-        const int b2 = g % 2;
-        const uint32_t tmem_s = tmem + b2 * kKeys + t_lane;
         // warp-uniform outcome: the tcgen05.ld/st below need a converged warp
-        if (!__all_sync(0xffffffffu, mbar_wait(&sm.s_full[b2], (g / 2) & 1))) { ok = false; break; }
+        if (!__all_sync(0xffffffffu, mbar_wait(&sm.s_full[s], g & 1))) { ok = false; break; }
         tc_fence_after();
-        const int kbase = j * kKeys + wg * 64;
-        uint32_t sr[2][32];
-        tmem_ld32(tmem_s + wg * 64, sr[0]);
-        tmem_ld32(tmem_s + wg * 64 + 32, sr[1]);
-        tmem_ld_wait();
-        if (kbase + 63 > lim) {
+        const int kbase = j * kKeys;
+        uint32_t sr[4][32];
 #pragma unroll
-          for (int c = 0; c < 2; ++c)
+        for (int c = 0; c < 4; ++c) tmem_ld32(tmem_s + c * 32, sr[c]);
+        tmem_ld_wait();
+        if (kbase + kKeys - 1 > lim) {
+#pragma unroll
+          for (int c = 0; c < 4; ++c)
 #pragma unroll
             for (int e = 0; e < 32; ++e)
               if (kbase + c * 32 + e > lim) sr[c][e] = __float_as_uint(-INFINITY);
         }
         // The max is taken over raw scores (scale > 0), the scale folded into
         // the exponent's FMA below; max is exact, so its order is free.
-        float mx0 = -INFINITY, mx1 = -INFINITY;
+        float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
-        for (int c = 0; c < 2; ++c)
+        for (int c = 0; c < 4; ++c)
 #pragma unroll
-          for (int e = 0; e < 32; e += 4) {
-            mx0 = fmax3(mx0, __uint_as_float(sr[c][e]), __uint_as_float(sr[c][e + 1]));
-            mx1 = fmax3(mx1, __uint_as_float(sr[c][e + 2]), __uint_as_float(sr[c][e + 3]));
-          }
-        // Row max over both halves: exchanged through shared memory (one slot
-        // per tile parity, so the next tile's writes cannot race these reads).
-        // (it also orders both warpgroups' score reads before the P writes below)
-        sm.rowmax[b2][wg][r] = fmaxf(mx0, mx1);
-        tc_fence_before();
-        mbar_arrive(&sm.max_ready[b2]);
-        if (!__all_sync(0xffffffffu, mbar_wait(&sm.max_ready[b2], (g / 2) & 1))) { ok = false; break; }
-        tc_fence_after();
-        const float mt = fmaxf(sm.rowmax[b2][0][r], sm.rowmax[b2][1][r]) * a.scale_log2;
+          for (int e = 0; e < 32; e += 2) mx[c] = fmax3(mx[c], __uint_as_float(sr[c][e]), __uint_as_float(sr[c][e + 1]));
+        const float mt = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])) * sc;
         const float m_new = fmaxf(m, mt);
         const bool resc = m_new > m + kRescaleThreshold;
         const float alpha = resc ? fast_exp2(m - m_new) : 1.f;
@@ -457,112 +441,96 @@ __global__ void __maxnreg__(168) prefill_kernel(const __grid_constant__ CUtensor
           m = m_new;
         }
         const float neg_mu = (m == -INFINITY) ? 0.f : -m;
-        const float sc = a.scale_log2;
         float sum[4] = {0.f, 0.f, 0.f, 0.f};  // independent add chains
-        // P of keys wg*64 .. wg*64+63 into columns wg*32 .. wg*32+31 of the S
-        // buffer (column k holds keys 2k and 2k+1 as a bf16 pair): columns
-        // whose scores both warpgroups read before the exchange above.
+        // P over the first 64 columns of S_s (column k holds keys 2k and 2k+1
+        // as a bf16 pair): word e of chunk c overwrites score e, already read.
 #pragma unroll
-        for (int c = 0; c < 2; ++c) {
+        for (int c = 0; c < 4; ++c) {
 #pragma unroll
-          for (int e = 0; e < 16; ++e) {  // word e of P overwrites score e, already read
+          for (int e = 0; e < 16; ++e) {
             const float p0 = fast_exp2(fmaf(__uint_as_float(sr[c][2 * e]), sc, neg_mu));
             const float p1 = fast_exp2(fmaf(__uint_as_float(sr[c][2 * e + 1]), sc, neg_mu));
             sum[(2 * e) & 3] += p0;
             sum[(2 * e + 1) & 3] += p1;
             sr[c][e] = pack_bf16x2(p0, p1);
           }
-          tmem_st16_first(tmem_s + wg * 32 + c * 16, sr[c]);
+          tmem_st16_first(tmem_s + c * 16, sr[c]);
         }
         l += (sum[0] + sum[1]) + (sum[2] + sum[3]);
-        // This warpgroup's half of the O rows rescales (rarely) once P V(j-1)
-        // is complete, before this tile's P is signalled and P V(j) issued.
+        // O_s rescales (rarely) before this tile's P is signalled: S_s(j)
+        // landed, so P V_s(j-1) is complete.
         if (j > 0 && __any_sync(0xffffffffu, resc)) {
-          if (!__all_sync(0xffffffffu, mbar_wait(&sm.pv_done[(g - 1) % 2], ((g - 1) / 2) & 1))) {
-            ok = false;
-            break;
+#pragma unroll 1
+          for (int c = 0; c < 4; ++c) {
+            uint32_t o[32];
+            tmem_ld32(tmem_o + c * 32, o);
+            tmem_ld_wait();
+#pragma unroll
+            for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
+            tmem_st32(tmem_o + c * 32, o);
           }
-          tc_fence_after();
-          rescale_o_half(tmem_o, alpha);
         }
         tmem_st_wait();
         tc_fence_before();
-        mbar_arrive(&sm.p_full[b2]);
+        mbar_arrive(&sm.p_full[s]);
       }
       if (!ok) break;
-      // The next item's Q goes into TMEM now, so that its first S tiles are
-      // computed while this item's output is written.
-      const int g_last = g - 1;
-      int w_next = w + gridDim.x;
-      Item nx;
-      const bool have_next = next_item(a, w_next, total, nx, zero_rows);
-      if (have_next && !copy_q(qi + 1)) { ok = false; break; }
-      sm.rowsum[wg][r] = l;
-      mbar_arrive(&sm.sum_ready);
-      // P V completes in issue order: the last tile's implies the item's.
-      if (!__all_sync(0xffffffffu, mbar_wait(&sm.pv_done[g_last % 2], (g_last / 2) & 1))) {
-        ok = false;
-        break;
-      }
-      if (!__all_sync(0xffffffffu, mbar_wait(&sm.sum_ready, qi & 1))) {  // both row sums written
-        ok = false;
-        break;
-      }
+      // The item's last P V_s complete: normalise the O_s rows and store them
+      // through stage[s], one 64-dim half at a time: thread r writes its row
+      // half there (16-byte chunk c of row r at chunk c ^ (r % 8): conflict
+      // free), then each warp stores four whole 128-byte row halves per
+      // instruction, so the global writes are coalesced.
+      if (!__all_sync(0xffffffffu, mbar_wait(&sm.o_ready[s], qi & 1))) { ok = false; break; }
       tc_fence_after();
-      // Output through the item's Q staging buffer (free since its copy into
-      // TMEM): thread r writes its half of the normalised row there (16-byte
-      // chunk c of row r at chunk c ^ (r % 16): conflict-free), then every
-      // warp stores two whole rows per instruction, so the global writes are
-      // coalesced.
-      const float lt = sm.rowsum[0][r] + sm.rowsum[1][r];
-      const float inv = lt > 0.f ? 1.f / lt : 0.f;
-      uint8_t* scratch = sm.q[qi % kStages];
+      const float inv = l > 0.f ? 1.f / l : 0.f;
+      const int rows = min(kRows, it.lq - it.qt * kRows);
+      const int wq = warp & 3;
 #pragma unroll 1
-      for (int c = 0; c < 2; ++c) {
-        uint32_t o[32];
-        tmem_ld32(tmem_o + c * 32, o);
-        tmem_ld_wait();
-#pragma unroll
-        for (int q4 = 0; q4 < 4; ++q4) {
-          uint4 wv;
-          wv.x = pack_bf16x2(__uint_as_float(o[q4 * 8 + 0]) * inv, __uint_as_float(o[q4 * 8 + 1]) * inv);
-          wv.y = pack_bf16x2(__uint_as_float(o[q4 * 8 + 2]) * inv, __uint_as_float(o[q4 * 8 + 3]) * inv);
-          wv.z = pack_bf16x2(__uint_as_float(o[q4 * 8 + 4]) * inv, __uint_as_float(o[q4 * 8 + 5]) * inv);
-          wv.w = pack_bf16x2(__uint_as_float(o[q4 * 8 + 6]) * inv, __uint_as_float(o[q4 * 8 + 7]) * inv);
-          const int chunk = wg * 8 + c * 4 + q4;
-          *reinterpret_cast<uint4*>(scratch + r * 256 + ((chunk ^ (r & 15)) << 4)) = wv;
+      for (int h = 0; h < 2; ++h) {
+        // the previous half's copy-out has read the buffer
+        if ((qi > 0 || h > 0) && !__all_sync(0xffffffffu, mbar_wait(&sm.drained[s], (h + 1) & 1))) {
+          ok = false;
+          break;
         }
-      }
-      // O is read out: the next item's first P V may overwrite it.
-      tc_fence_before();
-      mbar_arrive(&sm.o_free);
-      mbar_arrive(&sm.staged);
-      if (!__all_sync(0xffffffffu, mbar_wait(&sm.staged, qi & 1))) {  // the staged rows are complete
-        ok = false;
-        break;
-      }
-      {
-        const int c = lane & 15;
-        const int lq_rows = it.lq - it.qt * kRows;  // valid rows of this tile
+#pragma unroll 1
+        for (int c = 0; c < 2; ++c) {
+          uint32_t o[32];
+          tmem_ld32(tmem_o + h * 64 + c * 32, o);
+          tmem_ld_wait();
+#pragma unroll
+          for (int q4 = 0; q4 < 4; ++q4) {
+            const uint32_t x = pack_bf16x2(__uint_as_float(o[q4 * 8 + 0]) * inv, __uint_as_float(o[q4 * 8 + 1]) * inv);
+            const uint32_t y = pack_bf16x2(__uint_as_float(o[q4 * 8 + 2]) * inv, __uint_as_float(o[q4 * 8 + 3]) * inv);
+            const uint32_t z = pack_bf16x2(__uint_as_float(o[q4 * 8 + 4]) * inv, __uint_as_float(o[q4 * 8 + 5]) * inv);
+            const uint32_t u = pack_bf16x2(__uint_as_float(o[q4 * 8 + 6]) * inv, __uint_as_float(o[q4 * 8 + 7]) * inv);
+            const int chunk = c * 4 + q4;
+            st_shared_v4(smem_u32(stage + r * 128 + ((chunk ^ (r & 7)) << 4)), x, y, z, u);
+          }
+        }
+        if (h == 1) {  // O_s is read out: the next item's first P V_s may overwrite it
+          tc_fence_before();
+          mbar_arrive(&sm.o_free[s]);
+        }
+        mbar_arrive(&sm.staged[s]);
+        if (!__all_sync(0xffffffffu, mbar_wait(&sm.staged[s], h & 1))) {
+          ok = false;
+          break;
+        }
 #pragma unroll 4
         for (int k = 0; k < 8; ++k) {
-          const int row = warp * 16 + k * 2 + (lane >> 4);
-          if (row < lq_rows) {
-            const uint4 v4 = *reinterpret_cast<const uint4*>(scratch + row * 256 + ((c ^ (row & 15)) << 4));
-            __nv_bfloat16* dst =
-                a.out + (static_cast<int64_t>(it.q0 + it.qt * kRows + row) * a.num_heads + it.h) * kD + c * 8;
+          const int row = wq * 32 + k * 4 + (lane >> 3), c16 = lane & 7;
+          if (row < rows) {
+            const uint4 v4 = ld_shared_v4(smem_u32(stage + row * 128 + ((c16 ^ (row & 7)) << 4)));
+            __nv_bfloat16* dst = a.out +
+                                 (static_cast<int64_t>(it.q0 + it.qt * kRows + row) * a.num_heads + it.h0 + s) * kD +
+                                 h * 64 + c16 * 8;
             *reinterpret_cast<uint4*>(dst) = v4;
           }
         }
+        mbar_arrive(&sm.drained[s]);
       }
-      // The scratch reads are done: the stage may take the Q tile of the
-      // item after next (an async-proxy write).
-      fence_proxy_async_smem();
-      mbar_arrive(&sm.q_empty[qi % kStages]);
+      if (!ok) break;
       ++qi;
-      w = w_next;
-      it = nx;
-      have = have_next;
     }
     if (!ok) flag_error(a, sm, kErrWaitTimeout);
   }
@@ -584,7 +552,8 @@ int launch_prefill(const CUtensorMap& qm, const CUtensorMap& km, const CUtensorM
   int dev = 0, sms = 148;
   if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   a.qtiles = (max_q_len + kRows - 1) / kRows;
-  const int64_t items = static_cast<int64_t>(a.qtiles) * a.num_heads * a.batch;
+  a.paired = (a.qpk % 2 == 0) ? 1 : 0;
+  const int64_t items = static_cast<int64_t>(a.qtiles) * (a.num_heads / (a.paired ? kStreams : 1)) * a.batch;
   if (items > (int64_t(1) << 30))
     return fail(NVK_ERR_UNSUPPORTED, "prefill: %lld work items above the kernel's range", (long long)items);
   const int grid = static_cast<int>(items < sms ? items : sms);

@@ -56,6 +56,22 @@ __device__ __forceinline__ void umma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, ui
       : "memory");
 }
 
+// True in exactly one lane of the converged warp (elect.sync over all 32
+// lanes; the same lane every time). UMMAs and their commits go out this way
+// with the whole warp running the issue loop: the operand descriptors stay
+// warp-uniform values, and an M128 N128 K16 UMMA issues in ~68 cycles, where
+// the same loop run by lane 0 alone inside a divergent branch spends 100-125
+// cycles per UMMA on issue and starves the tensor pipe.
+__device__ __forceinline__ bool elect_one_sync() {
+  uint32_t pred = 0;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "elect.sync _|p, 0xffffffff;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(pred));
+  return pred != 0;
+}
+
 // Arrives once on `bar` when every previously issued tcgen05.mma of this
 // thread has completed.
 __device__ __forceinline__ void umma_commit(uint64_t* bar) {
