@@ -99,7 +99,8 @@ struct PrefillSmem {
   uint64_t full_k[kStages], k_empty[kStages];
   uint64_t full_v[kStages], v_empty[kStages];
   uint64_t s_full[kStreams];   // S_s(j) in TMEM (and, in issue order, P V_s(j-1) done)
-  uint64_t p_full[kStreams];   // P_s(j) written by the stream's 128 softmax threads
+  uint64_t p_lo[kStreams];     // P_s(j) of keys 0-63 written by the stream's 128 softmax threads
+  uint64_t p_hi[kStreams];     // P_s(j) of keys 64-127 written
   uint64_t o_ready[kStreams];  // an item's last P V_s complete (one phase per item)
   uint64_t o_free[kStreams];   // an item's O_s read out (one phase per item)
   uint64_t staged[kStreams];   // a 64-dim half of an item's rows is in stage[s] (two phases per item)
@@ -188,7 +189,8 @@ __global__ void __maxnreg__(168) prefill_kernel(const __grid_constant__ CUtensor
       mbar_init(&sm.q_full[s], 1);
       mbar_init(&sm.q_empty[s], 1);
       mbar_init(&sm.s_full[s], 1);
-      mbar_init(&sm.p_full[s], kStreamThreads);
+      mbar_init(&sm.p_lo[s], kStreamThreads);
+      mbar_init(&sm.p_hi[s], kStreamThreads);
       mbar_init(&sm.o_ready[s], 1);
       mbar_init(&sm.o_free[s], kStreamThreads);
       mbar_init(&sm.staged[s], kStreamThreads);
@@ -327,10 +329,11 @@ __global__ void __maxnreg__(168) prefill_kernel(const __grid_constant__ CUtensor
       }
       commit(&sm.s_full[s]);
     };
-    auto issue_pv = [&](int s, int st, bool first) {  // O_s (+)= P_s V(stage st)
+    // O_s (+)= P_s V(stage st) over the keys of 16-key steps kk0 .. kk0 + 3
+    auto issue_pv = [&](int s, int st, int kk0, bool first) {
       const uint32_t v_addr = smem_u32(sm.v[st]);
 #pragma unroll
-      for (int kk = 0; kk < kKeys / 16; ++kk) {
+      for (int kk = kk0; kk < kk0 + 4; ++kk) {
         const uint64_t vb = smem_desc_sw128(v_addr + kk * 16 * 128, kHalfBytes, 1024);
         if (elect_one_sync())
           umma_f16_ts(tmem + kColO + s * kD, tmem + s * kKeys + kk * 8, vb, idesc_pv, (!first || kk > 0) ? 1u : 0u);
@@ -365,12 +368,20 @@ __global__ void __maxnreg__(168) prefill_kernel(const __grid_constant__ CUtensor
           break;
         }
         for (int s = 0; s < ns; ++s) {
-          if (!wait_all(&sm.p_full[s], g & 1) || (j == 0 && qi > 0 && !wait_all(&sm.o_free[s], (qi - 1) & 1))) {
+          // the P V of the first 64 keys goes out while the softmax still
+          // computes the exponentials of the other 64
+          if (!wait_all(&sm.p_lo[s], g & 1) || (j == 0 && qi > 0 && !wait_all(&sm.o_free[s], (qi - 1) & 1))) {
             ok = false;
             break;
           }
           tc_fence_after();
-          issue_pv(s, st, j == 0);
+          issue_pv(s, st, 0, j == 0);
+          if (!wait_all(&sm.p_hi[s], g & 1)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          issue_pv(s, st, 4, false);
           if (more) {
             issue_s(s, st1);
             if (j + 2 == it.n_kv) commit(&sm.q_empty[s]);  // the item's last S_s
@@ -444,8 +455,9 @@ __global__ void __maxnreg__(168) prefill_kernel(const __grid_constant__ CUtensor
         float sum[4] = {0.f, 0.f, 0.f, 0.f};  // independent add chains
         // P over the first 64 columns of S_s (column k holds keys 2k and 2k+1
         // as a bf16 pair): word e of chunk c overwrites score e, already read.
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
+        // Keys 0-63 are signalled first, so that their P V starts while the
+        // exponentials of keys 64-127 are computed.
+        auto exps = [&](int c) {
 #pragma unroll
           for (int e = 0; e < 16; ++e) {
             const float p0 = fast_exp2(fmaf(__uint_as_float(sr[c][2 * e]), sc, neg_mu));
@@ -455,10 +467,11 @@ __global__ void __maxnreg__(168) prefill_kernel(const __grid_constant__ CUtensor
             sr[c][e] = pack_bf16x2(p0, p1);
           }
           tmem_st16_first(tmem_s + c * 16, sr[c]);
-        }
-        l += (sum[0] + sum[1]) + (sum[2] + sum[3]);
-        // O_s rescales (rarely) before this tile's P is signalled: S_s(j)
-        // landed, so P V_s(j-1) is complete.
+        };
+        exps(0);
+        exps(1);
+        // O_s rescales (rarely) before any P V of this tile: S_s(j) landed,
+        // so P V_s(j-1) is complete.
         if (j > 0 && __any_sync(0xffffffffu, resc)) {
 #pragma unroll 1
           for (int c = 0; c < 4; ++c) {
@@ -472,7 +485,13 @@ __global__ void __maxnreg__(168) prefill_kernel(const __grid_constant__ CUtensor
         }
         tmem_st_wait();
         tc_fence_before();
-        mbar_arrive(&sm.p_full[s]);
+        mbar_arrive(&sm.p_lo[s]);
+        exps(2);
+        exps(3);
+        l += (sum[0] + sum[1]) + (sum[2] + sum[3]);
+        tmem_st_wait();
+        tc_fence_before();
+        mbar_arrive(&sm.p_hi[s]);
       }
       if (!ok) break;
       // The item's last P V_s complete: normalise the O_s rows and store them
