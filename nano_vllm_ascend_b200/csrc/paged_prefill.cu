@@ -103,8 +103,6 @@ struct PrefillSmem {
   uint64_t p_hi[kStreams];     // P_s(j) of keys 64-127 written
   uint64_t o_ready[kStreams];  // an item's last P V_s complete (one phase per item)
   uint64_t o_free[kStreams];   // an item's O_s read out (one phase per item)
-  uint64_t staged[kStreams];   // a 64-dim half of an item's rows is in stage[s] (two phases per item)
-  uint64_t drained[kStreams];  // stage[s] copied out to global memory (two phases per item)
   uint64_t fin;
   uint32_t tmem_base;
   volatile int abort;
@@ -193,8 +191,6 @@ __global__ void __maxnreg__(168) prefill_kernel(const __grid_constant__ CUtensor
       mbar_init(&sm.p_hi[s], kStreamThreads);
       mbar_init(&sm.o_ready[s], 1);
       mbar_init(&sm.o_free[s], kStreamThreads);
-      mbar_init(&sm.staged[s], kStreamThreads);
-      mbar_init(&sm.drained[s], kStreamThreads);
     }
     for (int i = 0; i < kItemRing; ++i) mbar_init(&sm.item_full[i], 1);
     mbar_init(&sm.fin, 1);
@@ -497,20 +493,16 @@ __global__ void __maxnreg__(168) prefill_kernel(const __grid_constant__ CUtensor
       // The item's last P V_s complete: normalise the O_s rows and store them
       // through stage[s], one 64-dim half at a time: thread r writes its row
       // half there (16-byte chunk c of row r at chunk c ^ (r % 8): conflict
-      // free), then each warp stores four whole 128-byte row halves per
-      // instruction, so the global writes are coalesced.
+      // free), then its warp stores the 32 row halves its lanes wrote, four
+      // whole 128-byte row halves per instruction, so the global writes are
+      // coalesced and no warp waits for another.
       if (!__all_sync(0xffffffffu, mbar_wait(&sm.o_ready[s], qi & 1))) { ok = false; break; }
       tc_fence_after();
       const float inv = l > 0.f ? 1.f / l : 0.f;
       const int rows = min(kRows, it.lq - it.qt * kRows);
-      const int wq = warp & 3;
+      const int row0 = (warp & 3) * 32;
 #pragma unroll 1
       for (int h = 0; h < 2; ++h) {
-        // the previous half's copy-out has read the buffer
-        if ((qi > 0 || h > 0) && !__all_sync(0xffffffffu, mbar_wait(&sm.drained[s], (h + 1) & 1))) {
-          ok = false;
-          break;
-        }
 #pragma unroll 1
         for (int c = 0; c < 2; ++c) {
           uint32_t o[32];
@@ -530,14 +522,10 @@ __global__ void __maxnreg__(168) prefill_kernel(const __grid_constant__ CUtensor
           tc_fence_before();
           mbar_arrive(&sm.o_free[s]);
         }
-        mbar_arrive(&sm.staged[s]);
-        if (!__all_sync(0xffffffffu, mbar_wait(&sm.staged[s], h & 1))) {
-          ok = false;
-          break;
-        }
+        __syncwarp();  // this warp's 32 row halves are in stage[s]
 #pragma unroll 4
         for (int k = 0; k < 8; ++k) {
-          const int row = wq * 32 + k * 4 + (lane >> 3), c16 = lane & 7;
+          const int row = row0 + k * 4 + (lane >> 3), c16 = lane & 7;
           if (row < rows) {
             const uint4 v4 = ld_shared_v4(smem_u32(stage + row * 128 + ((c16 ^ (row & 7)) << 4)));
             __nv_bfloat16* dst = a.out +
@@ -546,7 +534,7 @@ __global__ void __maxnreg__(168) prefill_kernel(const __grid_constant__ CUtensor
             *reinterpret_cast<uint4*>(dst) = v4;
           }
         }
-        mbar_arrive(&sm.drained[s]);
+        __syncwarp();  // read out before the next half overwrites the rows
       }
       if (!ok) break;
       ++qi;
