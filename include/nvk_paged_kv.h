@@ -108,8 +108,12 @@ NVK_API int nvk_kv_append(const void* key, const void* value, int64_t key_token_
  * `num_kv_heads` KV heads and `num_heads` query heads on `num_ctas` CTAs
  * (0 = one per SM of the current device): an error word, one arrival ticket
  * per (sequence, KV head) and two partial-result slots per CTA. Zero it once
- * before first use; every call leaves the tickets at zero again. Calls that
- * share one workspace must be ordered on one stream.
+ * before first use; every call leaves the tickets at zero again for a next
+ * call of the same batch, num_heads, num_kv_heads and num_ctas. The tickets'
+ * place depends on those four (a call of another shape would find partial
+ * results of the previous call there): zero the workspace again before a
+ * call whose shape differs from the previous call's. Calls that share one
+ * workspace must be ordered on one stream.
  */
 NVK_API int nvk_paged_decode_workspace_size(int batch, int num_heads, int num_kv_heads, int head_dim, int num_ctas,
                                             size_t* bytes);

@@ -31,6 +31,7 @@ from .paged_kv_cache import take_deferred
 
 _NUM_SMS: dict[int, int] = {}
 _WORKSPACES: dict[int, torch.Tensor] = {}
+_SHAPES: dict[int, tuple] = {}  # per device: the shape of the last call on its workspace
 
 
 def num_sms(device: torch.device) -> int:
@@ -40,17 +41,23 @@ def num_sms(device: torch.device) -> int:
     return _NUM_SMS[idx]
 
 
-def shared_workspace(device: torch.device, nbytes: int) -> torch.Tensor:
+def shared_workspace(device: torch.device, nbytes: int, shape: tuple = ()) -> torch.Tensor:
     """Eager-mode split-K workspace, one per device, grown (zero-filled) on demand.
 
     Calls ordered on one stream may share it: each decode call returns its
-    arrival counters to zero.
+    arrival tickets to zero. Where the tickets lie depends on the call's
+    ``shape`` (batch, heads, KV heads, CTAs), and a call of another shape
+    would find the previous call's partial results there, so the workspace
+    is zeroed again, in stream order, whenever the shape changes.
     """
     idx = device.index if device.index is not None else torch.cuda.current_device()
     ws = _WORKSPACES.get(idx)
     if ws is None or ws.numel() < nbytes:
         ws = torch.zeros(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
         _WORKSPACES[idx] = ws
+    elif _SHAPES.get(idx) != shape:
+        ws[:nbytes].zero_()
+    _SHAPES[idx] = shape
     return ws
 
 
@@ -94,7 +101,8 @@ class PagedAttention(nn.Module):
             if workspace is not None:
                 word = None  # the graph runner reads its slot's word after each replay
             else:
-                workspace = shared_workspace(device, self.workspace_bytes(total_tokens))
+                workspace = shared_workspace(device, self.workspace_bytes(total_tokens),
+                                             (total_tokens, self.num_heads, self.num_key_value_heads, self.num_ctas))
                 word = errors.watch("paged decode", workspace)
             ctx = context_lens if context_lens.is_cuda else context_lens.to(device=device, dtype=torch.int32)
             tables = block_tables if block_tables.is_cuda else block_tables.to(device)

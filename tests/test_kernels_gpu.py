@@ -187,6 +187,25 @@ def test_decode_workspace_reuse_across_calls(cuda_device):
     assert_close(got2, want2, "second")
 
 
+def test_eager_shared_workspace_survives_a_batch_size_change(cuda_device):
+    """PagedAttention's per-device workspace serving a batch of 2, then 3, then
+    2 again: each call's tickets lie where the call before it left partial
+    results, which the workspace helper clears when the shape changes."""
+    from nano_vllm_ascend_b200 import PagedAttention, check_errors
+
+    attn = PagedAttention(16, 8, 128)
+    for seed, ctx in ((31, [300, 200]), (32, [700, 130, 2000]), (33, [50, 4000])):
+        nb = sum((n + 127) // 128 for n in ctx) + 3
+        kc, vc = random_pool(nb, 128, 8, 128, cuda_device, seed)
+        tables = seeded_tables(ctx, 128, nb, seed).to(cuda_device)
+        g = torch.Generator(device=cuda_device).manual_seed(seed + 1)
+        q = torch.randn(len(ctx), 16, 128, generator=g, device=cuda_device).to(torch.bfloat16)
+        out = attn(q, kc, vc, tables, torch.tensor(ctx, dtype=torch.int32, device=cuda_device))
+        check_errors(cuda_device)
+        want = orc.paged_decode(bits(q), bits(kc), bits(vc), tables.cpu().numpy(), np.array(ctx), 128 ** -0.5)
+        assert_close(out.float().cpu().numpy(), want, f"eager decode of batch {len(ctx)}")
+
+
 def test_decode_wide_padded_table(cuda_device):
     # graph-style static table: much wider than any context
     got, want, _ = run_decode(cuda_device, [130, 9], width=64, seed=4)

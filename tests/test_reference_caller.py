@@ -142,7 +142,7 @@ def reference(monkeypatch):
     monkeypatch.setattr(nvk.device_errors, "state", lambda *_: NoErrors())
     monkeypatch.setattr(nvk.PagedAttention, "workspace_bytes", lambda self, b: 64)
     monkeypatch.setattr(importlib.import_module("nano_vllm_ascend_b200.paged_attention"), "shared_workspace",
-                        lambda device, nbytes: torch.zeros(nbytes, dtype=torch.uint8))
+                        lambda device, nbytes, shape=(): torch.zeros(nbytes, dtype=torch.uint8))
     grad = torch.is_grad_enabled()
     torch.set_grad_enabled(False)  # the reference's runner works under torch.inference_mode()
     yield SimpleNamespace(qwen3=qwen3, rope=rope_mod, kernels=kernels)
