@@ -275,13 +275,16 @@ def free_device_memory() -> None:
 # ----------------------------------------------------------------- setup ----
 def rank_contexts(wl: Workload, world: int, rank: int) -> list[int]:
     """Context lengths (before this step's token) of this rank's sequences."""
-    from nano_vllm_ascend_b200.sharding import sequence_shard
+    from nano_vllm_ascend_b200.sharding import token_balanced_shard
 
     if wl.scaling == "strong":
+        # one batch split across the ranks by context length (equal KV bytes per rank)
         g = torch.Generator().manual_seed(0)
         ctx = torch.randint(wl.ctx_lo, wl.ctx_hi + 1, (wl.batch,), generator=g).tolist()
-        return [ctx[i] for i in sequence_shard(wl.batch, world, rank)]
-    g = torch.Generator().manual_seed(1000 + rank)
+        return [ctx[i] for i in token_balanced_shard(ctx, world, rank)]
+    # weak scaling: every rank decodes the same per-GPU workload (its own K/V
+    # values and block tables, the same context lengths)
+    g = torch.Generator().manual_seed(1000)
     return torch.randint(wl.ctx_lo, wl.ctx_hi + 1, (wl.batch,), generator=g).tolist()
 
 

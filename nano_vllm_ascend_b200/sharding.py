@@ -26,6 +26,25 @@ def sequence_shard(num_seqs: int, world_size: int, rank: int) -> range:
     return range(start, start + base + (1 if rank < extra else 0))
 
 
+def token_balanced_shard(lengths: list[int], world_size: int, rank: int) -> list[int]:
+    """Indices (ascending) of the sequences ``rank`` decodes when the batch is
+    split by context length instead of by position: longest first, each to
+    the rank holding the fewest tokens so far (lowest rank on ties). A decode
+    step reads every token's K and V once, so equal token totals mean equal
+    step times; the ranks' totals differ by at most one sequence's length.
+    Deterministic: every rank computes the same assignment."""
+    if world_size <= 0 or not 0 <= rank < world_size:
+        raise ValueError(f"bad rank {rank} for world size {world_size}")
+    totals = [0] * world_size
+    mine = []
+    for i in sorted(range(len(lengths)), key=lambda j: (-lengths[j], j)):
+        r = min(range(world_size), key=lambda k: (totals[k], k))
+        totals[r] += lengths[i]
+        if r == rank:
+            mine.append(i)
+    return sorted(mine)
+
+
 def kv_head_shard(num_heads: int, num_kv_heads: int, world_size: int, rank: int) -> tuple[range, range]:
     """(kv-head range, query-head range) owned by ``rank``."""
     if num_kv_heads % world_size != 0:

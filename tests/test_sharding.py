@@ -17,8 +17,26 @@ import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp
 
-from nano_vllm_ascend_b200.sharding import gather_head_shards, kv_head_shard, sequence_shard
+from nano_vllm_ascend_b200.sharding import gather_head_shards, kv_head_shard, sequence_shard, token_balanced_shard
 from oracle import paged_kv_oracle as orc
+
+
+def test_token_balanced_shard_partitions_and_balances():
+    g = torch.Generator().manual_seed(0)
+    for n, w in ((256, 8), (256, 2), (7, 3), (3, 4), (0, 2)):
+        lens = torch.randint(2048, 6145, (n,), generator=g).tolist()
+        parts = [token_balanced_shard(lens, w, r) for r in range(w)]
+        assert sorted(i for p in parts for i in p) == list(range(n))
+        assert all(p == sorted(p) for p in parts)
+        totals = [sum(lens[i] for i in p) for p in parts]
+        if n:
+            assert max(totals) - min(totals) <= max(lens)
+        assert parts == [token_balanced_shard(lens, w, r) for r in range(w)]  # deterministic
+    lens = torch.randint(2048, 6145, (256,), generator=torch.Generator().manual_seed(0)).tolist()
+    totals = [sum(lens[i] for i in token_balanced_shard(lens, 8, r)) for r in range(8)]
+    assert max(totals) / min(totals) < 1.01  # the contiguous split of the same batch is ~10 % apart
+    with pytest.raises(ValueError):
+        token_balanced_shard([1, 2], 2, 2)
 
 
 def test_sequence_shard_partitions_exactly():
