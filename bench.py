@@ -615,7 +615,8 @@ def measure_decode(args, wl: Workload, world: int, rank: int, local: int, with_c
     h2d = sum(t.numel() * t.element_size() for t in (h_q, h_k, h_v, h_tables, h_slots, h_ctx, h_pos, h_ids))
     d2h = h_out.numel() * h_out.element_size()
     per_rank = all_ranks({"rank": rank, "ms_per_step": t_step * 1e3, "sm_mhz": clk.get("sm_mhz"),
-                          "us_per_decode_launch": t_dec * 1e6, "reasons": clk.get("reasons")}, world)
+                          "us_per_decode_launch": t_dec * 1e6, "reasons": clk.get("reasons"),
+                          **({"gather": gather_split} if gather_split else {})}, world)
     t_step_max = max_over_ranks(t_step, world)
     t_e2e_max = max_over_ranks(t_e2e, world)
     t_dec_max = max_over_ranks(t_dec, world)
@@ -951,12 +952,18 @@ def measure_c5(args, world: int, rank: int, local: int, gather: str) -> dict:
         barrier_sync(world)
         ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         n_launch = layers * (1 if args.quick else 4)
+        timing0 = ws[128:152].view(torch.int64).cpu() if in_kernel else None
         ev0.record(stream)
         for i in range(n_launch):
             attend(i % layers, gather=False)
         ev1.record(stream)
         ev1.synchronize()
         t_dec = ev0.elapsed_time(ev1) / 1e3 / n_launch
+        gather_split = None
+        if in_kernel:  # the kernel's own clock: local work, then the wait for every rank's epoch
+            d = ws[128:152].view(torch.int64).cpu() - timing0
+            calls = max(int(d[2]), 1)
+            gather_split = {"local_us": float(d[0]) / calls / 1e3, "epoch_wait_us": float(d[1]) / calls / 1e3}
         if ops.decode_error_word(ws) != 0:
             raise RuntimeError(f"decode error word {ops.decode_error_word(ws)}")
         for _ in range(args.warmup):
@@ -1020,7 +1027,8 @@ def measure_c5(args, world: int, rank: int, local: int, gather: str) -> dict:
 
     bytes_layer = kv_bytes_per_layer([n + 1 for n in ctx], kvh)
     per_rank = all_ranks({"rank": rank, "ms_per_step": t_step * 1e3, "sm_mhz": clk.get("sm_mhz"),
-                          "us_per_decode_launch": t_dec * 1e6, "reasons": clk.get("reasons")}, world)
+                          "us_per_decode_launch": t_dec * 1e6, "reasons": clk.get("reasons"),
+                          **({"gather": gather_split} if gather_split else {})}, world)
     t_step_max = max_over_ranks(t_step, world)
     t_e2e_max = max_over_ranks(t_e2e, world)
     t_dec_max = max_over_ranks(t_dec, world)

@@ -111,6 +111,11 @@ struct DecodeArgs {
   uint32_t* peer_sig[NVK_MAX_PEERS];
   uint32_t* my_sig;
   int* done;  // CTAs finished this call (gather mode), back at zero after it
+  // Gather mode timing, accumulated over calls in the workspace header:
+  // [0] ns from CTA 0's release (griddepcontrol.wait) to the last CTA's
+  // arrival, [1] ns the last CTA then waited for every rank's epoch,
+  // [2] calls, [3] this call's release time (written by CTA 0).
+  unsigned long long* timing;
   // Fused append (new_slots != nullptr): this step's token of sequence b,
   // rows k_new/v_new + b * stride (16-byte words, heads and dims packed), is
   // written to pool slot new_slots[b] before any of its tiles is read.
@@ -363,6 +368,10 @@ __device__ __forceinline__ void gather_signal(const DecodeArgs& a, int ctas) {
       }
     }
   }
+  // (CTA 0's release time is ordered before this by the acq_rel ticket)
+  a.timing[0] += t0 - a.timing[3];
+  a.timing[1] += globaltimer_ns() - t0;
+  a.timing[2] += 1;
 }
 
 __device__ __forceinline__ void flag_error(const DecodeArgs& a, Smem& sm, int code) {
@@ -614,6 +623,7 @@ __global__ void __launch_bounds__(kThreads, 1) paged_decode_kernel(const __grid_
   __syncthreads();
   tc_fence_after();
   if (warp != kSchedWarp) pdl_wait();  // the scheduler waits after staging its first chunk
+  if (a.world > 0 && c == 0 && tid == 0) a.timing[3] = globaltimer_ns();
 
   const int total = sm.total_tiles;
   const Sched sc = make_sched(total, ctas);
@@ -1159,7 +1169,8 @@ struct WsLayout {
   size_t cnt_off, ml_off, o_off, total;
 };
 
-// [0, 256): error word | tickets [batch * KVH], one per 128-byte line | (m, l) [C][2][QPK] | o [C][2][QPK][128]
+// [0, 256): error word (byte 0), gather-mode CTA counter (64) and timing sums (128..159) |
+// tickets [batch * KVH], one per 128-byte line | (m, l) [C][2][QPK] | o [C][2][QPK][128]
 WsLayout ws_layout(int batch, int num_heads, int num_kv_heads, int ctas) {
   auto up = [](size_t x) { return (x + 255) & ~size_t(255); };
   const int qpk = num_heads / num_kv_heads;
@@ -1312,6 +1323,7 @@ int decode_impl(void* out, const void* query, const void* key_cache, const void*
     }
     a.my_sig = gt ? static_cast<uint32_t*>(gt->signal_peers[gt->rank]) : nullptr;
     a.done = reinterpret_cast<int*>(ws + 64);
+    a.timing = reinterpret_cast<unsigned long long*>(ws + 128);
     a.new_slots = ap ? ap->slots + b0 : nullptr;
     a.k_new = ap ? static_cast<const uint4*>(ap->key) + b0 * (ap->key_stride / 8) : nullptr;
     a.v_new = ap ? static_cast<const uint4*>(ap->value) + b0 * (ap->value_stride / 8) : nullptr;
