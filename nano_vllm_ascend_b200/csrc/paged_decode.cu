@@ -326,7 +326,9 @@ struct SegIter {
   }
 };
 
-// Stores output element d of (sequence b, local query head qh).
+// Stores output element d of (sequence b, local query head qh). In gather
+// mode into this rank's own gathered output; push_rows then copies whole
+// rows to the other ranks.
 __device__ __forceinline__ void store_out(const DecodeArgs& a, int b, int qh, int d, float v) {
   const int64_t off = (static_cast<int64_t>(b) * a.out_heads + a.head_offset + qh) * kD + d;
   const __nv_bfloat16 x = __float2bfloat16_rn(v);
@@ -334,9 +336,22 @@ __device__ __forceinline__ void store_out(const DecodeArgs& a, int b, int qh, in
     a.out[off] = x;
     return;
   }
-#pragma unroll
-  for (int r = 0; r < NVK_MAX_PEERS; ++r)
-    if (r < a.world) a.peer_out[r][off] = x;  // a peer's buffer: a store over NVLink
+  a.peer_out[a.rank][off] = x;
+}
+
+// Gather mode: the rows (sequence b, local query heads h0 .. h0 + nh - 1),
+// which the 128 epilogue threads have just stored into this rank's output
+// (ordered by the named barrier the caller took), copied to every other
+// rank's output over NVLink, 16 bytes a store (the rows are contiguous).
+__device__ __forceinline__ void push_rows(const DecodeArgs& a, int b, int h0, int nh, int e) {
+  const int64_t off = (static_cast<int64_t>(b) * a.out_heads + a.head_offset + h0) * kD;
+  const int chunks = nh * (kD * 2 / 16);
+  const uint4* src = reinterpret_cast<const uint4*>(a.peer_out[a.rank] + off);
+  for (int i = e; i < (a.world - 1) * chunks; i += kEpilogueThreads) {
+    const int p = i / chunks, k = i - p * chunks;
+    const int r = p < a.rank ? p : p + 1;  // every rank but this one
+    reinterpret_cast<uint4*>(a.peer_out[r] + off)[k] = src[k];
+  }
 }
 
 constexpr int kEpochSlot = NVK_MAX_PEERS;  // signal word holding this rank's call count
@@ -1108,6 +1123,10 @@ __global__ void __launch_bounds__(kThreads, 1) paged_decode_kernel(const __grid_
           }
         }
       }
+      if (a.world > 1 && (!part || pre_last)) {  // this CTA completed the pair: its rows go to the peers
+        named_barrier_sync(2, kEpilogueThreads);
+        push_rows(a, s.b, s.g * QPK, QPK, e);
+      }
       if (part && !pre_last) {
         // Publish: one acq_rel ticket releases the piece (every epilogue
         // thread's stores, ordered by the barrier) and acquires the others'.
@@ -1126,7 +1145,13 @@ __global__ void __launch_bounds__(kThreads, 1) paged_decode_kernel(const __grid_
           sm.last[pi] = last;
         }
         named_barrier_sync(2, kEpilogueThreads);
-        if (sm.last[pi]) merge_published<QPK>(sm, a, sc, e, d, s.b, s.g, s.pair_t0, c_first, pieces, ticket);
+        if (sm.last[pi]) {
+          merge_published<QPK>(sm, a, sc, e, d, s.b, s.g, s.pair_t0, c_first, pieces, ticket);
+          if (a.world > 1) {
+            named_barrier_sync(2, kEpilogueThreads);
+            push_rows(a, s.b, s.g * QPK, QPK, e);
+          }
+        }
       }
       if (part) ++npart;
     }
@@ -1137,6 +1162,10 @@ __global__ void __launch_bounds__(kThreads, 1) paged_decode_kernel(const __grid_
     for (int b = c; b < a.batch; b += ctas) {
       if (sm.tiles_before[b + 1] == sm.tiles_before[b]) {
         for (int h = 0; h < a.num_heads; ++h) store_out(a, b, h, e, 0.f);
+        if (a.world > 1) {
+          named_barrier_sync(2, kEpilogueThreads);
+          push_rows(a, b, 0, a.num_heads, e);
+        }
         if (a.new_slots != nullptr) {
           const int64_t slot = a.new_slots[b];
           const int words = kvh * (kD * 2 / 16);
