@@ -615,8 +615,7 @@ def measure_decode(args, wl: Workload, world: int, rank: int, local: int, with_c
     h2d = sum(t.numel() * t.element_size() for t in (h_q, h_k, h_v, h_tables, h_slots, h_ctx, h_pos, h_ids))
     d2h = h_out.numel() * h_out.element_size()
     per_rank = all_ranks({"rank": rank, "ms_per_step": t_step * 1e3, "sm_mhz": clk.get("sm_mhz"),
-                          "us_per_decode_launch": t_dec * 1e6, "reasons": clk.get("reasons"),
-                          **({"gather": gather_split} if gather_split else {})}, world)
+                          "us_per_decode_launch": t_dec * 1e6, "reasons": clk.get("reasons")}, world)
     t_step_max = max_over_ranks(t_step, world)
     t_e2e_max = max_over_ranks(t_e2e, world)
     t_dec_max = max_over_ranks(t_dec, world)
