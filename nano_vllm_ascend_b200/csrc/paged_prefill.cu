@@ -16,27 +16,32 @@
 // puts the heaviest query tiles first.
 // Tensor memory (512 columns): S/P of stream s at s * 128, its O accumulator
 // at 256 + s * 128.
-//   warp 8 (producer): per item the TMA loads of the streams' Q tiles (each
-//     as soon as the previous item's last S of that stream has read its
-//     buffer), then per key tile the K and V tiles (two 64-dim halves each,
+//   warp 8 (producer): walks the item list and publishes each item's
+//     descriptor through a 4-slot shared-memory ring (the other roles never
+//     read the item metadata from global memory); per item the TMA loads of
+//     the streams' Q tiles (once the previous item's last S has read their
+//     buffers), then per key tile the K and V tiles (two 64-dim halves each,
 //     128-byte swizzle = the canonical UMMA operand layout) into 2-stage
 //     rings; block ids 32 at a time (one parallel load per warp).
 //   warp 9 (MMA; the whole warp runs the loop, an elected lane issues):
-//     per tile j and stream s, once P_s(j) is written, O_s += P_s(j) V(j)
-//     (P read from TMEM where the softmax wrote it over S_s, V MN-major from
-//     smem) and right behind it S_s(j+1) = Q_s K(j+1)^T into the same
-//     columns. tcgen05.mma executes in issue order, so S_s(j+1) overwrites
-//     P_s(j) only after the P V has read it, and the tensor pipe has the
-//     other stream's work queued while one stream's softmax runs. An item's
-//     first S tiles are issued behind the previous item's last P V.
+//     per tile j and stream s, once the first 64 keys of P_s(j) are written,
+//     O_s += P V over them, then over the other 64 (P read from TMEM where
+//     the softmax wrote it over S_s, V MN-major from smem), and right behind
+//     it S_s(j+1) = Q_s K(j+1)^T into the same columns. tcgen05.mma executes
+//     in issue order, so S_s(j+1) overwrites P_s(j) only after the P V has
+//     read it, and the tensor pipe has the other stream's work queued while
+//     one stream's softmax runs. An item's first S tiles are issued behind
+//     the previous item's last P V.
 //   warps 0-3 / 4-7 (softmax of stream 0 / 1): thread r owns query row r =
 //     TMEM lane r. Per tile the 128 scores of its row in one round of
 //     tcgen05.ld, the mask, base-2 online softmax, P written as bf16 pairs
-//     over the first 64 columns of S_s (tcgen05.st), lazy rescaling of O_s
-//     (only when the running max grew by more than 2^8; S_s(j) having landed
-//     means P V_s(j-1), issued before it, is complete). Per item the
-//     normalised O_s row is stored once the item's last P V_s completed,
-//     which releases O_s to the next item.
+//     over the first 64 columns of S_s (tcgen05.st) in two halves, each
+//     signalled once stored; lazy rescaling of O_s (only when the running
+//     max grew by more than 2^8; S_s(j) having landed means P V_s(j-1),
+//     issued before it, is complete). Per item, once its last P V_s has
+//     completed, the normalised O_s rows go out through a staging buffer:
+//     each warp stores the 32 rows its own lanes staged as whole 128-byte
+//     row halves (coalesced), and O_s is released to the next item.
 // Ten warps put three on one SM sub-partition, whose register file holds
 // 3 x 32 x 168 registers: the kernel is held to 168 registers a thread.
 // Every mbarrier wait is bounded; on a timeout the CTA records the error,
