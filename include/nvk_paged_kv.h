@@ -82,7 +82,7 @@ NVK_API const char* nvk_last_error(void);
 /* ABI version, bumped on any signature change (2: persistent decode, num_ctas;
    3: KV-head-sharded decode with in-kernel gather, peer buffers, fused append,
    device-side decode metadata; 4: per-row lengths and table sizes for
-   nvk_decode_metadata). */
+   nvk_decode_metadata; 5: nvk_paged_decode_noalloc_error). */
 NVK_API int nvk_abi_version(void);
 
 /*
