@@ -204,14 +204,10 @@ __device__ __forceinline__ void fence_proxy_async_global() {
   asm volatile("fence.proxy.async.global;" ::: "memory");
 }
 
-// System-scope release store / acquire load of a 32-bit flag (may live in
-// another GPU's memory mapped into this process).
-__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
-  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-// A relaxed system-scope store: behind a system-scope fence (fence, then
-// relaxed stores) it publishes like a release store, without the fence each
-// release store would carry by itself.
+// System-scope flags (32-bit words that may live in another GPU's memory
+// mapped into this process). A system-scope fence followed by relaxed stores
+// publishes like release stores, without the fence each release store would
+// carry by itself; a flag is read with an acquire load.
 __device__ __forceinline__ void st_relaxed_sys(uint32_t* p, uint32_t v) {
   asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
